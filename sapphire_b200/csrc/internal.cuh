@@ -1,0 +1,168 @@
+// internal.cuh - context, device-weight and launcher declarations shared by
+// the .cu sources of libsapphire_cuda.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+#include <thread>
+#include <condition_variable>
+#include <atomic>
+
+#include "common.h"
+
+// Rows per tile of the GEMV device layout: one warp lane owns one row.
+constexpr int kTileRows = 32;
+
+// Device copy of one weight tensor, re-laid out for the GEMV kernels.
+//
+// Tile layout ("lane = row"): rows are grouped in tiles of 32; inside a tile
+// the packed row data is cut into 16-byte chunks and stored chunk-major,
+//     codes[((tile * kchunks) + chunk) * 32 + lane]   (uint4, lane = row % 32)
+// so one warp-wide 16-byte load reads chunk `chunk` of 32 consecutive rows as
+// one contiguous 512-byte segment.  Scales are stored the same way,
+//     scales[((tile * nscale) + s) * 32 + lane]        (fp32)
+// Chunk contents per dtype (weights in column order):
+//     Q8_0 : 16 int8 codes, two chunks per block, nscale = nb
+//     Q4_0 : the block's 16 code bytes (32 weights, interleaved nibbles), nscale = nb
+//     TQ2_0: two 8-byte trit blocks (64 weights), nscale = 1 (row scale)
+//     F32  : 4 floats;  BF16: 8 bf16 values; nscale = 0
+// Padding rows (past the tensor's last row) hold zero codes and zero scales.
+struct DevWeight {
+    uint64_t uid = 0;
+    const void *src = nullptr;     // tensor data pointer at upload time
+    tensor_dtype_t dtype = DTYPE_F32;
+    int rows = 0, cols = 0;        // logical shape of the full tensor
+    int row0 = 0, nrows = 0;       // rows held by this context (row shard)
+    int nb = 0;                    // 32-wide blocks per row (quantized dtypes)
+    int ntiles = 0;                // ceil(nrows / 32)
+    int kchunks = 0;               // 16-byte chunks per row
+    int nscale = 0;                // scales per row in the tile layout
+    uint4 *codes = nullptr;
+    float *scales = nullptr;
+    size_t bytes = 0;              // device bytes held
+};
+
+// Weights covered by one 16-byte chunk of the tile layout.
+inline int chunk_weights(tensor_dtype_t dt) {
+    switch (dt) {
+        case DTYPE_Q8_0: return 16;
+        case DTYPE_Q4_0: return 32;
+        case DTYPE_TQ2_0: return 64;
+        case DTYPE_F32: return 4;
+        case DTYPE_BF16: return 8;
+        default: return 0;
+    }
+}
+
+// Simple host worker pool for kernel_parallel_for (host callbacks only).
+struct HostPool {
+    std::vector<std::thread> threads;
+    std::mutex m;
+    std::condition_variable cv_work, cv_done;
+    uint64_t task_seq = 0;
+    int busy = 0;
+    bool stop = false;
+    parallel_for_fn_t fn = nullptr;
+    void *arg = nullptr;
+    int n = 0;
+    std::atomic<int> next{0};
+};
+
+struct sapphire_context {
+    int num_threads = 0;
+    int chunk_size = 16;
+    bool initialized = false;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    std::recursive_mutex exec_mutex;
+
+    std::unordered_map<uint64_t, DevWeight> weights;
+
+    // Device scratch: activations in, results out, gather buffer.
+    float *d_x = nullptr;  size_t d_x_cap = 0;
+    float *d_y = nullptr;  size_t d_y_cap = 0;
+    float *d_g = nullptr;  size_t d_g_cap = 0;
+    float *d_t = nullptr;  size_t d_t_cap = 0;
+
+    HostPool *pool = nullptr;
+
+    // Row sharding (NCCL); world == 1 means unsharded.
+    int rank = 0, world = 1;
+    void *nccl_comm = nullptr;   // ncclComm_t
+
+    std::string last_error;
+};
+
+// ------------------------------------------------------------------ helpers
+// Record an error on the context (if any) and log it.
+void ctx_fail(kernel_context_t *ctx, const char *where, const char *fmt, ...)
+    __attribute__((format(printf, 3, 4)));
+
+#define CUDA_TRY(ctx, call)                                                       \
+    do {                                                                          \
+        cudaError_t _e = (call);                                                  \
+        if (_e != cudaSuccess) {                                                  \
+            ctx_fail((ctx), __func__, "%s failed: %s", #call, cudaGetErrorString(_e)); \
+            return -1;                                                            \
+        }                                                                         \
+    } while (0)
+
+// True if p is device (or managed) memory; *dev receives its ordinal.
+bool ptr_is_device(const void *p, int *dev);
+
+// Process-wide context used for NULL-context dense GEMV and the row ABI.
+kernel_context_t *default_context();
+
+// Grow a device scratch buffer (on ctx's device) to at least `bytes`.
+int ensure_scratch(kernel_context_t *ctx, float **buf, size_t *cap, size_t bytes);
+
+// Device copy of A for ctx (uploads on first use).  nullptr on error.
+const DevWeight *ctx_weight(kernel_context_t *ctx, const tensor_t *A);
+
+// Logical (rows, cols) of a 2-D tensor; false if not a usable 2-D tensor.
+bool weight_shape(const tensor_t *A, int *rows, int *cols);
+
+// --------------------------------------------------------------- launchers
+// y[b*y_stride + r] = sum_k W[r,k] * x[b*x_stride + k] for r < w.nrows,
+// b < batch.  x, y are device pointers.  Enqueued on `stream`.
+int launch_gemv(kernel_context_t *ctx, const DevWeight &w, const float *x, int x_stride,
+                float *y, int y_stride, int batch, cudaStream_t stream);
+
+// Re-lay out `nrows` packed host-format rows (device pointer `src`, the
+// reference block layout) into tiles starting at tile `tile0` of w.
+int launch_repack(kernel_context_t *ctx, const DevWeight &w, const void *src, int nrows,
+                  int tile0, cudaStream_t stream);
+
+// Quantizers / unpack on device buffers.
+int launch_quantize(kernel_context_t *ctx, tensor_dtype_t dt, void *dst, const float *src,
+                    int rows, int cols, cudaStream_t stream);
+int launch_pack_tq2(kernel_context_t *ctx, void *dst, const int8_t *trits, const float *scales,
+                    int rows, int cols, int *d_err, cudaStream_t stream);
+int launch_dequantize(kernel_context_t *ctx, tensor_dtype_t dt, float *dst, const void *src,
+                      int rows, int cols, cudaStream_t stream);
+// One packed row (reference layout, device pointer) dotted with x -> out[0].
+int launch_row_dot(kernel_context_t *ctx, tensor_dtype_t dt, const void *row, const float *x,
+                   int nb, int cols, float *out, cudaStream_t stream);
+// y[i] += alpha * t[i] on device.
+int launch_axpy(kernel_context_t *ctx, float *y, const float *t, float alpha, size_t n,
+                cudaStream_t stream);
+
+// Sharded all-gather of per-rank slices (NCCL).  Defined in shard.cu.
+int shard_allgather(kernel_context_t *ctx, const float *send, float *recv, size_t count,
+                    cudaStream_t stream);
+void shard_destroy(kernel_context_t *ctx);
+
+// Rows owned by `rank` of `world` for a tensor of `rows` rows.
+inline void shard_rows(int rows, int rank, int world, int *row0, int *nrows) {
+    int per = (rows + world - 1) / world;
+    int b = rank * per;
+    int e = b + per;
+    if (b > rows) b = rows;
+    if (e > rows) e = rows;
+    *row0 = b;
+    *nrows = e - b;
+}
