@@ -208,6 +208,9 @@ extern "C" SAPPHIRE_API void kernel_ctx_destroy(kernel_context_t *ctx) {
             if (ctx->d_y) cudaFree(ctx->d_y);
             if (ctx->d_g) cudaFree(ctx->d_g);
             if (ctx->d_t) cudaFree(ctx->d_t);
+            if (ctx->d_part) cudaFree(ctx->d_part);
+            if (ctx->d_cnt) cudaFree(ctx->d_cnt);
+            if (ctx->h_err) cudaFreeHost(ctx->h_err);
             shard_destroy(ctx);
             if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
         }
@@ -282,6 +285,62 @@ int ensure_scratch(kernel_context_t *ctx, float **buf, size_t *cap, size_t bytes
     }
     CUDA_TRY(ctx, cudaMalloc((void **)buf, want));
     *cap = want;
+    return 0;
+}
+
+// ------------------------------------------------ pipelined GEMV scratch ---
+// Partial sums and zeroed arrival counters for the pipelined kernel, grown on
+// demand; the counters return to zero at the end of every launch, so only new
+// memory needs clearing.  The error word lives in mapped pinned host memory:
+// a kernel writes it only on failure and the host reads it after a sync.
+static int ensure_pipe_scratch(kernel_context_t *ctx, size_t part_floats, size_t cnt_ints) {
+    if (!ctx->h_err) {
+        int *h = nullptr;
+        CUDA_TRY(ctx, cudaHostAlloc((void **)&h, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable));
+        *h = 0;
+        int *d = nullptr;
+        if (cudaHostGetDevicePointer((void **)&d, h, 0) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFreeHost(h);
+            ctx_fail(ctx, "ensure_pipe_scratch", "no device alias for the mapped error word");
+            return -1;
+        }
+        ctx->h_err = h;
+        ctx->d_err = d;
+    }
+    if (ensure_scratch(ctx, &ctx->d_part, &ctx->d_part_cap, part_floats * sizeof(float))) return -1;
+    if (ctx->d_cnt_cap < cnt_ints * sizeof(int) || !ctx->d_cnt) {
+        float *buf = reinterpret_cast<float *>(ctx->d_cnt);
+        size_t cap = ctx->d_cnt_cap;
+        if (ensure_scratch(ctx, &buf, &cap, cnt_ints * sizeof(int))) return -1;
+        ctx->d_cnt = reinterpret_cast<int *>(buf);
+        ctx->d_cnt_cap = cap;
+        CUDA_TRY(ctx, cudaMemsetAsync(ctx->d_cnt, 0, cap, ctx->stream));
+    }
+    return 0;
+}
+
+int launch_gemv_best(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t st) {
+    // SAPPHIRE_GEMV_KERNEL=tile selects the one-warp-per-tile kernel (A/B runs).
+    static const bool force_tile = [] {
+        const char *v = getenv("SAPPHIRE_GEMV_KERNEL");
+        return v && strcmp(v, "tile") == 0;
+    }();
+    if (!force_tile && pipe_supported(w)) {
+        size_t pf = 0, ci = 0;
+        pipe_scratch_size(ctx, w, &pf, &ci);
+        if (ensure_pipe_scratch(ctx, pf, ci)) return -1;
+        return launch_gemv_pipe(ctx, w, x, y, ctx->d_part, ctx->d_cnt, ctx->d_err, st);
+    }
+    return launch_gemv(ctx, w, x, w.cols, y, w.nrows, 1, st);
+}
+
+int check_kernel_error(kernel_context_t *ctx, const char *who) {
+    if (ctx->h_err && *reinterpret_cast<volatile int *>(ctx->h_err)) {
+        *ctx->h_err = 0;
+        ctx_fail(ctx, who, "a GEMV kernel gave up waiting for its weight copies (bounded wait expired)");
+        return -1;
+    }
     return 0;
 }
 

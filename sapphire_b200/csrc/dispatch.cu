@@ -73,7 +73,8 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
             if (ensure_scratch(ctx, &ctx->d_y, &ctx->d_y_cap, (size_t)batch * rows * sizeof(float))) return -1;
             yd = ctx->d_y;
         }
-        if (launch_gemv(ctx, *w, xd, cols, yd, rows, batch, st)) return -1;
+        if (batch == 1 ? launch_gemv_best(ctx, *w, xd, yd, st) : launch_gemv(ctx, *w, xd, cols, yd, rows, batch, st))
+            return -1;
         if (!y_on_dev)
             CUDA_TRY(ctx, cudaMemcpyAsync(Y, yd, (size_t)batch * rows * sizeof(float), cudaMemcpyDeviceToHost, st));
     } else {
@@ -85,7 +86,9 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
         float *send = ctx->d_g;
         float *recv = ctx->d_g + slice;
         if (w->nrows < per) CUDA_TRY(ctx, cudaMemsetAsync(send, 0, slice * sizeof(float), st));
-        if (launch_gemv(ctx, *w, xd, cols, send, per, batch, st)) return -1;
+        if (batch == 1 ? launch_gemv_best(ctx, *w, xd, send, st)
+                       : launch_gemv(ctx, *w, xd, cols, send, per, batch, st))
+            return -1;
         if (shard_allgather(ctx, send, recv, slice, st)) return -1;
         const cudaMemcpyKind kind = y_on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
         for (int r = 0; r < ctx->world; ++r) {
@@ -102,6 +105,7 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
             ctx_fail(ctx, "kernel_gemv", "GPU execution failed: %s", cudaGetErrorString(e));
             return -1;
         }
+        if (check_kernel_error(ctx, "kernel_gemv")) return -1;
     }
     return 0;
 }

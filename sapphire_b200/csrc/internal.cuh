@@ -87,6 +87,12 @@ struct sapphire_context {
     float *d_y = nullptr;  size_t d_y_cap = 0;
     float *d_g = nullptr;  size_t d_g_cap = 0;
     float *d_t = nullptr;  size_t d_t_cap = 0;
+    // Scratch of the pipelined GEMV: split-tile partials and arrival
+    // counters (kept at zero between launches), and an error word in mapped
+    // host memory that kernels set when a bounded wait gives up.
+    float *d_part = nullptr; size_t d_part_cap = 0;
+    int *d_cnt = nullptr;    size_t d_cnt_cap = 0;
+    int *h_err = nullptr;    int *d_err = nullptr;
 
     HostPool *pool = nullptr;
 
@@ -150,6 +156,19 @@ int launch_row_dot(kernel_context_t *ctx, tensor_dtype_t dt, const void *row, co
 // y[i] += alpha * t[i] on device.
 int launch_axpy(kernel_context_t *ctx, float *y, const float *t, float alpha, size_t n,
                 cudaStream_t stream);
+
+// Pipelined batch-1 GEMV (gemv_pipe.cu).
+bool pipe_supported(const DevWeight &w);
+void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints);
+int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part,
+                     int *cnt, int *err, cudaStream_t stream);
+int pipe_kmax(long long T, long long W, int nseg);
+// Batch-1 product through the pipelined kernel when it applies, else the
+// tile kernel; checks nothing on the host (asynchronous).
+int launch_gemv_best(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t stream);
+// Reads and clears the error word after a synchronisation; -1 if a kernel
+// reported a failed wait.
+int check_kernel_error(kernel_context_t *ctx, const char *who);
 
 // Sharded all-gather of per-rank slices (NCCL).  Defined in shard.cu.
 int shard_allgather(kernel_context_t *ctx, const float *send, float *recv, size_t count,

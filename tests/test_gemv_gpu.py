@@ -152,6 +152,28 @@ def test_gemv_shapes(sp, ctx, oracle, dtype, rows, cols):
     assert normwise_rel(y, oracle_y(oracle, dtype, packed, rows, cols, x)[0]) < GEMV_RTOL
 
 
+SPLIT_SHAPES = [(Q8_0, 4096, 640), (Q4_0, 4096, 2560), (TQ2_0, 64, 16384), (TQ2_0, 2048, 4096),
+                (Q4_0, 33, 16384), (F32, 100, 3000), (BF16, 700, 4100)]
+
+
+def test_pipelined_split_tiles_deterministic_and_repeatable(sp, ctx, oracle):
+    # Shapes whose 32-row tiles are shared by several warps of the persistent
+    # kernel: the combine must be exact to the oracle bar, bitwise repeatable,
+    # and leave its counters at zero for the next call (interleaved shapes).
+    cases = []
+    for dtype, rows, cols in SPLIT_SHAPES:
+        packed = rand_packed(oracle, dtype, rows, cols, seed=rows + cols)
+        x = np.random.default_rng(rows).standard_normal(cols, dtype=np.float32)
+        A = sp.Tensor(dtype, (rows, cols), packed)
+        cases.append((A, x, oracle_y(oracle, dtype, packed, rows, cols, x)[0]))
+    first = [sp.gemv(ctx, A, x) for A, x, _ in cases]
+    for _ in range(3):
+        for (A, x, ref), y0 in zip(cases, first):
+            y = sp.gemv(ctx, A, x)
+            assert np.array_equal(y, y0)
+            assert normwise_rel(y, ref) < GEMV_RTOL
+
+
 @pytest.mark.parametrize("dtype", [Q4_0, Q8_0, TQ2_0, F32])
 @pytest.mark.parametrize("batch", [2, 3, 8, 11])
 def test_gemm_batched(sp, ctx, oracle, dtype, batch):
