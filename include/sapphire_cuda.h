@@ -69,6 +69,23 @@ SAPPHIRE_API size_t kernel_ctx_resident_bytes(kernel_context_t *ctx);
 SAPPHIRE_API int kernel_gemv_device(kernel_context_t *ctx, float *y, const tensor_t *A, const float *x);
 /** Y[b*rows + r] = A[r,:] . X[b*cols ..] for b < batch_size (device pointers). */
 SAPPHIRE_API int kernel_gemm_device(kernel_context_t *ctx, float *Y, const tensor_t *A, const float *X, int batch_size);
+/** Batch-1 y = A @ x like kernel_gemv_device, for callers that must not
+ *  allocate device memory when they multiply (a serving loop with a fixed
+ *  memory budget or pool, or a path where an allocation's implicit device
+ *  synchronisation would stall other work).  No counterpart in the reference.
+ *  Calls no cudaMalloc / cudaFree: A must already be resident
+ *  (kernel_tensor_upload, which allocates, at model load); y and x are device
+ *  pointers on the context's GPU; the work is enqueued on the context stream.
+ *  Scratch is a fixed 4 MiB device array inside the library, held by every
+ *  GPU that loads it until exit.  The scratch grows with the row count (about
+ *  260 bytes per 32 rows at 640 columns: the 262144-row LM head needs 2.1 MB);
+ *  a weight that needs more than 4 MiB is rejected with -1 and an error
+ *  message.  The first call on a device looks up the
+ *  array's device address, so make that call before any stream capture.  All
+ *  calls share the array and it keeps the last call's contents (each call
+ *  clears what must start at zero): calls that overlap on the GPU, from any
+ *  context or stream, race.  Not for sharded contexts. */
+SAPPHIRE_API int kernel_gemv_device_noalloc(kernel_context_t *ctx, float *y, const tensor_t *A, const float *x);
 SAPPHIRE_API int kernel_ctx_synchronize(kernel_context_t *ctx);
 /** The context's cudaStream_t (as void*). */
 SAPPHIRE_API void* kernel_ctx_get_stream(kernel_context_t *ctx);

@@ -82,6 +82,7 @@ _SIGNATURES = {
     "kernel_tensor_evict": (i32, [vp, vp]),
     "kernel_ctx_resident_bytes": (sz, [vp]),
     "kernel_gemv_device": (i32, [vp, vp, vp, vp]),
+    "kernel_gemv_device_noalloc": (i32, [vp, vp, vp, vp]),
     "kernel_gemm_device": (i32, [vp, vp, vp, vp, i32]),
     "kernel_ctx_synchronize": (i32, [vp]),
     "kernel_ctx_get_stream": (vp, [vp]),
