@@ -321,18 +321,26 @@ static int ensure_pipe_scratch(kernel_context_t *ctx, size_t part_floats, size_t
 }
 
 int launch_gemv_best(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t st) {
-    // SAPPHIRE_GEMV_KERNEL=tile selects the one-warp-per-tile kernel (A/B runs).
-    static const bool force_tile = [] {
-        const char *v = getenv("SAPPHIRE_GEMV_KERNEL");
-        return v && strcmp(v, "tile") == 0;
-    }();
-    if (!force_tile && pipe_supported(w)) {
+    if (pipe_supported(w)) {
         size_t pf = 0, ci = 0;
         pipe_scratch_size(ctx, w, &pf, &ci);
         if (ensure_pipe_scratch(ctx, pf, ci)) return -1;
         return launch_gemv_pipe(ctx, w, x, y, ctx->d_part, ctx->d_cnt, ctx->d_err, st);
     }
-    return launch_gemv(ctx, w, x, w.cols, y, w.nrows, 1, st);
+    if (w.dtype == DTYPE_F32 || w.dtype == DTYPE_BF16) return launch_gemv(ctx, w, x, w.cols, y, w.nrows, 1, st);
+    ctx_fail(ctx, "kernel_gemv", "%s weight with %d columns exceeds the kernel's shared-memory budget",
+             dtype_name(w.dtype), w.cols);
+    return -1;
+}
+
+int launch_product(kernel_context_t *ctx, const DevWeight &w, const float *x, int x_stride, float *y, int y_stride,
+                   int batch, cudaStream_t st) {
+    if (batch == 1) return launch_gemv_best(ctx, w, x, y, st);
+    if (w.dtype == DTYPE_F32 || w.dtype == DTYPE_BF16) return launch_gemv(ctx, w, x, x_stride, y, y_stride, batch, st);
+    // Quantized weights: one pipelined pass per activation row.
+    for (int b = 0; b < batch; ++b)
+        if (launch_gemv_best(ctx, w, x + (size_t)b * x_stride, y + (size_t)b * y_stride, st)) return -1;
+    return 0;
 }
 
 int check_kernel_error(kernel_context_t *ctx, const char *who) {

@@ -73,8 +73,7 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
             if (ensure_scratch(ctx, &ctx->d_y, &ctx->d_y_cap, (size_t)batch * rows * sizeof(float))) return -1;
             yd = ctx->d_y;
         }
-        if (batch == 1 ? launch_gemv_best(ctx, *w, xd, yd, st) : launch_gemv(ctx, *w, xd, cols, yd, rows, batch, st))
-            return -1;
+        if (launch_product(ctx, *w, xd, cols, yd, rows, batch, st)) return -1;
         if (!y_on_dev)
             CUDA_TRY(ctx, cudaMemcpyAsync(Y, yd, (size_t)batch * rows * sizeof(float), cudaMemcpyDeviceToHost, st));
     } else {
@@ -86,9 +85,7 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
         float *send = ctx->d_g;
         float *recv = ctx->d_g + slice;
         if (w->nrows < per) CUDA_TRY(ctx, cudaMemsetAsync(send, 0, slice * sizeof(float), st));
-        if (batch == 1 ? launch_gemv_best(ctx, *w, xd, send, st)
-                       : launch_gemv(ctx, *w, xd, cols, send, per, batch, st))
-            return -1;
+        if (launch_product(ctx, *w, xd, cols, send, per, batch, st)) return -1;
         if (shard_allgather(ctx, send, recv, slice, st)) return -1;
         const cudaMemcpyKind kind = y_on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
         for (int r = 0; r < ctx->world; ++r) {

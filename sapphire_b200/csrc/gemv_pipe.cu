@@ -1,30 +1,43 @@
 // gemv_pipe.cu - persistent, TMA-pipelined batch-1 GEMV (the decode hot path).
 //
-// Same products as gemv.cu (reference row kernels src/kernels/q4_0_avx.c,
-// q8_0_avx.c, applied to every row by src/kernels/pool.c:106-143, plus the
-// ternary and dense formats), over the same tile layout (internal.cuh).
+// Same products as the reference row kernels (src/kernels/q4_0_avx.c:102-148,
+// q8_0_avx.c:16-136, driven per row by src/kernels/pool.c:106-143), plus the
+// ternary format and dense F32 / BF16 rows.
 //
-// Work split.  The weight is cut into items = (32-row tile, K segment of SEG
-// 16-byte chunks).  Items are numbered tile-major and every warp of a
-// persistent grid (one CTA per SM) takes a contiguous, equal-size range of
-// them, so all SMs stream the same number of bytes whatever the matrix shape.
+// Work split.  The weight is cut into items = (32-row tile, K segment).  Items
+// are numbered tile-major and every warp of a persistent grid (one CTA per SM)
+// takes a contiguous, equal-size range of them, so every SM streams the same
+// number of bytes whatever the matrix shape.
 //
-// Memory pipeline.  Each warp owns a ring of STAGES shared-memory slots.  Lane
-// 0 fills a slot with one `cp.async.bulk` of the item's codes (SEG x 512
-// contiguous bytes) and one of its scales, completing on the slot's mbarrier
-// (expect_tx); the warp waits on the mbarrier, decodes and accumulates from
-// shared memory, and refills the slot with the item STAGES ahead.  That keeps
-// STAGES items of every warp in flight while it computes.
+// Memory pipeline.  Each warp owns a ring of kStages shared-memory slots.  Lane
+// 0 fills a slot with one `cp.async.bulk` of the item's codes (4 KB) and one of
+// its scales, completing on the slot's mbarrier (expect_tx); the warp waits on
+// the mbarrier, computes from shared memory and refills the slot with the item
+// kStages ahead, so kStages items per warp are always in flight.
+//
+// Dot products of the quantized formats run on the integer tensor cores
+// (mma.sync m16n8k32, s8 x s8 -> s32): x is split per 32-column block into
+// three balanced int8 digits of a 22-bit fixed-point value
+//     x_j ~= 2^-e_b * (d0_j + 256 d1_j + 65536 d2_j)
+// (error <= 2^-22 of the block's largest |x|), which form the B operand
+// (columns 0..2 of an n8 tile).  The codes are the A operand exactly as
+// stored (Q8_0), as nibbles with a column-sum correction for the -8 offset
+// (Q4_0, u8 x s8), or as 2-bit trits mapped to -1/0/+1 by a byte permute
+// (TQ2_0).  Integer products are exact; each block's int32 result is scaled
+// by its fp32 scale (and 2^-e_b) in fp32, like the reference's per-block scale.
+// Dense F32 / BF16 rows use fp32 FMAs (one lane per row).
 //
 // Split tiles.  A tile whose segments span several warps is finished by the
-// last contributor to arrive: each contributor stores its per-row partial in
-// the scratch slot of its rank among the tile's contributors, fences, and bumps
-// the tile's counter; the one that sees the count complete sums the slots in
-// slot order (deterministic), writes y and resets the counter to 0.
+// last contributor: each stores its per-row partial (fp32, or the exact int64
+// sum for ternary) in the slot of its rank among the tile's contributors,
+// fences, and bumps the tile's counter; the one that completes the count sums
+// the slots in slot order (deterministic), writes y and resets the counter.
 //
 // Waits are bounded: a slot that does not fill within kWaitLimit polls sets
-// bit 0 of *err, the warp waits (bounded again) for its copies in flight and
-// returns.
+// bit 0 of *err; the warp then waits (bounded again) for its copies in flight
+// and returns.
+#include <cfloat>
+
 #include "internal.cuh"
 
 namespace {
@@ -32,9 +45,9 @@ namespace {
 constexpr int kPipeWarps = 8;
 constexpr int kPipeThreads = kPipeWarps * 32;
 constexpr int kStages = 4;
-constexpr int kSeg = 8;                       // 16-byte chunks per item (4 KB of codes)
-constexpr float kTwo23 = 8388608.0f;
+constexpr int kUnitsPerItem = 8;              // dense: 8 x 512 B of codes per item
 constexpr unsigned kWaitLimit = 1u << 26;
+constexpr int kDigitBytesPerBlock = 96;       // 3 digit rows x 4 lanes x 8 bytes
 
 // ------------------------------------------------------------ PTX helpers --
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -53,8 +66,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                  : "memory");
 }
-// Bulk global -> shared copy of `bytes` (16-byte aligned, multiple of 16),
-// completing on `bar`.  No multicast.
+// Bulk global -> shared copy (16-byte aligned, multiple of 16 bytes), no multicast.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -71,120 +83,323 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
         : "memory");
     return ok != 0;
 }
-// Poll until the phase completes; false after kWaitLimit polls.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase) {
     for (unsigned i = 0; i < kWaitLimit; ++i)
         if (mbar_try_wait(bar, phase)) return true;
     return false;
 }
 
-__device__ __forceinline__ float byte_plus_2p23(uint32_t w, const int k) {
-    return __int_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (unsigned)k));
+// D += A(16x32, s8 row) * B(32x8, s8 col)
+__device__ __forceinline__ void mma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+// D += A(16x32, u8 row) * B(32x8, s8 col)
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
-// --------------------------------------------------------- format traits --
-// Per-format constants and the consumer step of one 16-byte chunk (the lane's
-// row) against the shared-memory copy of x.
+template <typename T>
+__device__ __forceinline__ T lds(const uint8_t *p) {
+    return *reinterpret_cast<const T *>(p);
+}
+
+// ------------------------------------------------------------ formats -----
+// Per-format geometry of an item in the device layout (internal.cuh).
 template <tensor_dtype_t DT>
-struct Fmt;
-
+struct Geo;
 template <>
-struct Fmt<DTYPE_Q8_0> {
-    static constexpr int kCPB = 2;            // chunks per 32-weight block
-    static constexpr int kW = 16;             // weights per chunk
-    static constexpr bool kBlockScale = true;
-    static __device__ __forceinline__ float chunk(uint4 c, const float *xs) {
-        const uint32_t w[4] = {c.x ^ 0x80808080u, c.y ^ 0x80808080u, c.z ^ 0x80808080u, c.w ^ 0x80808080u};
-        const float4 *x4 = reinterpret_cast<const float4 *>(xs);
-        float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float4 v = x4[i];
-            a0 = fmaf(byte_plus_2p23(w[i], 0) - (kTwo23 + 128.0f), v.x, a0);
-            a1 = fmaf(byte_plus_2p23(w[i], 1) - (kTwo23 + 128.0f), v.y, a1);
-            a0 = fmaf(byte_plus_2p23(w[i], 2) - (kTwo23 + 128.0f), v.z, a0);
-            a1 = fmaf(byte_plus_2p23(w[i], 3) - (kTwo23 + 128.0f), v.w, a1);
-        }
-        return a0 + a1;
-    }
+struct Geo<DTYPE_Q8_0> {
+    static constexpr bool kMma = true;
+    static constexpr int kCodeBpb = 1024;     // code bytes per (tile, block)
+    static constexpr int kBpi = 4;            // blocks per item
+    static constexpr int kScaleBytes = kBpi * 128;
+};
+template <>
+struct Geo<DTYPE_Q4_0> {
+    static constexpr bool kMma = true;
+    static constexpr int kCodeBpb = 512;
+    static constexpr int kBpi = 8;
+    static constexpr int kScaleBytes = kBpi * 128;
+};
+template <>
+struct Geo<DTYPE_TQ2_0> {
+    static constexpr bool kMma = true;
+    static constexpr int kCodeBpb = 256;
+    static constexpr int kBpi = 16;
+    static constexpr int kScaleBytes = 0;     // row scale, read at the end of a tile
+};
+template <>
+struct Geo<DTYPE_F32> {                     // dense: items are 8 x 512-byte units
+    static constexpr bool kMma = false;
+    static constexpr int kCodeBpb = 512;
+    static constexpr int kBpi = 1;
+    static constexpr int kScaleBytes = 0;
+};
+template <>
+struct Geo<DTYPE_BF16> {
+    static constexpr bool kMma = false;
+    static constexpr int kCodeBpb = 512;
+    static constexpr int kBpi = 1;
+    static constexpr int kScaleBytes = 0;
 };
 
-template <>
-struct Fmt<DTYPE_Q4_0> {
-    static constexpr int kCPB = 1;
-    static constexpr int kW = 32;
-    static constexpr bool kBlockScale = true;
-    static __device__ __forceinline__ float chunk(uint4 c, const float *xs) {
-        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-        const float4 *x4 = reinterpret_cast<const float4 *>(xs);
-        float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t lo = w[i] & 0x0F0F0F0Fu;
-            const uint32_t hi = (w[i] >> 4) & 0x0F0F0F0Fu;
-            const float4 v0 = x4[2 * i], v1 = x4[2 * i + 1];
-            a0 = fmaf(byte_plus_2p23(lo, 0) - (kTwo23 + 8.0f), v0.x, a0);
-            a1 = fmaf(byte_plus_2p23(hi, 0) - (kTwo23 + 8.0f), v0.y, a1);
-            a0 = fmaf(byte_plus_2p23(lo, 1) - (kTwo23 + 8.0f), v0.z, a0);
-            a1 = fmaf(byte_plus_2p23(hi, 1) - (kTwo23 + 8.0f), v0.w, a1);
-            a0 = fmaf(byte_plus_2p23(lo, 2) - (kTwo23 + 8.0f), v1.x, a0);
-            a1 = fmaf(byte_plus_2p23(hi, 2) - (kTwo23 + 8.0f), v1.y, a1);
-            a0 = fmaf(byte_plus_2p23(lo, 3) - (kTwo23 + 8.0f), v1.z, a0);
-            a1 = fmaf(byte_plus_2p23(hi, 3) - (kTwo23 + 8.0f), v1.w, a1);
-        }
-        return a0 + a1;
-    }
+template <tensor_dtype_t DT>
+__host__ __device__ constexpr int stage_bytes() {
+    return 4096 + Geo<DT>::kScaleBytes;
+}
+
+struct PipeParams {
+    const uint8_t *codes;
+    const float *scales;
+    const float *x;
+    float *y;
+    void *part;                 // [ntiles][kmax][32] partials of split tiles (fp32; int64 for TQ2_0)
+    int *cnt;                   // [ntiles] arrival counters, zero between launches
+    int *err;                   // error word
+    long long total_items;
+    int nrows, cols, nb, ntiles, kchunks, nseg, kmax, total_warps;
 };
 
-template <>
-struct Fmt<DTYPE_TQ2_0> {
-    static constexpr int kCPB = 1;            // unused: row scale, not block scale
-    static constexpr int kW = 64;
-    static constexpr bool kBlockScale = false;
-    // (c - 1) * 4^p decoded in place, position-wise accumulators rescaled here.
-    static __device__ __forceinline__ float chunk(uint4 c, const float *xs) {
-        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-        const float4 *x4 = reinterpret_cast<const float4 *>(xs);
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint32_t bb = __byte_perm(w[i], 0x4B000000u, 0x7440u | (unsigned)k);
-                const float4 v = x4[4 * i + k];
-                a0 = fmaf(__int_as_float(bb & 0x4B000003u) - (kTwo23 + 1.0f), v.x, a0);
-                a1 = fmaf(__int_as_float(bb & 0x4B00000Cu) - (kTwo23 + 4.0f), v.y, a1);
-                a2 = fmaf(__int_as_float(bb & 0x4B000030u) - (kTwo23 + 16.0f), v.z, a2);
-                a3 = fmaf(__int_as_float(bb & 0x4B0000C0u) - (kTwo23 + 64.0f), v.w, a3);
+__device__ __forceinline__ long long range_begin(long long w, long long T, long long W) { return (w * T) / W; }
+__device__ __forceinline__ int item_owner(long long i, long long T, long long W) {
+    long long w = ((i + 1) * W + T - 1) / T - 1;
+    return (int)(w < W - 1 ? w : W - 1);
+}
+
+// ------------------------------------------------------- x preparation ----
+// Shared-memory image of x for the MMA formats:
+//   digits[nb][3][4][8]  B fragments (digit rows 0..2, per lane-in-group tig:
+//                        word 0 then word 1), a 16-byte zero word after them
+//                        for lanes whose B column is 3..7;
+//   pexp[nb]             2^-e_b per block (TQ2_0: one global value in [0]);
+//   corr[nb][4][2]       Q4_0 only: -8 * (sum of the block's digits of row
+//                        2*tig+j), the correction of the unsigned codes.
+struct XPrep {
+    uint8_t *digits;
+    float *pexp;
+    int *corr;
+    int *nonfinite;
+};
+
+__device__ __forceinline__ size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+
+__host__ __device__ inline size_t xprep_bytes_h(int nb, bool q4) {
+    size_t b = (size_t)nb * kDigitBytesPerBlock + 16;
+    b = (b + 15) & ~(size_t)15;
+    b += ((size_t)nb * 4 + 15) & ~(size_t)15;
+    if (q4) b += (size_t)nb * 32;
+    return b + 16;
+}
+
+// Balanced base-256 digits of an integer |X| < 2^22: X = d0 + 256 d1 + 65536 d2.
+__device__ __forceinline__ void digits3(int X, int &d0, int &d1, int &d2) {
+    d0 = ((X & 0xFF) ^ 0x80) - 0x80;
+    const int X1 = (X - d0) >> 8;
+    d1 = ((X1 & 0xFF) ^ 0x80) - 0x80;
+    d2 = (X1 - d1) >> 8;
+}
+
+// Exponent e with max|x| * 2^e < 2^22 (0 for an all-zero block).
+__device__ __forceinline__ int block_exponent(float m) {
+    if (!(m > 0.0f)) return 0;
+    int E;
+    frexpf(m, &E);
+    return 22 - E;
+}
+
+// Byte offset of x position p (0..31) of a block inside its 32-byte digit
+// row image [tig][word][byte], for each format's A-fragment k order.
+template <tensor_dtype_t DT>
+__device__ __forceinline__ int digit_slot(int p) {
+    if (DT == DTYPE_Q8_0) {                   // k = p
+        const int tig = (p & 15) >> 2, w = p >> 4, j = p & 3;
+        return tig * 8 + w * 4 + j;
+    } else if (DT == DTYPE_Q4_0) {            // k = tig*4+j <-> p = 8tig+2j (word 0), +1 (word 1)
+        const int tig = p >> 3, j = (p & 7) >> 1, w = p & 1;
+        return tig * 8 + w * 4 + j;
+    } else {                                  // TQ2_0: byte-permute order of the trit decode
+        const int hi = p >> 4, q = p & 15, tig = q >> 2, r = q & 3;
+        return tig * 8 + (r & 1) * 4 + (r >> 1) + 2 * hi;
+    }
+}
+
+template <tensor_dtype_t DT>
+__device__ void prepare_x(const PipeParams &p, XPrep xp) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ float s_red[kPipeWarps];
+    int gexp = 0;
+    if (DT == DTYPE_TQ2_0) {
+        // One exponent for the whole row (the ternary sum runs over all of K in int32).
+        float m = 0.0f;
+        for (int i = threadIdx.x; i < p.cols; i += blockDim.x) m = fmaxf(m, fabsf(p.x[i]));
+        bool bad = false;
+        for (int i = threadIdx.x; i < p.cols; i += blockDim.x) bad |= !isfinite(p.x[i]);
+        if (bad) *xp.nonfinite = 1;
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_red[warp] = m;
+        __syncthreads();
+        m = 0.0f;
+        for (int i = 0; i < kPipeWarps; ++i) m = fmaxf(m, s_red[i]);
+        gexp = block_exponent(isfinite(m) ? m : FLT_MAX);
+        if (threadIdx.x == 0) xp.pexp[0] = ldexpf(1.0f, -gexp);
+    }
+    for (int b = warp; b < p.nb; b += kPipeWarps) {
+        const int c = b * 32 + lane;
+        const float v = c < p.cols ? p.x[c] : 0.0f;
+        int e = gexp;
+        if (DT != DTYPE_TQ2_0) {
+            if (!isfinite(v)) *xp.nonfinite = 1;
+            float m = fabsf(v);
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            e = block_exponent(isfinite(m) ? m : FLT_MAX);
+            if (lane == 0) xp.pexp[b] = ldexpf(1.0f, -e);
+        }
+        const int X = isfinite(v) ? __float2int_rn(ldexpf(v, e)) : 0;
+        int d0, d1, d2;
+        digits3(X, d0, d1, d2);
+        uint8_t *row = xp.digits + (size_t)b * kDigitBytesPerBlock;
+        const int off = digit_slot<DT>(lane);
+        row[0 * 32 + off] = (uint8_t)(int8_t)d0;
+        row[1 * 32 + off] = (uint8_t)(int8_t)d1;
+        row[2 * 32 + off] = (uint8_t)(int8_t)d2;
+        if (DT == DTYPE_Q4_0) {
+            int s0 = d0, s1 = d1, s2 = d2;
+            for (int o = 16; o; o >>= 1) {
+                s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+                s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+                s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+            }
+            if (lane < 8) {
+                // corr[b][tig][j] for digit row 2*tig + j (rows 3..7 are zero)
+                const int r = lane;       // lane = 2*tig + j
+                xp.corr[b * 8 + lane] = r == 0 ? -8 * s0 : r == 1 ? -8 * s1 : r == 2 ? -8 * s2 : 0;
             }
         }
-        return a0 + 0.25f * a1 + 0.0625f * a2 + 0.015625f * a3;
+    }
+    if (threadIdx.x < 4) reinterpret_cast<uint32_t *>(xp.digits + (size_t)p.nb * kDigitBytesPerBlock)[threadIdx.x] = 0;
+}
+
+// --------------------------------------------------------- MMA consumers --
+// Accumulator state of one 32-row tile for a lane (g = lane/4, tig = lane%4).
+struct MmaAcc {
+    float f[2][4];      // Q8_0 / Q4_0: scaled partial sums per (half, D register)
+    int d[2][4];        // TQ2_0: exact int32 sums
+    __device__ __forceinline__ void reset() {
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                f[h][i] = 0.0f;
+                d[h][i] = 0;
+            }
     }
 };
 
-template <>
-struct Fmt<DTYPE_F32> {
-    static constexpr int kCPB = 1;
-    static constexpr int kW = 4;
-    static constexpr bool kBlockScale = false;
-    static __device__ __forceinline__ float chunk(uint4 c, const float *xs) {
-        const float4 v = *reinterpret_cast<const float4 *>(xs);
+__device__ __forceinline__ uint2 load_b(const XPrep &xp, int nb, int b, int lane) {
+    const int g = lane >> 2, tig = lane & 3;
+    const size_t off = g < 3 ? (size_t)b * kDigitBytesPerBlock + g * 32 + tig * 8 : (size_t)nb * kDigitBytesPerBlock;
+    return lds<uint2>(xp.digits + off);
+}
+
+template <tensor_dtype_t DT>
+__device__ __forceinline__ void consume_mma(const uint8_t *st, int nblk, int blk0, int nb, int lane, const XPrep &xp,
+                                            MmaAcc &acc) {
+    using G = Geo<DT>;
+    const int g = lane >> 2, tig = lane & 3;
+#pragma unroll
+    for (int bi = 0; bi < G::kBpi; ++bi) {
+        if (bi >= nblk) break;
+        const int b = blk0 + bi;
+        const uint2 B = load_b(xp, nb, b, lane);
+        if (DT == DTYPE_TQ2_0) {
+            const uint2 A = lds<uint2>(st + bi * G::kCodeBpb + lane * 8);
+            const uint32_t tbl = 0x020100FFu;   // code c -> c - 1
+            const uint32_t m0 = A.x & 0x33333333u, n0 = (A.x >> 2) & 0x33333333u;
+            const uint32_t m1 = A.y & 0x33333333u, n1 = (A.y >> 2) & 0x33333333u;
+            mma_s8s8(acc.d[0], __byte_perm(tbl, 0, m0), __byte_perm(tbl, 0, m0 >> 16), __byte_perm(tbl, 0, n0),
+                     __byte_perm(tbl, 0, n0 >> 16), B.x, B.y);
+            mma_s8s8(acc.d[1], __byte_perm(tbl, 0, m1), __byte_perm(tbl, 0, m1 >> 16), __byte_perm(tbl, 0, n1),
+                     __byte_perm(tbl, 0, n1 >> 16), B.x, B.y);
+        } else {
+            int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
+            if (DT == DTYPE_Q8_0) {
+                const uint4 A0 = lds<uint4>(st + bi * G::kCodeBpb + lane * 16);
+                const uint4 A1 = lds<uint4>(st + bi * G::kCodeBpb + 512 + lane * 16);
+                mma_s8s8(d0, A0.x, A0.y, A0.z, A0.w, B.x, B.y);
+                mma_s8s8(d1, A1.x, A1.y, A1.z, A1.w, B.x, B.y);
+            } else {
+                const uint4 A = lds<uint4>(st + bi * G::kCodeBpb + lane * 16);
+                const uint32_t lo0 = A.x & 0x0F0F0F0Fu, hi0 = (A.x >> 4) & 0x0F0F0F0Fu;
+                const uint32_t lo1 = A.y & 0x0F0F0F0Fu, hi1 = (A.y >> 4) & 0x0F0F0F0Fu;
+                const uint32_t lo2 = A.z & 0x0F0F0F0Fu, hi2 = (A.z >> 4) & 0x0F0F0F0Fu;
+                const uint32_t lo3 = A.w & 0x0F0F0F0Fu, hi3 = (A.w >> 4) & 0x0F0F0F0Fu;
+                mma_u8s8(d0, lo0, lo1, hi0, hi1, B.x, B.y);
+                mma_u8s8(d1, lo2, lo3, hi2, hi3, B.x, B.y);
+                const int2 C = lds<int2>(reinterpret_cast<const uint8_t *>(xp.corr) + (size_t)b * 32 + tig * 8);
+                d0[0] += C.x; d0[2] += C.x; d1[0] += C.x; d1[2] += C.x;
+                d0[1] += C.y; d0[3] += C.y; d1[1] += C.y; d1[3] += C.y;
+            }
+            // Scales of rows g, g+8, g+16, g+24 for this block, times 2^-e_b.
+            const float4 S = lds<float4>(st + 4096 + bi * 128 + g * 16);
+            const float pe = xp.pexp[b];
+            const float s0 = S.x * pe, s1 = S.y * pe, s2 = S.z * pe, s3 = S.w * pe;
+            acc.f[0][0] = fmaf(s0, (float)d0[0], acc.f[0][0]);
+            acc.f[0][1] = fmaf(s0, (float)d0[1], acc.f[0][1]);
+            acc.f[0][2] = fmaf(s1, (float)d0[2], acc.f[0][2]);
+            acc.f[0][3] = fmaf(s1, (float)d0[3], acc.f[0][3]);
+            acc.f[1][0] = fmaf(s2, (float)d1[0], acc.f[1][0]);
+            acc.f[1][1] = fmaf(s2, (float)d1[1], acc.f[1][1]);
+            acc.f[1][2] = fmaf(s3, (float)d1[2], acc.f[1][2]);
+            acc.f[1][3] = fmaf(s3, (float)d1[3], acc.f[1][3]);
+        }
+    }
+}
+
+// Per-row results of a tile for lanes with tig == 0: rows g + 8*i, i = 0..3,
+// as 8-byte values (fp32 bits for Q8_0 / Q4_0, the exact int64 sum for
+// TQ2_0).  All lanes must call (shuffles).
+template <tensor_dtype_t DT>
+__device__ __forceinline__ void mma_rows(const MmaAcc &acc, unsigned long long (&v)[4]) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        if (DT == DTYPE_TQ2_0) {
+            const int up0 = __shfl_down_sync(0xffffffffu, acc.d[h][0], 1);
+            const int up2 = __shfl_down_sync(0xffffffffu, acc.d[h][2], 1);
+            const long long r0 = (long long)acc.d[h][0] + 256LL * acc.d[h][1] + 65536LL * up0;
+            const long long r1 = (long long)acc.d[h][2] + 256LL * acc.d[h][3] + 65536LL * up2;
+            v[2 * h] = (unsigned long long)r0;
+            v[2 * h + 1] = (unsigned long long)r1;
+        } else {
+            const float up0 = __shfl_down_sync(0xffffffffu, acc.f[h][0], 1);
+            const float up2 = __shfl_down_sync(0xffffffffu, acc.f[h][2], 1);
+            const float r0 = (float)((double)acc.f[h][0] + 256.0 * acc.f[h][1] + 65536.0 * up0);
+            const float r1 = (float)((double)acc.f[h][2] + 256.0 * acc.f[h][3] + 65536.0 * up2);
+            v[2 * h] = __float_as_uint(r0);
+            v[2 * h + 1] = __float_as_uint(r1);
+        }
+    }
+}
+
+// ------------------------------------------------------- dense consumer ---
+template <tensor_dtype_t DT>
+__device__ __forceinline__ float dense_chunk(uint4 c, const float *xs) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
+    if (DT == DTYPE_F32) {
+        const float4 v = x4[0];
         float a = __uint_as_float(c.x) * v.x;
         a = fmaf(__uint_as_float(c.y), v.y, a);
         a = fmaf(__uint_as_float(c.z), v.z, a);
         return fmaf(__uint_as_float(c.w), v.w, a);
-    }
-};
-
-template <>
-struct Fmt<DTYPE_BF16> {
-    static constexpr int kCPB = 1;
-    static constexpr int kW = 8;
-    static constexpr bool kBlockScale = false;
-    static __device__ __forceinline__ float chunk(uint4 c, const float *xs) {
+    } else {
         const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-        const float4 *x4 = reinterpret_cast<const float4 *>(xs);
         const float4 v0 = x4[0], v1 = x4[1];
         float a0 = __uint_as_float(w[0] << 16) * v0.x, a1 = __uint_as_float(w[0] & 0xFFFF0000u) * v0.y;
         a0 = fmaf(__uint_as_float(w[1] << 16), v0.z, a0);
@@ -195,49 +410,42 @@ struct Fmt<DTYPE_BF16> {
         a1 = fmaf(__uint_as_float(w[3] & 0xFFFF0000u), v1.w, a1);
         return a0 + a1;
     }
-};
-
-template <tensor_dtype_t DT>
-struct Layout {
-    static constexpr int kCodeBytes = kSeg * 512;
-    static constexpr int kScaleBytes = Fmt<DT>::kBlockScale ? (kSeg / Fmt<DT>::kCPB) * 128 : 0;
-    static constexpr int kStageBytes = kCodeBytes + kScaleBytes;   // multiple of 128
-};
-
-struct PipeParams {
-    const uint4 *codes;
-    const float *scales;
-    const float *x;
-    float *y;
-    float *part;              // [ntiles][kmax][32] partial sums of split tiles
-    int *cnt;                 // [ntiles] arrival counters, zero between calls
-    int *err;                 // error word (host-mapped)
-    long long total_items;
-    int nrows, cols, nb, ntiles, kchunks, nseg, kmax, total_warps;
-};
-
-__device__ __forceinline__ long long range_begin(long long w, long long T, long long W) { return (w * T) / W; }
-// Warp whose range holds item i (ranges are [begin(w), begin(w+1))).
-__device__ __forceinline__ int item_owner(long long i, long long T, long long W) {
-    long long w = ((i + 1) * W + T - 1) / T - 1;
-    return (int)(w < W - 1 ? w : W - 1);
 }
 
+// ---------------------------------------------------------- tile output ---
+// Final fp32 value of one row from its 8-byte sum.
 template <tensor_dtype_t DT>
-__device__ __forceinline__ float finalize(const PipeParams &p, int tile, int lane, float v) {
-    if (DT == DTYPE_TQ2_0) return __ldg(p.scales + (size_t)tile * 32 + lane) * v;
-    return v;
+__device__ __forceinline__ float finish_row(const PipeParams &p, const XPrep &xp, int tile, int r, unsigned long long v,
+                                            bool nonfinite) {
+    float out;
+    if (DT == DTYPE_TQ2_0) {
+        const float s = __ldg(p.scales + (size_t)tile * 32 + (r & 7) * 4 + (r >> 3));
+        out = (float)((double)s * ((double)(long long)v * (double)xp.pexp[0]));
+    } else {
+        out = __uint_as_float((uint32_t)v);
+    }
+    return nonfinite ? __int_as_float(0x7FC00000) : out;
 }
 
-// Write a tile's result, or hand a partial to the split-tile combine.
+// Rows owned by this lane: MMA formats hold rows g + 8i (i = 0..3) on lanes
+// with tig == 0; dense formats hold row `lane` in v[0].
 template <tensor_dtype_t DT>
-__device__ void flush_tile(const PipeParams &p, int tile, int lane, int my_warp, bool whole, float acc) {
-    const int row = tile * 32 + lane;
+__device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int lane, int my_warp, bool whole,
+                           const unsigned long long (&v)[4], bool nonfinite) {
+    constexpr bool kMma = Geo<DT>::kMma;
+    const bool owner_lane = kMma ? ((lane & 3) == 0) : true;
+    constexpr int kRows = kMma ? 4 : 1;
+    auto row_of = [&](int i) { return kMma ? ((lane >> 2) + 8 * i) : lane; };
     if (whole) {
-        if (row < p.nrows) p.y[row] = finalize<DT>(p, tile, lane, acc);
+        if (owner_lane) {
+#pragma unroll
+            for (int i = 0; i < kRows; ++i) {
+                const int r = row_of(i);
+                if (tile * 32 + r < p.nrows) p.y[(size_t)tile * 32 + r] = finish_row<DT>(p, xp, tile, r, v[i], nonfinite);
+            }
+        }
         return;
     }
-    // Contributors are the distinct owners of the tile's items, in item order.
     const long long first = (long long)tile * p.nseg;
     int k = 0, slot = -1, prev = -1;
     for (int s = 0; s < p.nseg; ++s) {
@@ -248,8 +456,15 @@ __device__ void flush_tile(const PipeParams &p, int tile, int lane, int my_warp,
             prev = o;
         }
     }
-    float *base = p.part + (size_t)tile * p.kmax * 32;
-    base[(size_t)slot * 32 + lane] = acc;
+    long long *base64 = reinterpret_cast<long long *>(p.part) + (size_t)tile * p.kmax * 32;
+    float *base32 = reinterpret_cast<float *>(p.part) + (size_t)tile * p.kmax * 32;
+    if (owner_lane) {
+#pragma unroll
+        for (int i = 0; i < kRows; ++i) {
+            if (DT == DTYPE_TQ2_0) base64[(size_t)slot * 32 + row_of(i)] = (long long)v[i];
+            else base32[(size_t)slot * 32 + row_of(i)] = __uint_as_float((uint32_t)v[i]);
+        }
+    }
     __threadfence();
     __syncwarp();
     int old = 0;
@@ -257,26 +472,50 @@ __device__ void flush_tile(const PipeParams &p, int tile, int lane, int my_warp,
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old == k - 1) {
         __threadfence();
-        float sum = 0.0f;
-        for (int j = 0; j < k; ++j) sum += __ldcg(base + (size_t)j * 32 + lane);
-        if (row < p.nrows) p.y[row] = finalize<DT>(p, tile, lane, sum);
+        if (owner_lane) {
+#pragma unroll
+            for (int i = 0; i < kRows; ++i) {
+                const int r = row_of(i);
+                unsigned long long sum;
+                if (DT == DTYPE_TQ2_0) {
+                    long long s = 0;
+                    for (int j = 0; j < k; ++j) s += __ldcg(base64 + (size_t)j * 32 + r);
+                    sum = (unsigned long long)s;
+                } else {
+                    float s = 0.0f;
+                    for (int j = 0; j < k; ++j) s += __ldcg(base32 + (size_t)j * 32 + r);
+                    sum = __float_as_uint(s);
+                }
+                if (tile * 32 + r < p.nrows) p.y[(size_t)tile * 32 + r] = finish_row<DT>(p, xp, tile, r, sum, nonfinite);
+            }
+        }
         __syncwarp();
         if (lane == 0) p.cnt[tile] = 0;
     }
 }
 
+__host__ __device__ size_t ximage_bytes(tensor_dtype_t dt, int nb, int kchunks);
+
+// --------------------------------------------------------------- kernel ---
 template <tensor_dtype_t DT>
 __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe(const PipeParams p) {
-    using F = Fmt<DT>;
-    using L = Layout<DT>;
+    using G = Geo<DT>;
+    constexpr int kStage = stage_bytes<DT>();
     extern __shared__ __align__(128) uint8_t smem[];
-    const int xpad = p.kchunks * F::kW;
-    float *xs = reinterpret_cast<float *>(smem);
-    uint8_t *ring_all = smem + (((size_t)xpad * 4 + 127) & ~(size_t)127);
+    __shared__ int s_nonfinite;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint8_t *ring = ring_all + (size_t)warp * kStages * L::kStageBytes;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ring_all + (size_t)kPipeWarps * kStages * L::kStageBytes) +
-                     warp * kStages;
+
+    // Shared memory: [x image][rings][barriers]
+    const size_t ximg = ximage_bytes(DT, p.nb, p.kchunks);
+    uint8_t *ring = smem + ximg + (size_t)warp * kStages * kStage;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ximg + (size_t)kPipeWarps * kStages * kStage) + warp * kStages;
+    XPrep xp;
+    xp.digits = smem;
+    const size_t dig_bytes = align16((size_t)p.nb * kDigitBytesPerBlock + 16);
+    xp.pexp = reinterpret_cast<float *>(smem + dig_bytes);
+    xp.corr = reinterpret_cast<int *>(smem + dig_bytes + align16((size_t)p.nb * 4));
+    xp.nonfinite = &s_nonfinite;
+    float *xs = reinterpret_cast<float *>(smem);
 
     const int gw = blockIdx.x * kPipeWarps + warp;
     const long long T = p.total_items, W = p.total_warps;
@@ -285,23 +524,31 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe(const PipeParams p)
 
     auto issue = [&](long long item, int stage) {
         const int tile = (int)(item / p.nseg), seg = (int)(item % p.nseg);
-        const int c0 = seg * kSeg;
-        const int nch = min(kSeg, p.kchunks - c0);
-        uint8_t *dst = ring + (size_t)stage * L::kStageBytes;
-        const uint8_t *src = reinterpret_cast<const uint8_t *>(p.codes) + ((size_t)tile * p.kchunks + c0) * 512;
-        uint32_t bytes = (uint32_t)nch * 512;
-        uint32_t sbytes = 0;
+        uint8_t *dst = ring + (size_t)stage * kStage;
+        const uint8_t *src;
+        uint32_t bytes, sbytes = 0;
         const float *ssrc = nullptr;
-        if (F::kBlockScale) {
-            const int b0 = c0 / F::kCPB, nblk = nch / F::kCPB;
-            ssrc = p.scales + ((size_t)tile * p.nb + b0) * 32;
-            sbytes = (uint32_t)nblk * 128;
+        if (G::kMma) {
+            const int b0 = seg * Geo<DT>::kBpi;
+            const int nblk = min(Geo<DT>::kBpi, p.nb - b0);
+            src = p.codes + (size_t)tile * p.kchunks * 512 + (size_t)b0 * Geo<DT>::kCodeBpb;
+            bytes = (uint32_t)nblk * Geo<DT>::kCodeBpb;
+            if (G::kScaleBytes) {
+                ssrc = p.scales + ((size_t)tile * p.nb + b0) * 32;
+                sbytes = (uint32_t)nblk * 128;
+            }
+        } else {
+            const int c0 = seg * kUnitsPerItem;
+            const int nch = min(kUnitsPerItem, p.kchunks - c0);
+            src = p.codes + ((size_t)tile * p.kchunks + c0) * 512;
+            bytes = (uint32_t)nch * 512;
         }
         mbar_expect_tx(bars + stage, bytes + sbytes);
         bulk_g2s(dst, src, bytes, bars + stage);
-        if (sbytes) bulk_g2s(dst + L::kCodeBytes, ssrc, sbytes, bars + stage);
+        if (sbytes) bulk_g2s(dst + 4096, ssrc, sbytes, bars + stage);
     };
 
+    if (threadIdx.x == 0) s_nonfinite = 0;
     if (lane == 0) {
         for (int s = 0; s < kStages; ++s) mbar_init(bars + s, 1);
         fence_mbar_init();
@@ -309,79 +556,98 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe(const PipeParams p)
     __syncwarp();
     if (lane == 0)
         for (int j = 0; j < kStages && j < n_items; ++j) issue(it0 + j, j);
+    __syncthreads();   // s_nonfinite initialised before x preparation writes it
 
-    // x (zero-padded to whole chunks) staged once per CTA, overlapping the
-    // first copies.
-    for (int i = threadIdx.x; i < xpad; i += blockDim.x) xs[i] = (i < p.cols) ? p.x[i] : 0.0f;
+    // x image, built once per CTA while the first copies are in flight.
+    if (G::kMma) {
+        prepare_x<DT>(p, xp);
+    } else {
+        const int xpad = p.kchunks * (DT == DTYPE_F32 ? 4 : 8);
+        for (int i = threadIdx.x; i < xpad; i += blockDim.x) xs[i] = (i < p.cols) ? p.x[i] : 0.0f;
+    }
     __syncthreads();
+    const bool nonfinite = G::kMma && s_nonfinite != 0;
 
     int cur_tile = -1;
     bool cur_whole = false;
-    float acc = 0.0f;
+    MmaAcc macc;
+    macc.reset();
+    float dacc = 0.0f;
     for (int j = 0; j < n_items; ++j) {
         const long long item = it0 + j;
         const int stage = j % kStages;
         const uint32_t phase = (uint32_t)(j / kStages) & 1u;
         if (!mbar_wait_bounded(bars + stage, phase)) {
             if (lane == 0) atomicOr(p.err, 1);
-            // Drain this warp's copies still in flight (bounded), then leave.
             for (int q = j; q < n_items && q < j + kStages; ++q)
                 (void)mbar_wait_bounded(bars + (q % kStages), (uint32_t)(q / kStages) & 1u);
             return;
         }
         const int tile = (int)(item / p.nseg), seg = (int)(item % p.nseg);
         if (tile != cur_tile) {
-            if (cur_tile >= 0) flush_tile<DT>(p, cur_tile, lane, gw, cur_whole, acc);
+            if (cur_tile >= 0) {
+                unsigned long long v[4] = {0, 0, 0, 0};
+                if (G::kMma) mma_rows<DT>(macc, v);
+                else v[0] = __float_as_uint(dacc);
+                flush_tile<DT>(p, xp, cur_tile, lane, gw, cur_whole, v, nonfinite);
+            }
             cur_tile = tile;
-            acc = 0.0f;
-            // whole = this warp holds every segment of the tile
+            macc.reset();
+            dacc = 0.0f;
             cur_whole = (seg == 0) && ((long long)tile * p.nseg + p.nseg <= it1);
         }
-        const int c0 = seg * kSeg;
-        const int nch = min(kSeg, p.kchunks - c0);
-        const uint8_t *st = ring + (size_t)stage * L::kStageBytes;
-        if (F::kBlockScale) {
-            constexpr int kBlk = kSeg / F::kCPB;
-            const int nblk = nch / F::kCPB;
-            const float *sc = reinterpret_cast<const float *>(st + L::kCodeBytes);
-#pragma unroll
-            for (int b = 0; b < kBlk; ++b) {
-                if (b < nblk) {
-                    float part = 0.0f;
-#pragma unroll
-                    for (int h = 0; h < F::kCPB; ++h) {
-                        const int ch = b * F::kCPB + h;
-                        part += F::chunk(lds128(st + (size_t)ch * 512 + lane * 16), xs + (size_t)(c0 + ch) * F::kW);
-                    }
-                    acc = fmaf(sc[b * 32 + lane], part, acc);
-                }
-            }
+        const uint8_t *st = ring + (size_t)stage * kStage;
+        if (G::kMma) {
+            const int b0 = seg * Geo<DT>::kBpi;
+            consume_mma<DT>(st, min(Geo<DT>::kBpi, p.nb - b0), b0, p.nb, lane, xp, macc);
         } else {
+            constexpr int kW = (DT == DTYPE_F32) ? 4 : 8;
+            const int c0 = seg * kUnitsPerItem;
+            const int nch = min(kUnitsPerItem, p.kchunks - c0);
 #pragma unroll
-            for (int ch = 0; ch < kSeg; ++ch)
-                if (ch < nch) acc += F::chunk(lds128(st + (size_t)ch * 512 + lane * 16), xs + (size_t)(c0 + ch) * F::kW);
+            for (int ch = 0; ch < kUnitsPerItem; ++ch)
+                if (ch < nch) dacc += dense_chunk<DT>(lds<uint4>(st + (size_t)ch * 512 + lane * 16), xs + (size_t)(c0 + ch) * kW);
         }
-        // Refill this slot with the item kStages ahead: order this warp's
-        // reads of the slot before the asynchronous write into it.
+        // Order this warp's reads of the slot before the asynchronous refill.
         fence_proxy_async();
         __syncwarp();
         if (lane == 0 && j + kStages < n_items) issue(item + kStages, stage);
     }
-    if (cur_tile >= 0) flush_tile<DT>(p, cur_tile, lane, gw, cur_whole, acc);
+    if (cur_tile >= 0) {
+        unsigned long long v[4] = {0, 0, 0, 0};
+        if (G::kMma) mma_rows<DT>(macc, v);
+        else v[0] = __float_as_uint(dacc);
+        flush_tile<DT>(p, xp, cur_tile, lane, gw, cur_whole, v, nonfinite);
+    }
 }
 
-size_t pipe_smem(tensor_dtype_t dt, int kchunks, int chunk_w) {
-    size_t stage = 0;
+__host__ __device__ size_t ximage_bytes(tensor_dtype_t dt, int nb, int kchunks) {
+    size_t b;
+    if (dt == DTYPE_Q8_0 || dt == DTYPE_Q4_0 || dt == DTYPE_TQ2_0) b = xprep_bytes_h(nb, dt == DTYPE_Q4_0);
+    else b = (size_t)kchunks * (dt == DTYPE_F32 ? 4 : 8) * 4;
+    return (b + 127) & ~(size_t)127;
+}
+
+size_t pipe_smem(tensor_dtype_t dt, int nb, int kchunks) {
+    int stage = 0;
     switch (dt) {
-        case DTYPE_Q8_0: stage = Layout<DTYPE_Q8_0>::kStageBytes; break;
-        case DTYPE_Q4_0: stage = Layout<DTYPE_Q4_0>::kStageBytes; break;
-        case DTYPE_TQ2_0: stage = Layout<DTYPE_TQ2_0>::kStageBytes; break;
-        case DTYPE_F32: stage = Layout<DTYPE_F32>::kStageBytes; break;
-        case DTYPE_BF16: stage = Layout<DTYPE_BF16>::kStageBytes; break;
+        case DTYPE_Q8_0: stage = stage_bytes<DTYPE_Q8_0>(); break;
+        case DTYPE_Q4_0: stage = stage_bytes<DTYPE_Q4_0>(); break;
+        case DTYPE_TQ2_0: stage = stage_bytes<DTYPE_TQ2_0>(); break;
+        case DTYPE_F32: stage = stage_bytes<DTYPE_F32>(); break;
+        case DTYPE_BF16: stage = stage_bytes<DTYPE_BF16>(); break;
         default: return 0;
     }
-    const size_t xbytes = ((size_t)kchunks * chunk_w * 4 + 127) & ~(size_t)127;
-    return xbytes + (size_t)kPipeWarps * kStages * stage + (size_t)kPipeWarps * kStages * 8;
+    return ximage_bytes(dt, nb, kchunks) + (size_t)kPipeWarps * kStages * stage + (size_t)kPipeWarps * kStages * 8;
+}
+
+int item_nseg(const DevWeight &w) {
+    switch (w.dtype) {
+        case DTYPE_Q8_0: return (w.nb + Geo<DTYPE_Q8_0>::kBpi - 1) / Geo<DTYPE_Q8_0>::kBpi;
+        case DTYPE_Q4_0: return (w.nb + Geo<DTYPE_Q4_0>::kBpi - 1) / Geo<DTYPE_Q4_0>::kBpi;
+        case DTYPE_TQ2_0: return (w.nb + Geo<DTYPE_TQ2_0>::kBpi - 1) / Geo<DTYPE_TQ2_0>::kBpi;
+        default: return (w.kchunks + kUnitsPerItem - 1) / kUnitsPerItem;
+    }
 }
 
 int sm_count(int dev) {
@@ -397,10 +663,10 @@ int sm_count(int dev) {
 
 }  // namespace
 
-// Largest number of warps that can share one tile: ranges have at least
-// floor(T/W) items each, so n = nseg consecutive items meet at most
-// ceil((n-1)/L) + 1 of them; with fewer items than warps every range holds at
-// most one item.
+// Largest number of warps that can share one tile: ranges hold at least
+// floor(T/W) items each, so nseg consecutive items meet at most
+// ceil((nseg-1)/L) + 1 of them; with fewer items than warps every range holds
+// at most one item.
 int pipe_kmax(long long T, long long W, int nseg) {
     if (T <= 0) return 1;
     if (T < W) return nseg;
@@ -413,17 +679,26 @@ bool pipe_supported(const DevWeight &w) {
     if (w.dtype != DTYPE_Q8_0 && w.dtype != DTYPE_Q4_0 && w.dtype != DTYPE_TQ2_0 && w.dtype != DTYPE_F32 &&
         w.dtype != DTYPE_BF16)
         return false;
-    return pipe_smem(w.dtype, w.kchunks, chunk_weights(w.dtype)) <= 227 * 1024;
+    return pipe_smem(w.dtype, w.nb, w.kchunks) <= 227 * 1024;
 }
 
-// Batch-1 product y[r] = W[r,:] . x with the pipelined kernel.  part / cnt:
-// scratch of at least ntiles*kmax*32 floats and ntiles zeroed ints (see
-// pipe_scratch_floats); err: device-visible error word.
+// Scratch in float units: partials [ntiles][kmax][32] (two floats per entry
+// for the int64 ternary sums), counters [ntiles].
+void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints) {
+    const int nseg = item_nseg(w);
+    const long long T = (long long)w.ntiles * nseg;
+    const long long W = (long long)sm_count(ctx->device) * kPipeWarps;
+    *part_floats = (size_t)w.ntiles * pipe_kmax(T, W, nseg) * 32 * (w.dtype == DTYPE_TQ2_0 ? 2 : 1);
+    *cnt_ints = (size_t)w.ntiles;
+}
+
+// Batch-1 product y[r] = W[r,:] . x with the pipelined kernel.  part / cnt /
+// err: scratch sized by pipe_scratch_size (counters zero), error word.
 int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
                      int *err, cudaStream_t st) {
     if (w.ntiles == 0) return 0;
     PipeParams p;
-    p.codes = w.codes;
+    p.codes = reinterpret_cast<const uint8_t *>(w.codes);
     p.scales = w.scales;
     p.x = x;
     p.y = y;
@@ -435,12 +710,12 @@ int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, 
     p.nb = w.nb;
     p.ntiles = w.ntiles;
     p.kchunks = w.kchunks;
-    p.nseg = (w.kchunks + kSeg - 1) / kSeg;
+    p.nseg = item_nseg(w);
     p.total_items = (long long)w.ntiles * p.nseg;
     const int grid = sm_count(ctx->device);
     p.total_warps = grid * kPipeWarps;
     p.kmax = pipe_kmax(p.total_items, p.total_warps, p.nseg);
-    const size_t smem = pipe_smem(w.dtype, w.kchunks, chunk_weights(w.dtype));
+    const size_t smem = pipe_smem(w.dtype, w.nb, w.kchunks);
     auto launch = [&](auto kernel) -> int {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) {
@@ -465,13 +740,4 @@ int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, 
             ctx_fail(ctx, "launch_gemv_pipe", "unsupported dtype");
             return -1;
     }
-}
-
-// Scratch the pipelined kernel needs for a weight on this device.
-void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints) {
-    const int nseg = (w.kchunks + kSeg - 1) / kSeg;
-    const long long T = (long long)w.ntiles * nseg;
-    const long long W = (long long)sm_count(ctx->device) * kPipeWarps;
-    *part_floats = (size_t)w.ntiles * pipe_kmax(T, W, nseg) * 32;
-    *cnt_ints = (size_t)w.ntiles;
 }

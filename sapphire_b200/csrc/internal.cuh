@@ -166,6 +166,9 @@ int pipe_kmax(long long T, long long W, int nseg);
 // Batch-1 product through the pipelined kernel when it applies, else the
 // tile kernel; checks nothing on the host (asynchronous).
 int launch_gemv_best(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t stream);
+// Y[b*y_stride + r] for b < batch with whichever kernel serves the format.
+int launch_product(kernel_context_t *ctx, const DevWeight &w, const float *x, int x_stride, float *y, int y_stride,
+                   int batch, cudaStream_t stream);
 // Reads and clears the error word after a synchronisation; -1 if a kernel
 // reported a failed wait.
 int check_kernel_error(kernel_context_t *ctx, const char *who);

@@ -1,10 +1,24 @@
-// repack.cu - host block layout -> GEMV tile layout (see internal.cuh).
+// repack.cu - host block layout -> device layout (see internal.cuh).
 //
 // Input rows are the reference's packed formats, rows back to back
 // (row r starts at r * row_bytes, src/kernels/pool.c:297-301):
 //   Q4_0 20-byte and Q8_0 36-byte blocks (include/kernels.h:28-38), TQ2_0 rows
 //   (fp32 scale + 8-byte trit blocks), dense F32 / BF16 rows.
 // The repack only moves bytes: codes and scales keep their exact bits.
+//
+// Quantized formats go to the fragment layout: for each 32-row tile and
+// 32-column block, the bytes a warp lane (g = lane/4, tig = lane%4) feeds to
+// mma.sync m16n8k32 as its A operand are stored contiguously per lane:
+//   Q8_0 : per half h (rows 16h+g, 16h+g+8) a uint4 {r0 bytes 4tig..+3,
+//          r1 bytes 4tig..+3, r0 bytes 16+4tig..+3, r1 bytes 16+4tig..+3};
+//          1024 bytes per (tile, block), half-major then lane.
+//   Q4_0 : a uint4 of code word tig (bytes 4tig..4tig+3, i.e. elements
+//          8tig..8tig+7) of rows g, g+8, g+16, g+24; 512 bytes per (tile, block).
+//   TQ2_0: a uint2 of four 16-bit values, rows g, g+8, g+16, g+24, each
+//          (block byte tig) | (block byte 4+tig) << 8; 256 bytes per (tile, block).
+// Scales: per (tile, block) (Q8_0 / Q4_0) or per tile (TQ2_0), 32 floats in
+// the order g*4 + i -> row g + 8i.  Rows past the tensor are zero codes
+// (TQ2_0: code 1, trit 0) with zero scales.
 #include "internal.cuh"
 
 namespace {
@@ -15,29 +29,43 @@ __device__ __forceinline__ uint32_t ld_u32(const uint8_t *p, bool aligned) {
     return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
 }
 
-// One thread per (tile, block, lane).  Q8_0: two output chunks per block.
+// Scale slot q (0..31) of a tile holds row (q / 4) + 8 * (q % 4).
+__device__ __forceinline__ int scale_row(int q) { return (q >> 2) + 8 * (q & 3); }
+
+// Q8_0: one thread per (tile, block, half, lane).
 __global__ void repack_q8_0(const uint8_t *__restrict__ src, int nrows, int nb, int tile0, int ntile_in,
                             uint4 *__restrict__ codes, float *__restrict__ scales, bool aligned) {
-    const size_t n = (size_t)ntile_in * nb * 32;
+    const size_t n = (size_t)ntile_in * nb * 64;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int lane = (int)(i & 31);
-        const size_t tb = i >> 5;                  // tile_local * nb + b
+        const int h = (int)((i >> 5) & 1);
+        const size_t tb = i >> 6;                  // tile_local * nb + b
         const int b = (int)(tb % nb);
         const int tl = (int)(tb / nb);
-        const int r = tl * 32 + lane;              // row within this upload chunk
-        uint32_t w[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
-        if (r < nrows) {
-            const uint8_t *p = src + ((size_t)r * nb + b) * 36;
-#pragma unroll
-            for (int k = 0; k < 9; ++k) w[k] = ld_u32(p + 4 * k, aligned);
+        const int g = lane >> 2, tig = lane & 3;
+        const int r0 = tl * 32 + 16 * h + g, r1 = r0 + 8;
+        uint32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+        if (r0 < nrows) {
+            const uint8_t *p = src + ((size_t)r0 * nb + b) * 36 + 4;
+            a0 = ld_u32(p + 4 * tig, aligned);
+            a2 = ld_u32(p + 16 + 4 * tig, aligned);
+        }
+        if (r1 < nrows) {
+            const uint8_t *p = src + ((size_t)r1 * nb + b) * 36 + 4;
+            a1 = ld_u32(p + 4 * tig, aligned);
+            a3 = ld_u32(p + 16 + 4 * tig, aligned);
         }
         const size_t tile = (size_t)tile0 + tl;
-        codes[(tile * 2 * nb + 2 * b + 0) * 32 + lane] = make_uint4(w[1], w[2], w[3], w[4]);
-        codes[(tile * 2 * nb + 2 * b + 1) * 32 + lane] = make_uint4(w[5], w[6], w[7], w[8]);
-        scales[(tile * nb + b) * 32 + lane] = __uint_as_float(w[0]);
+        codes[((tile * nb + b) * 2 + h) * 32 + lane] = make_uint4(a0, a1, a2, a3);
+        if (h == 0) {
+            const int r = tl * 32 + scale_row(lane);
+            scales[(tile * nb + b) * 32 + lane] =
+                r < nrows ? __uint_as_float(ld_u32(src + ((size_t)r * nb + b) * 36, aligned)) : 0.0f;
+        }
     }
 }
 
+// Q4_0: one thread per (tile, block, lane).
 __global__ void repack_q4_0(const uint8_t *__restrict__ src, int nrows, int nb, int tile0, int ntile_in,
                             uint4 *__restrict__ codes, float *__restrict__ scales, bool aligned) {
     const size_t n = (size_t)ntile_in * nb * 32;
@@ -46,52 +74,54 @@ __global__ void repack_q4_0(const uint8_t *__restrict__ src, int nrows, int nb, 
         const size_t tb = i >> 5;
         const int b = (int)(tb % nb);
         const int tl = (int)(tb / nb);
-        const int r = tl * 32 + lane;
-        uint32_t w[5] = {0, 0, 0, 0, 0};
-        if (r < nrows) {
-            const uint8_t *p = src + ((size_t)r * nb + b) * 20;
+        const int g = lane >> 2, tig = lane & 3;
+        uint32_t w[4];
 #pragma unroll
-            for (int k = 0; k < 5; ++k) w[k] = ld_u32(p + 4 * k, aligned);
+        for (int k = 0; k < 4; ++k) {
+            const int r = tl * 32 + g + 8 * k;
+            w[k] = r < nrows ? ld_u32(src + ((size_t)r * nb + b) * 20 + 4 + 4 * tig, aligned) : 0u;
         }
         const size_t tile = (size_t)tile0 + tl;
-        codes[(tile * nb + b) * 32 + lane] = make_uint4(w[1], w[2], w[3], w[4]);
-        scales[(tile * nb + b) * 32 + lane] = __uint_as_float(w[0]);
+        codes[(tile * nb + b) * 32 + lane] = make_uint4(w[0], w[1], w[2], w[3]);
+        const int r = tl * 32 + scale_row(lane);
+        scales[(tile * nb + b) * 32 + lane] =
+            r < nrows ? __uint_as_float(ld_u32(src + ((size_t)r * nb + b) * 20, aligned)) : 0.0f;
     }
 }
 
-// TQ2_0 row: 4-byte scale then nb 8-byte blocks; one output chunk = 2 blocks.
+// TQ2_0 row: 4-byte scale then nb 8-byte blocks.  One thread per (tile, block, lane).
 __global__ void repack_tq2_0(const uint8_t *__restrict__ src, int nrows, int nb, int kchunks, int tile0,
-                             int ntile_in, uint4 *__restrict__ codes, float *__restrict__ scales, bool aligned) {
+                             int ntile_in, uint2 *__restrict__ codes, float *__restrict__ scales, bool aligned) {
     const size_t row_bytes = 4 + (size_t)8 * nb;
-    const size_t n = (size_t)ntile_in * kchunks * 32;
+    const size_t n = (size_t)ntile_in * nb * 32;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int lane = (int)(i & 31);
-        const size_t tk = i >> 5;
-        const int kc = (int)(tk % kchunks);
-        const int tl = (int)(tk / kchunks);
-        const int r = tl * 32 + lane;
-        // Padding trits decode to 0 (code 1) so padded columns stay inert even
-        // if the staged activation were not zero there.
-        uint32_t w[4] = {0x55555555u, 0x55555555u, 0x55555555u, 0x55555555u};
-        uint32_t s = 0;
-        if (r < nrows) {
-            const uint8_t *p = src + (size_t)r * row_bytes;
-            if (kc == 0) s = ld_u32(p, aligned);
-            const uint8_t *q = p + 4 + (size_t)16 * kc;
-            w[0] = ld_u32(q, aligned);
-            w[1] = ld_u32(q + 4, aligned);
-            if (2 * kc + 1 < nb) {
-                w[2] = ld_u32(q + 8, aligned);
-                w[3] = ld_u32(q + 12, aligned);
+        const size_t tb = i >> 5;
+        const int b = (int)(tb % nb);
+        const int tl = (int)(tb / nb);
+        const int g = lane >> 2, tig = lane & 3;
+        uint32_t u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int r = tl * 32 + g + 8 * k;
+            if (r < nrows) {
+                const uint8_t *blk = src + (size_t)r * row_bytes + 4 + (size_t)8 * b;
+                u[k] = (uint32_t)blk[tig] | ((uint32_t)blk[4 + tig] << 8);
+            } else {
+                u[k] = 0x5555u;                    // trits 0
             }
         }
         const size_t tile = (size_t)tile0 + tl;
-        codes[(tile * kchunks + kc) * 32 + lane] = make_uint4(w[0], w[1], w[2], w[3]);
-        if (kc == 0) scales[tile * 32 + lane] = __uint_as_float(s);
+        // A tile spans kchunks * 512 bytes = kchunks * 64 uint2.
+        codes[tile * (size_t)kchunks * 64 + (size_t)b * 32 + lane] = make_uint2(u[0] | (u[1] << 16), u[2] | (u[3] << 16));
+        if (b == 0) {
+            const int r = tl * 32 + scale_row(lane);
+            scales[tile * 32 + lane] = r < nrows ? __uint_as_float(ld_u32(src + (size_t)r * row_bytes, aligned)) : 0.0f;
+        }
     }
 }
 
-// Dense rows: W elements of `esize` bytes per 16-byte chunk.
+// Dense rows (tile layout): W elements of `esize` bytes per 16-byte chunk.
 __global__ void repack_dense(const uint8_t *__restrict__ src, int nrows, int cols, int esize, int kchunks,
                              int tile0, int ntile_in, uint4 *__restrict__ codes) {
     const int per = 16 / esize;
@@ -140,7 +170,7 @@ int launch_repack(kernel_context_t *ctx, const DevWeight &w, const void *src, in
     const bool aligned = ((uintptr_t)src & 3) == 0;
     switch (w.dtype) {
         case DTYPE_Q8_0: {
-            size_t n = (size_t)ntile_in * w.nb * 32;
+            size_t n = (size_t)ntile_in * w.nb * 64;
             repack_q8_0<<<grid_for(n), 256, 0, st>>>(s, nrows, w.nb, tile0, ntile_in, w.codes, w.scales, aligned);
             break;
         }
@@ -150,9 +180,9 @@ int launch_repack(kernel_context_t *ctx, const DevWeight &w, const void *src, in
             break;
         }
         case DTYPE_TQ2_0: {
-            size_t n = (size_t)ntile_in * w.kchunks * 32;
-            repack_tq2_0<<<grid_for(n), 256, 0, st>>>(s, nrows, w.nb, w.kchunks, tile0, ntile_in, w.codes,
-                                                      w.scales, aligned);
+            size_t n = (size_t)ntile_in * w.nb * 32;
+            repack_tq2_0<<<grid_for(n), 256, 0, st>>>(s, nrows, w.nb, w.kchunks, tile0, ntile_in,
+                                                      reinterpret_cast<uint2 *>(w.codes), w.scales, aligned);
             break;
         }
         case DTYPE_F32:
