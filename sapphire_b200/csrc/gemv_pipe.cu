@@ -9,11 +9,13 @@
 // takes a contiguous, equal-size range of them, so every SM streams the same
 // number of bytes whatever the matrix shape.
 //
-// Memory pipeline.  Each warp owns a ring of kStages shared-memory slots.  Lane
-// 0 fills a slot with one `cp.async.bulk` of the item's codes (4 KB) and one of
-// its scales, completing on the slot's mbarrier (expect_tx); the warp waits on
-// the mbarrier, computes from shared memory and refills the slot with the item
-// kStages ahead, so kStages items per warp are always in flight.
+// Memory pipeline.  Each warp owns a ring of NS shared-memory slots.  Lane 0
+// fills a slot with one `cp.async.bulk` of the item's codes and one of its
+// scales, completing on the slot's mbarrier (expect_tx).  The warp waits on
+// the mbarrier, copies the item into registers, refills the slot with the
+// item NS ahead at once, and only then computes - so all NS slots of every
+// warp stay in flight while it computes.  (On B200 a read stream needs about
+// 150 KB in flight per SM to reach full HBM bandwidth.)
 //
 // Dot products of the quantized formats run on the integer tensor cores
 // (mma.sync m16n8k32, s8 x s8 -> s32): x is split per 32-column block into
@@ -42,10 +44,14 @@
 
 namespace {
 
-constexpr int kPipeWarps = 8;
-constexpr int kPipeThreads = kPipeWarps * 32;
-constexpr int kStages = 4;
-constexpr int kUnitsPerItem = 8;              // dense: 8 x 512 B of codes per item
+// Warps per CTA (NW) and ring slots per warp (NS) are template parameters;
+// the host uses kPipeConfigs[0] (SAPPHIRE_PIPE_CFG selects another one for
+// tuning runs).
+struct PipeCfg {
+    int nw, ns;
+};
+constexpr PipeCfg kPipeConfigs[] = {{12, 3}, {8, 4}, {16, 2}};
+constexpr int kMaxPipeWarps = 16;
 constexpr unsigned kWaitLimit = 1u << 26;
 constexpr int kDigitBytesPerBlock = 96;       // 3 digit rows x 4 lanes x 8 bytes
 
@@ -112,21 +118,23 @@ __device__ __forceinline__ T lds(const uint8_t *p) {
 }
 
 // ------------------------------------------------------------ formats -----
-// Per-format geometry of an item in the device layout (internal.cuh).
+// Per-format geometry of an item in the device layout (internal.cuh):
+// kCodeBpb code bytes per (tile, block), kBpi blocks per item; the dense
+// formats use kBpi units of 512 bytes (one 16-byte chunk of 32 rows).
 template <tensor_dtype_t DT>
 struct Geo;
 template <>
 struct Geo<DTYPE_Q8_0> {
     static constexpr bool kMma = true;
-    static constexpr int kCodeBpb = 1024;     // code bytes per (tile, block)
-    static constexpr int kBpi = 4;            // blocks per item
+    static constexpr int kCodeBpb = 1024;
+    static constexpr int kBpi = 4;
     static constexpr int kScaleBytes = kBpi * 128;
 };
 template <>
 struct Geo<DTYPE_Q4_0> {
     static constexpr bool kMma = true;
     static constexpr int kCodeBpb = 512;
-    static constexpr int kBpi = 8;
+    static constexpr int kBpi = 4;
     static constexpr int kScaleBytes = kBpi * 128;
 };
 template <>
@@ -137,23 +145,27 @@ struct Geo<DTYPE_TQ2_0> {
     static constexpr int kScaleBytes = 0;     // row scale, read at the end of a tile
 };
 template <>
-struct Geo<DTYPE_F32> {                     // dense: items are 8 x 512-byte units
+struct Geo<DTYPE_F32> {
     static constexpr bool kMma = false;
     static constexpr int kCodeBpb = 512;
-    static constexpr int kBpi = 1;
+    static constexpr int kBpi = 8;
     static constexpr int kScaleBytes = 0;
 };
 template <>
 struct Geo<DTYPE_BF16> {
     static constexpr bool kMma = false;
     static constexpr int kCodeBpb = 512;
-    static constexpr int kBpi = 1;
+    static constexpr int kBpi = 8;
     static constexpr int kScaleBytes = 0;
 };
 
 template <tensor_dtype_t DT>
+__host__ __device__ constexpr int code_bytes() {
+    return Geo<DT>::kBpi * Geo<DT>::kCodeBpb;
+}
+template <tensor_dtype_t DT>
 __host__ __device__ constexpr int stage_bytes() {
-    return 4096 + Geo<DT>::kScaleBytes;
+    return code_bytes<DT>() + Geo<DT>::kScaleBytes;
 }
 
 struct PipeParams {
@@ -189,17 +201,29 @@ struct XPrep {
     int *nonfinite;
 };
 
-__device__ __forceinline__ size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+__host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
 
-__host__ __device__ inline size_t xprep_bytes_h(int nb, bool q4) {
-    size_t b = (size_t)nb * kDigitBytesPerBlock + 16;
-    b = (b + 15) & ~(size_t)15;
-    b += ((size_t)nb * 4 + 15) & ~(size_t)15;
+__host__ __device__ inline size_t xprep_bytes(int nb, bool q4) {
+    size_t b = align16((size_t)nb * kDigitBytesPerBlock + 16);
+    b += align16((size_t)nb * 4);
     if (q4) b += (size_t)nb * 32;
     return b + 16;
 }
 
-// Balanced base-256 digits of an integer |X| < 2^22: X = d0 + 256 d1 + 65536 d2.
+// Dense formats stage x as fp32, zero-padded to whole items of 8 chunks so a
+// tail item's zero chunks meet zeros.
+__host__ __device__ inline int dense_xpad(tensor_dtype_t dt, int kchunks) {
+    return ((kchunks + 7) / 8) * 8 * (dt == DTYPE_F32 ? 4 : 8);
+}
+
+__host__ __device__ inline size_t ximage_bytes(tensor_dtype_t dt, int nb, int kchunks) {
+    size_t b;
+    if (dt == DTYPE_Q8_0 || dt == DTYPE_Q4_0 || dt == DTYPE_TQ2_0) b = xprep_bytes(nb, dt == DTYPE_Q4_0);
+    else b = (size_t)dense_xpad(dt, kchunks) * 4;
+    return (b + 127) & ~(size_t)127;
+}
+
+// Balanced base-256 digits of an integer |X| <= 2^22: X = d0 + 256 d1 + 65536 d2.
 __device__ __forceinline__ void digits3(int X, int &d0, int &d1, int &d2) {
     d0 = ((X & 0xFF) ^ 0x80) - 0x80;
     const int X1 = (X - d0) >> 8;
@@ -231,189 +255,311 @@ __device__ __forceinline__ int digit_slot(int p) {
     }
 }
 
-template <tensor_dtype_t DT>
+template <tensor_dtype_t DT, int NW>
 __device__ void prepare_x(const PipeParams &p, XPrep xp) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __shared__ float s_red[kPipeWarps];
+    __shared__ float s_red[kMaxPipeWarps];
     int gexp = 0;
     if (DT == DTYPE_TQ2_0) {
-        // One exponent for the whole row (the ternary sum runs over all of K in int32).
+        // One exponent for the whole row (the ternary sum runs over all of K
+        // in int32).  Loads are unrolled so each thread has 8 in flight.
         float m = 0.0f;
-        for (int i = threadIdx.x; i < p.cols; i += blockDim.x) m = fmaxf(m, fabsf(p.x[i]));
         bool bad = false;
-        for (int i = threadIdx.x; i < p.cols; i += blockDim.x) bad |= !isfinite(p.x[i]);
+#pragma unroll 8
+        for (int i = threadIdx.x; i < p.cols; i += blockDim.x) {
+            const float v = __ldg(p.x + i);
+            bad |= !isfinite(v);
+            m = fmaxf(m, fabsf(v));
+        }
         if (bad) *xp.nonfinite = 1;
         for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (lane == 0) s_red[warp] = m;
         __syncthreads();
         m = 0.0f;
-        for (int i = 0; i < kPipeWarps; ++i) m = fmaxf(m, s_red[i]);
+        for (int i = 0; i < NW; ++i) m = fmaxf(m, s_red[i]);
         gexp = block_exponent(isfinite(m) ? m : FLT_MAX);
         if (threadIdx.x == 0) xp.pexp[0] = ldexpf(1.0f, -gexp);
     }
-    for (int b = warp; b < p.nb; b += kPipeWarps) {
-        const int c = b * 32 + lane;
-        const float v = c < p.cols ? p.x[c] : 0.0f;
-        int e = gexp;
-        if (DT != DTYPE_TQ2_0) {
-            if (!isfinite(v)) *xp.nonfinite = 1;
-            float m = fabsf(v);
-            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            e = block_exponent(isfinite(m) ? m : FLT_MAX);
-            if (lane == 0) xp.pexp[b] = ldexpf(1.0f, -e);
+    // Blocks b = warp + NW*u: the loads of kGroup blocks are issued together,
+    // then each block is converted.
+    constexpr int kGroup = 8;
+    for (int b0 = warp; b0 < p.nb; b0 += NW * kGroup) {
+        float vg[kGroup];
+#pragma unroll
+        for (int u = 0; u < kGroup; ++u) {
+            const int c = (b0 + u * NW) * 32 + lane;
+            vg[u] = (b0 + u * NW < p.nb && c < p.cols) ? __ldg(p.x + c) : 0.0f;
         }
-        const int X = isfinite(v) ? __float2int_rn(ldexpf(v, e)) : 0;
-        int d0, d1, d2;
-        digits3(X, d0, d1, d2);
-        uint8_t *row = xp.digits + (size_t)b * kDigitBytesPerBlock;
-        const int off = digit_slot<DT>(lane);
-        row[0 * 32 + off] = (uint8_t)(int8_t)d0;
-        row[1 * 32 + off] = (uint8_t)(int8_t)d1;
-        row[2 * 32 + off] = (uint8_t)(int8_t)d2;
-        if (DT == DTYPE_Q4_0) {
-            int s0 = d0, s1 = d1, s2 = d2;
-            for (int o = 16; o; o >>= 1) {
-                s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-                s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-                s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+#pragma unroll
+        for (int u = 0; u < kGroup; ++u) {
+            const int b = b0 + u * NW;
+            if (b >= p.nb) break;
+            const float v = vg[u];
+            int e = gexp;
+            if (DT != DTYPE_TQ2_0) {
+                if (!isfinite(v)) *xp.nonfinite = 1;
+                float m = fabsf(v);
+                for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                e = block_exponent(isfinite(m) ? m : FLT_MAX);
+                if (lane == 0) xp.pexp[b] = ldexpf(1.0f, -e);
             }
-            if (lane < 8) {
-                // corr[b][tig][j] for digit row 2*tig + j (rows 3..7 are zero)
-                const int r = lane;       // lane = 2*tig + j
-                xp.corr[b * 8 + lane] = r == 0 ? -8 * s0 : r == 1 ? -8 * s1 : r == 2 ? -8 * s2 : 0;
+            const int X = isfinite(v) ? __float2int_rn(ldexpf(v, e)) : 0;
+            int d0, d1, d2;
+            digits3(X, d0, d1, d2);
+            uint8_t *row = xp.digits + (size_t)b * kDigitBytesPerBlock;
+            const int off = digit_slot<DT>(lane);
+            row[0 * 32 + off] = (uint8_t)(int8_t)d0;
+            row[1 * 32 + off] = (uint8_t)(int8_t)d1;
+            row[2 * 32 + off] = (uint8_t)(int8_t)d2;
+            if (DT == DTYPE_Q4_0) {
+                int s0 = d0, s1 = d1, s2 = d2;
+                for (int o = 16; o; o >>= 1) {
+                    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+                    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+                    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+                }
+                // corr[b][tig][j] for digit row lane = 2*tig + j (rows 3..7 are zero)
+                if (lane < 8) xp.corr[b * 8 + lane] = lane == 0 ? -8 * s0 : lane == 1 ? -8 * s1 : lane == 2 ? -8 * s2 : 0;
             }
         }
     }
     if (threadIdx.x < 4) reinterpret_cast<uint32_t *>(xp.digits + (size_t)p.nb * kDigitBytesPerBlock)[threadIdx.x] = 0;
 }
 
-// --------------------------------------------------------- MMA consumers --
+// ----------------------------------------------------------- item in regs --
+// The part of a staged item one lane needs, copied out of shared memory so
+// the slot can be refilled before the compute.  Blocks past the end of a row
+// are zero codes with zero scales (TQ2_0: code 1, trit 0).
+template <tensor_dtype_t DT>
+struct ItemRegs;
+template <>
+struct ItemRegs<DTYPE_Q8_0> {
+    uint4 a[4][2];
+    float4 s[4];
+    __device__ __forceinline__ void load(const uint8_t *st, int nblk, int lane) {
+        const int g = lane >> 2;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const bool ok = u < nblk;
+            a[u][0] = ok ? lds<uint4>(st + u * 1024 + lane * 16) : make_uint4(0, 0, 0, 0);
+            a[u][1] = ok ? lds<uint4>(st + u * 1024 + 512 + lane * 16) : make_uint4(0, 0, 0, 0);
+            s[u] = ok ? lds<float4>(st + code_bytes<DTYPE_Q8_0>() + u * 128 + g * 16) : make_float4(0, 0, 0, 0);
+        }
+    }
+};
+template <>
+struct ItemRegs<DTYPE_Q4_0> {
+    uint4 a[4];
+    float4 s[4];
+    __device__ __forceinline__ void load(const uint8_t *st, int nblk, int lane) {
+        const int g = lane >> 2;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const bool ok = u < nblk;
+            a[u] = ok ? lds<uint4>(st + u * 512 + lane * 16) : make_uint4(0, 0, 0, 0);
+            s[u] = ok ? lds<float4>(st + code_bytes<DTYPE_Q4_0>() + u * 128 + g * 16) : make_float4(0, 0, 0, 0);
+        }
+    }
+};
+template <>
+struct ItemRegs<DTYPE_TQ2_0> {
+    uint2 a[16];
+    __device__ __forceinline__ void load(const uint8_t *st, int nblk, int lane) {
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+            a[u] = u < nblk ? lds<uint2>(st + u * 256 + lane * 8) : make_uint2(0x55555555u, 0x55555555u);
+    }
+};
+struct DenseRegs {
+    uint4 c[8];
+    __device__ __forceinline__ void load(const uint8_t *st, int nch, int lane) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) c[u] = u < nch ? lds<uint4>(st + u * 512 + lane * 16) : make_uint4(0, 0, 0, 0);
+    }
+};
+template <>
+struct ItemRegs<DTYPE_F32> : DenseRegs {};
+template <>
+struct ItemRegs<DTYPE_BF16> : DenseRegs {};
+
+// ------------------------------------------------------------ consumers ---
 // Accumulator state of one 32-row tile for a lane (g = lane/4, tig = lane%4).
 struct MmaAcc {
     float f[2][4];      // Q8_0 / Q4_0: scaled partial sums per (half, D register)
-    int d[2][4];        // TQ2_0: exact int32 sums
+    int d[2][2][4];     // TQ2_0: exact int32 sums, two independent sets (set, half, reg)
+    float dense;        // F32 / BF16: this lane's row
     __device__ __forceinline__ void reset() {
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 f[h][i] = 0.0f;
-                d[h][i] = 0;
+                d[0][h][i] = 0;
+                d[1][h][i] = 0;
             }
+        dense = 0.0f;
     }
 };
 
+// B fragment of block b (clamped to the last block; rows past the end of x
+// have zero codes, so the clamped digits meet zeros).
 __device__ __forceinline__ uint2 load_b(const XPrep &xp, int nb, int b, int lane) {
     const int g = lane >> 2, tig = lane & 3;
+    b = b < nb ? b : nb - 1;
     const size_t off = g < 3 ? (size_t)b * kDigitBytesPerBlock + g * 32 + tig * 8 : (size_t)nb * kDigitBytesPerBlock;
     return lds<uint2>(xp.digits + off);
 }
 
-template <tensor_dtype_t DT>
-__device__ __forceinline__ void consume_mma(const uint8_t *st, int nblk, int blk0, int nb, int lane, const XPrep &xp,
-                                            MmaAcc &acc) {
-    using G = Geo<DT>;
-    const int g = lane >> 2, tig = lane & 3;
+// Scaled epilogue of one block's two D tiles (rows g, g+8 | g+16, g+24).
+__device__ __forceinline__ void scale_acc(MmaAcc &acc, const int (&D0)[4], const int (&D1)[4], float4 S, float pe) {
+    const float s0 = S.x * pe, s1 = S.y * pe, s2 = S.z * pe, s3 = S.w * pe;
+    acc.f[0][0] = fmaf(s0, (float)D0[0], acc.f[0][0]);
+    acc.f[0][1] = fmaf(s0, (float)D0[1], acc.f[0][1]);
+    acc.f[0][2] = fmaf(s1, (float)D0[2], acc.f[0][2]);
+    acc.f[0][3] = fmaf(s1, (float)D0[3], acc.f[0][3]);
+    acc.f[1][0] = fmaf(s2, (float)D1[0], acc.f[1][0]);
+    acc.f[1][1] = fmaf(s2, (float)D1[1], acc.f[1][1]);
+    acc.f[1][2] = fmaf(s3, (float)D1[2], acc.f[1][2]);
+    acc.f[1][3] = fmaf(s3, (float)D1[3], acc.f[1][3]);
+}
+
+__device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_Q8_0> &R, int blk0, int nb, int lane,
+                                             const XPrep &xp, const float *, MmaAcc &acc) {
 #pragma unroll
-    for (int bi = 0; bi < G::kBpi; ++bi) {
-        if (bi >= nblk) break;
-        const int b = blk0 + bi;
-        const uint2 B = load_b(xp, nb, b, lane);
-        if (DT == DTYPE_TQ2_0) {
-            const uint2 A = lds<uint2>(st + bi * G::kCodeBpb + lane * 8);
-            const uint32_t tbl = 0x020100FFu;   // code c -> c - 1
+    for (int u0 = 0; u0 < 4; u0 += 2) {
+        uint2 B[2];
+        float pe[2];
+        int D[2][2][4];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            B[u] = load_b(xp, nb, blk0 + u0 + u, lane);
+            pe[u] = xp.pexp[min(blk0 + u0 + u, nb - 1)];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) D[u][0][i] = D[u][1][i] = 0;
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const uint4 a0 = R.a[u0 + u][0], a1 = R.a[u0 + u][1];
+            mma_s8s8(D[u][0], a0.x, a0.y, a0.z, a0.w, B[u].x, B[u].y);
+            mma_s8s8(D[u][1], a1.x, a1.y, a1.z, a1.w, B[u].x, B[u].y);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) scale_acc(acc, D[u][0], D[u][1], R.s[u0 + u], pe[u]);
+    }
+}
+
+__device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_Q4_0> &R, int blk0, int nb, int lane,
+                                             const XPrep &xp, const float *, MmaAcc &acc) {
+    const int tig = lane & 3;
+    uint2 B[4];
+    int2 C[4];
+    float pe[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int b = min(blk0 + u, nb - 1);
+        B[u] = load_b(xp, nb, b, lane);
+        C[u] = lds<int2>(reinterpret_cast<const uint8_t *>(xp.corr) + (size_t)b * 32 + tig * 8);
+        pe[u] = xp.pexp[b];
+    }
+    int D[4][2][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const uint4 A = R.a[u];
+        const uint32_t lo0 = A.x & 0x0F0F0F0Fu, hi0 = (A.x >> 4) & 0x0F0F0F0Fu;
+        const uint32_t lo1 = A.y & 0x0F0F0F0Fu, hi1 = (A.y >> 4) & 0x0F0F0F0Fu;
+        const uint32_t lo2 = A.z & 0x0F0F0F0Fu, hi2 = (A.z >> 4) & 0x0F0F0F0Fu;
+        const uint32_t lo3 = A.w & 0x0F0F0F0Fu, hi3 = (A.w >> 4) & 0x0F0F0F0Fu;
+        // Start from the -8 offset correction of the unsigned codes.
+        D[u][0][0] = D[u][0][2] = D[u][1][0] = D[u][1][2] = C[u].x;
+        D[u][0][1] = D[u][0][3] = D[u][1][1] = D[u][1][3] = C[u].y;
+        mma_u8s8(D[u][0], lo0, lo1, hi0, hi1, B[u].x, B[u].y);
+        mma_u8s8(D[u][1], lo2, lo3, hi2, hi3, B[u].x, B[u].y);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) scale_acc(acc, D[u][0], D[u][1], R.s[u], pe[u]);
+}
+
+__device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_TQ2_0> &R, int blk0, int nb, int lane,
+                                             const XPrep &xp, const float *, MmaAcc &acc) {
+    const uint32_t tbl = 0x020100FFu;   // code c -> c - 1
+#pragma unroll
+    for (int u0 = 0; u0 < 16; u0 += 4) {
+        uint2 B[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) B[u] = load_b(xp, nb, blk0 + u0 + u, lane);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint2 A = R.a[u0 + u];
             const uint32_t m0 = A.x & 0x33333333u, n0 = (A.x >> 2) & 0x33333333u;
             const uint32_t m1 = A.y & 0x33333333u, n1 = (A.y >> 2) & 0x33333333u;
-            mma_s8s8(acc.d[0], __byte_perm(tbl, 0, m0), __byte_perm(tbl, 0, m0 >> 16), __byte_perm(tbl, 0, n0),
-                     __byte_perm(tbl, 0, n0 >> 16), B.x, B.y);
-            mma_s8s8(acc.d[1], __byte_perm(tbl, 0, m1), __byte_perm(tbl, 0, m1 >> 16), __byte_perm(tbl, 0, n1),
-                     __byte_perm(tbl, 0, n1 >> 16), B.x, B.y);
-        } else {
-            int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0};
-            if (DT == DTYPE_Q8_0) {
-                const uint4 A0 = lds<uint4>(st + bi * G::kCodeBpb + lane * 16);
-                const uint4 A1 = lds<uint4>(st + bi * G::kCodeBpb + 512 + lane * 16);
-                mma_s8s8(d0, A0.x, A0.y, A0.z, A0.w, B.x, B.y);
-                mma_s8s8(d1, A1.x, A1.y, A1.z, A1.w, B.x, B.y);
-            } else {
-                const uint4 A = lds<uint4>(st + bi * G::kCodeBpb + lane * 16);
-                const uint32_t lo0 = A.x & 0x0F0F0F0Fu, hi0 = (A.x >> 4) & 0x0F0F0F0Fu;
-                const uint32_t lo1 = A.y & 0x0F0F0F0Fu, hi1 = (A.y >> 4) & 0x0F0F0F0Fu;
-                const uint32_t lo2 = A.z & 0x0F0F0F0Fu, hi2 = (A.z >> 4) & 0x0F0F0F0Fu;
-                const uint32_t lo3 = A.w & 0x0F0F0F0Fu, hi3 = (A.w >> 4) & 0x0F0F0F0Fu;
-                mma_u8s8(d0, lo0, lo1, hi0, hi1, B.x, B.y);
-                mma_u8s8(d1, lo2, lo3, hi2, hi3, B.x, B.y);
-                const int2 C = lds<int2>(reinterpret_cast<const uint8_t *>(xp.corr) + (size_t)b * 32 + tig * 8);
-                d0[0] += C.x; d0[2] += C.x; d1[0] += C.x; d1[2] += C.x;
-                d0[1] += C.y; d0[3] += C.y; d1[1] += C.y; d1[3] += C.y;
-            }
-            // Scales of rows g, g+8, g+16, g+24 for this block, times 2^-e_b.
-            const float4 S = lds<float4>(st + 4096 + bi * 128 + g * 16);
-            const float pe = xp.pexp[b];
-            const float s0 = S.x * pe, s1 = S.y * pe, s2 = S.z * pe, s3 = S.w * pe;
-            acc.f[0][0] = fmaf(s0, (float)d0[0], acc.f[0][0]);
-            acc.f[0][1] = fmaf(s0, (float)d0[1], acc.f[0][1]);
-            acc.f[0][2] = fmaf(s1, (float)d0[2], acc.f[0][2]);
-            acc.f[0][3] = fmaf(s1, (float)d0[3], acc.f[0][3]);
-            acc.f[1][0] = fmaf(s2, (float)d1[0], acc.f[1][0]);
-            acc.f[1][1] = fmaf(s2, (float)d1[1], acc.f[1][1]);
-            acc.f[1][2] = fmaf(s3, (float)d1[2], acc.f[1][2]);
-            acc.f[1][3] = fmaf(s3, (float)d1[3], acc.f[1][3]);
+            mma_s8s8(acc.d[u & 1][0], __byte_perm(tbl, 0, m0), __byte_perm(tbl, 0, m0 >> 16), __byte_perm(tbl, 0, n0),
+                     __byte_perm(tbl, 0, n0 >> 16), B[u].x, B[u].y);
+            mma_s8s8(acc.d[u & 1][1], __byte_perm(tbl, 0, m1), __byte_perm(tbl, 0, m1 >> 16), __byte_perm(tbl, 0, n1),
+                     __byte_perm(tbl, 0, n1 >> 16), B[u].x, B[u].y);
         }
     }
 }
 
-// Per-row results of a tile for lanes with tig == 0: rows g + 8*i, i = 0..3,
-// as 8-byte values (fp32 bits for Q8_0 / Q4_0, the exact int64 sum for
-// TQ2_0).  All lanes must call (shuffles).
+__device__ __forceinline__ float dense_f32(uint4 c, const float *xs) {
+    const float4 v = *reinterpret_cast<const float4 *>(xs);
+    float a = __uint_as_float(c.x) * v.x;
+    a = fmaf(__uint_as_float(c.y), v.y, a);
+    a = fmaf(__uint_as_float(c.z), v.z, a);
+    return fmaf(__uint_as_float(c.w), v.w, a);
+}
+__device__ __forceinline__ float dense_bf16(uint4 c, const float *xs) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
+    const float4 v0 = x4[0], v1 = x4[1];
+    float a0 = __uint_as_float(c.x << 16) * v0.x, a1 = __uint_as_float(c.x & 0xFFFF0000u) * v0.y;
+    a0 = fmaf(__uint_as_float(c.y << 16), v0.z, a0);
+    a1 = fmaf(__uint_as_float(c.y & 0xFFFF0000u), v0.w, a1);
+    a0 = fmaf(__uint_as_float(c.z << 16), v1.x, a0);
+    a1 = fmaf(__uint_as_float(c.z & 0xFFFF0000u), v1.y, a1);
+    a0 = fmaf(__uint_as_float(c.w << 16), v1.z, a0);
+    a1 = fmaf(__uint_as_float(c.w & 0xFFFF0000u), v1.w, a1);
+    return a0 + a1;
+}
+__device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_F32> &R, int c0, int, int, const XPrep &,
+                                             const float *xs, MmaAcc &acc) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc.dense += dense_f32(R.c[u], xs + (size_t)(c0 + u) * 4);
+}
+__device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_BF16> &R, int c0, int, int, const XPrep &,
+                                             const float *xs, MmaAcc &acc) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc.dense += dense_bf16(R.c[u], xs + (size_t)(c0 + u) * 8);
+}
+
+// Per-row results of a tile.  MMA formats: lanes with tig == 0 hold rows
+// g + 8*i (i = 0..3) as 8-byte values (fp32 bits for Q8_0 / Q4_0, the exact
+// int64 sum for TQ2_0); all lanes must call (shuffles).  Dense: row = lane.
 template <tensor_dtype_t DT>
-__device__ __forceinline__ void mma_rows(const MmaAcc &acc, unsigned long long (&v)[4]) {
+__device__ __forceinline__ void tile_rows(const MmaAcc &acc, unsigned long long (&v)[4]) {
+    if constexpr (!Geo<DT>::kMma) {
+        v[0] = __float_as_uint(acc.dense);
+        return;
+    } else {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         if (DT == DTYPE_TQ2_0) {
-            const int up0 = __shfl_down_sync(0xffffffffu, acc.d[h][0], 1);
-            const int up2 = __shfl_down_sync(0xffffffffu, acc.d[h][2], 1);
-            const long long r0 = (long long)acc.d[h][0] + 256LL * acc.d[h][1] + 65536LL * up0;
-            const long long r1 = (long long)acc.d[h][2] + 256LL * acc.d[h][3] + 65536LL * up2;
-            v[2 * h] = (unsigned long long)r0;
-            v[2 * h + 1] = (unsigned long long)r1;
+            int d[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) d[i] = acc.d[0][h][i] + acc.d[1][h][i];
+            const int up0 = __shfl_down_sync(0xffffffffu, d[0], 1);
+            const int up2 = __shfl_down_sync(0xffffffffu, d[2], 1);
+            v[2 * h] = (unsigned long long)((long long)d[0] + 256LL * d[1] + 65536LL * up0);
+            v[2 * h + 1] = (unsigned long long)((long long)d[2] + 256LL * d[3] + 65536LL * up2);
         } else {
             const float up0 = __shfl_down_sync(0xffffffffu, acc.f[h][0], 1);
             const float up2 = __shfl_down_sync(0xffffffffu, acc.f[h][2], 1);
-            const float r0 = (float)((double)acc.f[h][0] + 256.0 * acc.f[h][1] + 65536.0 * up0);
-            const float r1 = (float)((double)acc.f[h][2] + 256.0 * acc.f[h][3] + 65536.0 * up2);
-            v[2 * h] = __float_as_uint(r0);
-            v[2 * h + 1] = __float_as_uint(r1);
+            v[2 * h] = __float_as_uint((float)((double)acc.f[h][0] + 256.0 * acc.f[h][1] + 65536.0 * up0));
+            v[2 * h + 1] = __float_as_uint((float)((double)acc.f[h][2] + 256.0 * acc.f[h][3] + 65536.0 * up2));
         }
     }
-}
-
-// ------------------------------------------------------- dense consumer ---
-template <tensor_dtype_t DT>
-__device__ __forceinline__ float dense_chunk(uint4 c, const float *xs) {
-    const float4 *x4 = reinterpret_cast<const float4 *>(xs);
-    if (DT == DTYPE_F32) {
-        const float4 v = x4[0];
-        float a = __uint_as_float(c.x) * v.x;
-        a = fmaf(__uint_as_float(c.y), v.y, a);
-        a = fmaf(__uint_as_float(c.z), v.z, a);
-        return fmaf(__uint_as_float(c.w), v.w, a);
-    } else {
-        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-        const float4 v0 = x4[0], v1 = x4[1];
-        float a0 = __uint_as_float(w[0] << 16) * v0.x, a1 = __uint_as_float(w[0] & 0xFFFF0000u) * v0.y;
-        a0 = fmaf(__uint_as_float(w[1] << 16), v0.z, a0);
-        a1 = fmaf(__uint_as_float(w[1] & 0xFFFF0000u), v0.w, a1);
-        a0 = fmaf(__uint_as_float(w[2] << 16), v1.x, a0);
-        a1 = fmaf(__uint_as_float(w[2] & 0xFFFF0000u), v1.y, a1);
-        a0 = fmaf(__uint_as_float(w[3] << 16), v1.z, a0);
-        a1 = fmaf(__uint_as_float(w[3] & 0xFFFF0000u), v1.w, a1);
-        return a0 + a1;
     }
 }
 
 // ---------------------------------------------------------- tile output ---
-// Final fp32 value of one row from its 8-byte sum.
 template <tensor_dtype_t DT>
 __device__ __forceinline__ float finish_row(const PipeParams &p, const XPrep &xp, int tile, int r, unsigned long long v,
                                             bool nonfinite) {
@@ -427,8 +573,6 @@ __device__ __forceinline__ float finish_row(const PipeParams &p, const XPrep &xp
     return nonfinite ? __int_as_float(0x7FC00000) : out;
 }
 
-// Rows owned by this lane: MMA formats hold rows g + 8i (i = 0..3) on lanes
-// with tig == 0; dense formats hold row `lane` in v[0].
 template <tensor_dtype_t DT>
 __device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int lane, int my_warp, bool whole,
                            const unsigned long long (&v)[4], bool nonfinite) {
@@ -494,11 +638,9 @@ __device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int l
     }
 }
 
-__host__ __device__ size_t ximage_bytes(tensor_dtype_t dt, int nb, int kchunks);
-
 // --------------------------------------------------------------- kernel ---
-template <tensor_dtype_t DT>
-__global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe(const PipeParams p) {
+template <tensor_dtype_t DT, int NW, int NS>
+__global__ void __launch_bounds__(NW * 32, 1) gemv_pipe(const PipeParams p) {
     using G = Geo<DT>;
     constexpr int kStage = stage_bytes<DT>();
     extern __shared__ __align__(128) uint8_t smem[];
@@ -507,8 +649,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe(const PipeParams p)
 
     // Shared memory: [x image][rings][barriers]
     const size_t ximg = ximage_bytes(DT, p.nb, p.kchunks);
-    uint8_t *ring = smem + ximg + (size_t)warp * kStages * kStage;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ximg + (size_t)kPipeWarps * kStages * kStage) + warp * kStages;
+    uint8_t *ring = smem + ximg + (size_t)warp * NS * kStage;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + ximg + (size_t)NW * NS * kStage) + warp * NS;
     XPrep xp;
     xp.digits = smem;
     const size_t dig_bytes = align16((size_t)p.nb * kDigitBytesPerBlock + 16);
@@ -517,137 +659,142 @@ __global__ void __launch_bounds__(kPipeThreads, 1) gemv_pipe(const PipeParams p)
     xp.nonfinite = &s_nonfinite;
     float *xs = reinterpret_cast<float *>(smem);
 
-    const int gw = blockIdx.x * kPipeWarps + warp;
+    const int gw = blockIdx.x * NW + warp;
     const long long T = p.total_items, W = p.total_warps;
     const long long it0 = range_begin(gw, T, W), it1 = range_begin(gw + 1, T, W);
     const int n_items = (int)(it1 - it0);
+    const int units = G::kMma ? p.nb : p.kchunks;   // blocks (quantized) or 512-byte units (dense)
 
-    auto issue = [&](long long item, int stage) {
-        const int tile = (int)(item / p.nseg), seg = (int)(item % p.nseg);
-        uint8_t *dst = ring + (size_t)stage * kStage;
-        const uint8_t *src;
-        uint32_t bytes, sbytes = 0;
-        const float *ssrc = nullptr;
-        if (G::kMma) {
-            const int b0 = seg * Geo<DT>::kBpi;
-            const int nblk = min(Geo<DT>::kBpi, p.nb - b0);
-            src = p.codes + (size_t)tile * p.kchunks * 512 + (size_t)b0 * Geo<DT>::kCodeBpb;
-            bytes = (uint32_t)nblk * Geo<DT>::kCodeBpb;
-            if (G::kScaleBytes) {
-                ssrc = p.scales + ((size_t)tile * p.nb + b0) * 32;
-                sbytes = (uint32_t)nblk * 128;
-            }
-        } else {
-            const int c0 = seg * kUnitsPerItem;
-            const int nch = min(kUnitsPerItem, p.kchunks - c0);
-            src = p.codes + ((size_t)tile * p.kchunks + c0) * 512;
-            bytes = (uint32_t)nch * 512;
+    // (tile, segment) of the next item to copy, advanced without division.
+    const int tile0 = (int)(it0 / p.nseg), seg0 = (int)(it0 % p.nseg);
+    int q_tile = tile0, q_seg = seg0;
+    auto issue = [&](int stage) {
+        const int tile = q_tile, seg = q_seg;
+        if (++q_seg == p.nseg) {
+            q_seg = 0;
+            ++q_tile;
         }
+        const int u0 = seg * G::kBpi;
+        const int nu = min(G::kBpi, units - u0);
+        uint8_t *dst = ring + (size_t)stage * kStage;
+        const uint8_t *src = p.codes + (size_t)tile * p.kchunks * 512 + (size_t)u0 * G::kCodeBpb;
+        const uint32_t bytes = (uint32_t)nu * G::kCodeBpb;
+        const uint32_t sbytes = G::kScaleBytes ? (uint32_t)nu * 128 : 0;
         mbar_expect_tx(bars + stage, bytes + sbytes);
         bulk_g2s(dst, src, bytes, bars + stage);
-        if (sbytes) bulk_g2s(dst + 4096, ssrc, sbytes, bars + stage);
+        if (sbytes) bulk_g2s(dst + code_bytes<DT>(), p.scales + ((size_t)tile * p.nb + u0) * 32, sbytes, bars + stage);
     };
 
     if (threadIdx.x == 0) s_nonfinite = 0;
     if (lane == 0) {
-        for (int s = 0; s < kStages; ++s) mbar_init(bars + s, 1);
+        for (int s = 0; s < NS; ++s) mbar_init(bars + s, 1);
         fence_mbar_init();
     }
     __syncwarp();
     if (lane == 0)
-        for (int j = 0; j < kStages && j < n_items; ++j) issue(it0 + j, j);
+        for (int j = 0; j < NS && j < n_items; ++j) issue(j);
     __syncthreads();   // s_nonfinite initialised before x preparation writes it
 
     // x image, built once per CTA while the first copies are in flight.
     if (G::kMma) {
-        prepare_x<DT>(p, xp);
+        prepare_x<DT, NW>(p, xp);
     } else {
-        const int xpad = p.kchunks * (DT == DTYPE_F32 ? 4 : 8);
+        const int xpad = dense_xpad(DT, p.kchunks);
         for (int i = threadIdx.x; i < xpad; i += blockDim.x) xs[i] = (i < p.cols) ? p.x[i] : 0.0f;
     }
     __syncthreads();
     const bool nonfinite = G::kMma && s_nonfinite != 0;
 
-    int cur_tile = -1;
+    int cur_tile = -1, c_tile = tile0, c_seg = seg0;
     bool cur_whole = false;
-    MmaAcc macc;
-    macc.reset();
-    float dacc = 0.0f;
+    MmaAcc acc;
+    acc.reset();
     for (int j = 0; j < n_items; ++j) {
-        const long long item = it0 + j;
-        const int stage = j % kStages;
-        const uint32_t phase = (uint32_t)(j / kStages) & 1u;
+        const int stage = j % NS;
+        const uint32_t phase = (uint32_t)(j / NS) & 1u;
         if (!mbar_wait_bounded(bars + stage, phase)) {
             if (lane == 0) atomicOr(p.err, 1);
-            for (int q = j; q < n_items && q < j + kStages; ++q)
-                (void)mbar_wait_bounded(bars + (q % kStages), (uint32_t)(q / kStages) & 1u);
+            for (int q = j; q < n_items && q < j + NS; ++q)
+                (void)mbar_wait_bounded(bars + (q % NS), (uint32_t)(q / NS) & 1u);
             return;
         }
-        const int tile = (int)(item / p.nseg), seg = (int)(item % p.nseg);
+        const int tile = c_tile, seg = c_seg;
+        if (++c_seg == p.nseg) {
+            c_seg = 0;
+            ++c_tile;
+        }
+        // Item into registers, then refill the slot before computing.
+        const int u0 = seg * G::kBpi;
+        ItemRegs<DT> R;
+        R.load(ring + (size_t)stage * kStage, min(G::kBpi, units - u0), lane);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0 && j + NS < n_items) issue(stage);
+
         if (tile != cur_tile) {
             if (cur_tile >= 0) {
                 unsigned long long v[4] = {0, 0, 0, 0};
-                if (G::kMma) mma_rows<DT>(macc, v);
-                else v[0] = __float_as_uint(dacc);
+                tile_rows<DT>(acc, v);
                 flush_tile<DT>(p, xp, cur_tile, lane, gw, cur_whole, v, nonfinite);
             }
             cur_tile = tile;
-            macc.reset();
-            dacc = 0.0f;
+            acc.reset();
             cur_whole = (seg == 0) && ((long long)tile * p.nseg + p.nseg <= it1);
         }
-        const uint8_t *st = ring + (size_t)stage * kStage;
-        if (G::kMma) {
-            const int b0 = seg * Geo<DT>::kBpi;
-            consume_mma<DT>(st, min(Geo<DT>::kBpi, p.nb - b0), b0, p.nb, lane, xp, macc);
-        } else {
-            constexpr int kW = (DT == DTYPE_F32) ? 4 : 8;
-            const int c0 = seg * kUnitsPerItem;
-            const int nch = min(kUnitsPerItem, p.kchunks - c0);
-#pragma unroll
-            for (int ch = 0; ch < kUnitsPerItem; ++ch)
-                if (ch < nch) dacc += dense_chunk<DT>(lds<uint4>(st + (size_t)ch * 512 + lane * 16), xs + (size_t)(c0 + ch) * kW);
-        }
-        // Order this warp's reads of the slot before the asynchronous refill.
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0 && j + kStages < n_items) issue(item + kStages, stage);
+        compute_item(R, u0, p.nb, lane, xp, xs, acc);
     }
     if (cur_tile >= 0) {
         unsigned long long v[4] = {0, 0, 0, 0};
-        if (G::kMma) mma_rows<DT>(macc, v);
-        else v[0] = __float_as_uint(dacc);
+        tile_rows<DT>(acc, v);
         flush_tile<DT>(p, xp, cur_tile, lane, gw, cur_whole, v, nonfinite);
     }
 }
 
-__host__ __device__ size_t ximage_bytes(tensor_dtype_t dt, int nb, int kchunks) {
-    size_t b;
-    if (dt == DTYPE_Q8_0 || dt == DTYPE_Q4_0 || dt == DTYPE_TQ2_0) b = xprep_bytes_h(nb, dt == DTYPE_Q4_0);
-    else b = (size_t)kchunks * (dt == DTYPE_F32 ? 4 : 8) * 4;
-    return (b + 127) & ~(size_t)127;
-}
-
-size_t pipe_smem(tensor_dtype_t dt, int nb, int kchunks) {
-    int stage = 0;
+// ----------------------------------------------------------------- host ---
+int stage_of(tensor_dtype_t dt) {
     switch (dt) {
-        case DTYPE_Q8_0: stage = stage_bytes<DTYPE_Q8_0>(); break;
-        case DTYPE_Q4_0: stage = stage_bytes<DTYPE_Q4_0>(); break;
-        case DTYPE_TQ2_0: stage = stage_bytes<DTYPE_TQ2_0>(); break;
-        case DTYPE_F32: stage = stage_bytes<DTYPE_F32>(); break;
-        case DTYPE_BF16: stage = stage_bytes<DTYPE_BF16>(); break;
+        case DTYPE_Q8_0: return stage_bytes<DTYPE_Q8_0>();
+        case DTYPE_Q4_0: return stage_bytes<DTYPE_Q4_0>();
+        case DTYPE_TQ2_0: return stage_bytes<DTYPE_TQ2_0>();
+        case DTYPE_F32: return stage_bytes<DTYPE_F32>();
+        case DTYPE_BF16: return stage_bytes<DTYPE_BF16>();
         default: return 0;
     }
-    return ximage_bytes(dt, nb, kchunks) + (size_t)kPipeWarps * kStages * stage + (size_t)kPipeWarps * kStages * 8;
+}
+
+int bpi_of(tensor_dtype_t dt) {
+    switch (dt) {
+        case DTYPE_Q8_0: return Geo<DTYPE_Q8_0>::kBpi;
+        case DTYPE_Q4_0: return Geo<DTYPE_Q4_0>::kBpi;
+        case DTYPE_TQ2_0: return Geo<DTYPE_TQ2_0>::kBpi;
+        case DTYPE_F32: return Geo<DTYPE_F32>::kBpi;
+        case DTYPE_BF16: return Geo<DTYPE_BF16>::kBpi;
+        default: return 1;
+    }
+}
+
+size_t pipe_smem(tensor_dtype_t dt, int nb, int kchunks, PipeCfg c) {
+    const int stage = stage_of(dt);
+    if (!stage) return 0;
+    return ximage_bytes(dt, nb, kchunks) + (size_t)c.nw * c.ns * stage + (size_t)c.nw * c.ns * 8;
+}
+
+// The configuration this process uses: SAPPHIRE_PIPE_CFG = index into
+// kPipeConfigs (default 0).
+PipeCfg pipe_cfg() {
+    static const int idx = [] {
+        const char *v = getenv("SAPPHIRE_PIPE_CFG");
+        int i = v ? atoi(v) : 0;
+        const int n = (int)(sizeof(kPipeConfigs) / sizeof(kPipeConfigs[0]));
+        return (i >= 0 && i < n) ? i : 0;
+    }();
+    return kPipeConfigs[idx];
 }
 
 int item_nseg(const DevWeight &w) {
-    switch (w.dtype) {
-        case DTYPE_Q8_0: return (w.nb + Geo<DTYPE_Q8_0>::kBpi - 1) / Geo<DTYPE_Q8_0>::kBpi;
-        case DTYPE_Q4_0: return (w.nb + Geo<DTYPE_Q4_0>::kBpi - 1) / Geo<DTYPE_Q4_0>::kBpi;
-        case DTYPE_TQ2_0: return (w.nb + Geo<DTYPE_TQ2_0>::kBpi - 1) / Geo<DTYPE_TQ2_0>::kBpi;
-        default: return (w.kchunks + kUnitsPerItem - 1) / kUnitsPerItem;
-    }
+    const int units = (w.dtype == DTYPE_Q8_0 || w.dtype == DTYPE_Q4_0 || w.dtype == DTYPE_TQ2_0) ? w.nb : w.kchunks;
+    const int bpi = bpi_of(w.dtype);
+    return (units + bpi - 1) / bpi;
 }
 
 int sm_count(int dev) {
@@ -659,6 +806,27 @@ int sm_count(int dev) {
         cached[dev] = n;
     }
     return cached[dev];
+}
+
+template <tensor_dtype_t DT>
+int launch_cfg(kernel_context_t *ctx, const PipeParams &p, PipeCfg c, int grid, size_t smem, cudaStream_t st) {
+    auto run = [&](auto kernel, int threads) -> int {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) {
+            ctx_fail(ctx, "launch_gemv_pipe", "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+            return -1;
+        }
+        kernel<<<grid, threads, smem, st>>>(p);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            ctx_fail(ctx, "launch_gemv_pipe", "launch failed: %s", cudaGetErrorString(e));
+            return -1;
+        }
+        return 0;
+    };
+    if (c.nw == 8 && c.ns == 4) return run(gemv_pipe<DT, 8, 4>, 8 * 32);
+    if (c.nw == 16 && c.ns == 2) return run(gemv_pipe<DT, 16, 2>, 16 * 32);
+    return run(gemv_pipe<DT, 12, 3>, 12 * 32);
 }
 
 }  // namespace
@@ -679,7 +847,7 @@ bool pipe_supported(const DevWeight &w) {
     if (w.dtype != DTYPE_Q8_0 && w.dtype != DTYPE_Q4_0 && w.dtype != DTYPE_TQ2_0 && w.dtype != DTYPE_F32 &&
         w.dtype != DTYPE_BF16)
         return false;
-    return pipe_smem(w.dtype, w.nb, w.kchunks) <= 227 * 1024;
+    return pipe_smem(w.dtype, w.nb, w.kchunks, pipe_cfg()) <= 227 * 1024;
 }
 
 // Scratch in float units: partials [ntiles][kmax][32] (two floats per entry
@@ -687,7 +855,7 @@ bool pipe_supported(const DevWeight &w) {
 void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints) {
     const int nseg = item_nseg(w);
     const long long T = (long long)w.ntiles * nseg;
-    const long long W = (long long)sm_count(ctx->device) * kPipeWarps;
+    const long long W = (long long)sm_count(ctx->device) * pipe_cfg().nw;
     *part_floats = (size_t)w.ntiles * pipe_kmax(T, W, nseg) * 32 * (w.dtype == DTYPE_TQ2_0 ? 2 : 1);
     *cnt_ints = (size_t)w.ntiles;
 }
@@ -697,6 +865,7 @@ void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_f
 int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
                      int *err, cudaStream_t st) {
     if (w.ntiles == 0) return 0;
+    const PipeCfg c = pipe_cfg();
     PipeParams p;
     p.codes = reinterpret_cast<const uint8_t *>(w.codes);
     p.scales = w.scales;
@@ -713,29 +882,15 @@ int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, 
     p.nseg = item_nseg(w);
     p.total_items = (long long)w.ntiles * p.nseg;
     const int grid = sm_count(ctx->device);
-    p.total_warps = grid * kPipeWarps;
+    p.total_warps = grid * c.nw;
     p.kmax = pipe_kmax(p.total_items, p.total_warps, p.nseg);
-    const size_t smem = pipe_smem(w.dtype, w.nb, w.kchunks);
-    auto launch = [&](auto kernel) -> int {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) {
-            ctx_fail(ctx, "launch_gemv_pipe", "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-            return -1;
-        }
-        kernel<<<grid, kPipeThreads, smem, st>>>(p);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) {
-            ctx_fail(ctx, "launch_gemv_pipe", "launch failed: %s", cudaGetErrorString(e));
-            return -1;
-        }
-        return 0;
-    };
+    const size_t smem = pipe_smem(w.dtype, w.nb, w.kchunks, c);
     switch (w.dtype) {
-        case DTYPE_Q8_0: return launch(gemv_pipe<DTYPE_Q8_0>);
-        case DTYPE_Q4_0: return launch(gemv_pipe<DTYPE_Q4_0>);
-        case DTYPE_TQ2_0: return launch(gemv_pipe<DTYPE_TQ2_0>);
-        case DTYPE_F32: return launch(gemv_pipe<DTYPE_F32>);
-        case DTYPE_BF16: return launch(gemv_pipe<DTYPE_BF16>);
+        case DTYPE_Q8_0: return launch_cfg<DTYPE_Q8_0>(ctx, p, c, grid, smem, st);
+        case DTYPE_Q4_0: return launch_cfg<DTYPE_Q4_0>(ctx, p, c, grid, smem, st);
+        case DTYPE_TQ2_0: return launch_cfg<DTYPE_TQ2_0>(ctx, p, c, grid, smem, st);
+        case DTYPE_F32: return launch_cfg<DTYPE_F32>(ctx, p, c, grid, smem, st);
+        case DTYPE_BF16: return launch_cfg<DTYPE_BF16>(ctx, p, c, grid, smem, st);
         default:
             ctx_fail(ctx, "launch_gemv_pipe", "unsupported dtype");
             return -1;
