@@ -112,6 +112,7 @@ def ncu_traffic(kernel_tag: str):
     if not os.path.exists(p):
         return None
     for line in open(p):
+        line = line.strip()
         if line.startswith("dram_bytes_per_launch:"):
             try:
                 return int(float(line.split(":", 1)[1].strip().split()[0]))
@@ -396,6 +397,250 @@ def run_gpu_arm(args, cfg):
     return 0
 
 
+# ------------------------------------------------------------- prefill ------
+PREFILL_METRIC = "Q4_0 prefill dequant-GEMM TFLOP/s (tcgen05 tensor cores)"
+PREFILL_UNIT = "TFLOP/s"
+
+
+def prefill_flops(cfg, tokens=None) -> int:
+    return 2 * (cfg.batch if tokens is None else tokens) * cfg.rows * cfg.cols
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def cpu_prefill_time(cfg, packed, X, tokens: int, threads: int):
+    """Seconds for `tokens` reference kernel_gemv calls (one per token, the
+    reference's prefill; its Q4_0 kernel_gemm returns -1) on bf16-rounded
+    activations.  Falls back to the oracle port without oracle/_ref."""
+    from oracle.oracle import Reference, Oracle, available_reference
+    from sapphire_b200 import workloads
+    xs = workloads.pad_cols(bf16_round(X[:tokens]), cfg.cols)
+    if available_reference():
+        ref = Reference()
+        ctx = ref.ctx(threads)
+        t = ref.view(cfg.dtype, cfg.rows, cfg.cols, packed)
+        y = np.zeros(cfg.rows, dtype=np.float32)
+        ref.L.kernel_gemv(ctx, y.ctypes.data, t, xs[0].ctypes.data)          # warm
+        t0 = time.perf_counter()
+        for i in range(tokens):
+            ref.L.kernel_gemv(ctx, y.ctypes.data, t, xs[i].ctypes.data)
+        el = time.perf_counter() - t0
+        ref.L.tensor_release(t)
+        ref.L.kernel_ctx_destroy(ctx)
+        return el, "reference"
+    o = Oracle()
+    t0 = time.perf_counter()
+    o.gemv(cfg.dtype, packed, cfg.rows, cfg.cols, xs, nthreads=threads)
+    return time.perf_counter() - t0, "port"
+
+
+def prefill_cpu_baseline(cfg, packed, X, budget_s=10.0):
+    threads = os.cpu_count() or 1
+    el, kind = cpu_prefill_time(cfg, packed, X, 4, threads)
+    tokens = int(max(4, min(cfg.batch, 4 * budget_s / max(el, 1e-6))))
+    el, kind = cpu_prefill_time(cfg, packed, X, tokens, threads)
+    return {"value": round(prefill_flops(cfg, tokens) / el / 1e12, 5), "unit": PREFILL_UNIT, "cores": threads,
+            "kind": kind,
+            "sample": f"{tokens} of the {cfg.batch} tokens, one {'reference kernel_gemv' if kind == 'reference' else 'oracle port GEMV'}"
+                      f" call per token ({el / tokens * 1e3:.2f} ms each) with {threads} threads"}
+
+
+def run_reference_prefill(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import sapphire_b200 as sp
+    from oracle.oracle import Oracle
+    from sapphire_b200 import workloads
+    src, X = workloads.make_inputs(cfg, seed=0)
+    packed = Oracle().quantize(cfg.dtype, src)
+    del src
+    threads = os.cpu_count() or 1
+    tokens = 8                                   # per step: a bounded sample of the 2048 tokens
+    for _ in range(args.warmup):
+        cpu_prefill_time(cfg, packed, X, 1, threads)
+    total, kind = 0.0, "reference"
+    for _ in range(args.steps):
+        el, kind = cpu_prefill_time(cfg, packed, X, tokens, threads)
+        total += el
+    value = prefill_flops(cfg, tokens) * args.steps / total / 1e12
+    line = {"impl": "reference", "metric": PREFILL_METRIC, "value": round(value, 5), "unit": PREFILL_UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (PCG64 seed 0)",
+            "config": {"workload": cfg.name, "rows": cfg.rows, "cols": cfg.cols, "tokens": cfg.batch,
+                       "format": "Q4_0", "parallelism": "host thread pool"},
+            "cpu_baseline": {"value": round(value, 5), "unit": PREFILL_UNIT, "cores": threads, "kind": kind,
+                             "sample": f"each step {tokens} of the {cfg.batch} tokens, one kernel_gemv per token"},
+            "e2e": {"value": round(value, 5), "unit": PREFILL_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_gpu_prefill(args, cfg):
+    import torch
+    import torch.distributed as dist
+    import sapphire_b200 as sp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    ctx = sp.Context(num_threads=1)
+    if world > 1:
+        uid = torch.zeros(sp.UNIQUE_ID_BYTES, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(sp.shard_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        ctx.shard(rank, world, bytes(uid.cpu().numpy().tobytes()))
+
+    packed0, X = build_weight(sp, ctx, cfg, seed=0)
+    packed1, X1 = build_weight(sp, ctx, cfg, seed=1)
+    A = [sp.Tensor(cfg.dtype, (cfg.rows, cfg.cols), packed0), sp.Tensor(cfg.dtype, (cfg.rows, cfg.cols), packed1)]
+    for a in A:
+        ctx.check(sp.lib.kernel_tensor_upload(ctx.handle, a.handle), "upload")
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    Xd = [torch.from_numpy(np.ascontiguousarray(X)).cuda(), torch.from_numpy(np.ascontiguousarray(X1)).cuda()]
+    Yd = torch.zeros((cfg.batch, cfg.rows), device="cuda")
+    flops = prefill_flops(cfg)
+
+    def step(i):
+        return sp.lib.kernel_gemm_device(ctx.handle, Yd.data_ptr(), A[i & 1].handle, Xd[i & 1].data_ptr(), cfg.batch)
+
+    for i in range(args.warmup):
+        ctx.check(step(i), "warm-up")
+    ctx.synchronize()
+    t0e = torch.cuda.Event(enable_timing=True)
+    t1e = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    t0e.record(stream)
+    for i in range(args.steps):
+        ctx.check(step(i), "step")
+    t1e.record(stream)
+    ctx.synchronize()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.__exit__()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([t0e.elapsed_time(t1e)], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t.item()) / args.steps
+    value = flops / (ms_per_step * 1e-3) / 1e12
+
+    # GEMM kernel alone (activations already bf16 on the device), unsharded.
+    kern_ms = None
+    if world == 1:
+        kp = ((cfg.cols + 31) // 32 * 32 + 63) // 64 * 64
+        Xb = []
+        for x in Xd:
+            xb = torch.zeros((cfg.batch, kp), dtype=torch.bfloat16, device="cuda")
+            xb[:, :cfg.cols] = x.to(torch.bfloat16)
+            Xb.append(xb)
+        torch.cuda.synchronize()
+
+        def kstep(i):
+            return sp.lib.kernel_gemm_device_bf16(ctx.handle, Yd.data_ptr(), A[i & 1].handle, Xb[i & 1].data_ptr(),
+                                                  cfg.batch, kp)
+        for i in range(args.warmup):
+            ctx.check(kstep(i), "kernel warm-up")
+        ctx.synchronize()
+        evs = []
+        for i in range(args.steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            ctx.check(kstep(i), "kernel step")
+            e1.record(stream)
+            evs.append((e0, e1))
+        ctx.synchronize()
+        kern_ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+
+    # End to end through kernel_gemm with pinned host buffers (X in, Y out).
+    xh = [torch.from_numpy(np.ascontiguousarray(X)).pin_memory(), torch.from_numpy(np.ascontiguousarray(X1)).pin_memory()]
+    yh = torch.zeros((cfg.batch, cfg.rows)).pin_memory()
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step(i):
+        return sp.lib.kernel_gemm(ctx.handle, yh.data_ptr(), A[i & 1].handle, xh[i & 1].data_ptr(), cfg.batch,
+                                  cfg.rows)
+    for i in range(args.warmup):
+        ctx.check(e2e_step(i), "e2e warm-up")
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    w0 = time.perf_counter()
+    for i in range(e2e_steps):
+        ctx.check(e2e_step(i), "e2e step")
+    ev1.record(stream)
+    ctx.synchronize()
+    e2e_ms = max(ev0.elapsed_time(ev1), (time.perf_counter() - w0) * 1e3)
+    t = torch.tensor([e2e_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item()) / e2e_steps
+
+    result = None
+    if rank == 0:
+        peaks = measured_peaks()
+        tag = f"gemm_tc_{cfg.name}"
+        roof = {"bound": "tensor", "unit": PREFILL_UNIT, "peak": peaks["bf16_tflops"],
+                "peak_source": peaks["source"] + " (dense bf16 cuBLAS, burst)", "kernel": tag,
+                "traffic": ncu_traffic(tag),
+                "note": "achieved counts the algorithmic 2*tokens*rows*cols FLOP; the kernel issues twice as "
+                        "many MMA FLOP (hi + lo weight halves)"}
+        if kern_ms is not None:
+            ach = flops / (kern_ms * 1e-3) / 1e12
+            roof.update({"achieved": round(ach, 2), "frac": round(ach / peaks["bf16_tflops"], 4),
+                         "kernel_ms": round(kern_ms, 5)})
+        else:
+            roof.update({"achieved": None, "frac": None, "kernel_ms": None})
+        result = {
+            "metric": PREFILL_METRIC, "value": round(value, 3), "unit": PREFILL_UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (PCG64 seed 0; N(0,0.02) weights quantised on the GPU, N(0,1) X)",
+            "config": {"workload": cfg.name, "rows": cfg.rows, "cols": cfg.cols, "tokens": cfg.batch,
+                       "format": "Q4_0", "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1
+                       else "single GPU", "flop_per_step": flops,
+                       "l2": "inputs larger than L2: 84 MB of Y written per step, weights and X alternate"},
+            "roofline": roof,
+            "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 3), "unit": PREFILL_UNIT,
+                    "h2d_bytes_per_step": 4 * cfg.batch * cfg.cols, "d2h_bytes_per_step": 4 * cfg.batch * cfg.rows,
+                    "ms_per_step": round(e2e_ms, 4), "path": "kernel_gemm with pinned host X/Y"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": sampler.summary() if sampler else {},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = prefill_cpu_baseline(cfg, packed0, X)
+    for a in A:
+        a.release()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -409,6 +654,8 @@ def main():
         args.warmup = 3
     from sapphire_b200 import workloads
     cfg = workloads.CONFIGS[args.config]
+    if cfg.batch > 1:
+        return run_reference_prefill(args, cfg) if args.impl == "reference" else run_gpu_prefill(args, cfg)
     if args.impl == "reference":
         return run_reference_arm(args, cfg)
     return run_gpu_arm(args, cfg)

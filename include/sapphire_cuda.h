@@ -67,8 +67,19 @@ SAPPHIRE_API size_t kernel_ctx_resident_bytes(kernel_context_t *ctx);
  * context, or kernel_ctx_synchronize, sees the result.
  * ------------------------------------------------------------------------- */
 SAPPHIRE_API int kernel_gemv_device(kernel_context_t *ctx, float *y, const tensor_t *A, const float *x);
-/** Y[b*rows + r] = A[r,:] . X[b*cols ..] for b < batch_size (device pointers). */
+/** Y[b*rows + r] = A[r,:] . X[b*cols ..] for b < batch_size (device pointers).
+ *  A Q4_0 weight with batch_size >= 16 (here and in kernel_gemm) runs the
+ *  tensor-core prefill product: activations rounded to bf16 (nearest even),
+ *  weights dequantised exactly, fp32 accumulation. */
 SAPPHIRE_API int kernel_gemm_device(kernel_context_t *ctx, float *Y, const tensor_t *A, const float *X, int batch_size);
+/** Tensor-core prefill product from bf16 activations already on the device
+ *  (no counterpart in the reference, whose Q4_0 kernel_gemm returns -1):
+ *  Y[b*rows + r] = A[r,:] . Xb[b*x_stride ..] for b < batch_size.  A: Q4_0.
+ *  Xb: bf16 values, 16-byte aligned, x_stride a multiple of 8 and at least
+ *  32 * ceil(cols / 32), zero from column `cols` to the end of the last
+ *  block.  Unsharded contexts only.  Asynchronous like kernel_gemm_device. */
+SAPPHIRE_API int kernel_gemm_device_bf16(kernel_context_t *ctx, float *Y, const tensor_t *A, const void *Xb,
+                                         int batch_size, int x_stride);
 /** Batch-1 y = A @ x like kernel_gemv_device, for callers that must not
  *  allocate device memory when they multiply (a serving loop with a fixed
  *  memory budget or pool, or a path where an allocation's implicit device

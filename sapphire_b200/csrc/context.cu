@@ -210,6 +210,7 @@ extern "C" SAPPHIRE_API void kernel_ctx_destroy(kernel_context_t *ctx) {
             if (ctx->d_t) cudaFree(ctx->d_t);
             if (ctx->d_part) cudaFree(ctx->d_part);
             if (ctx->d_cnt) cudaFree(ctx->d_cnt);
+            if (ctx->d_xb) cudaFree(ctx->d_xb);
             if (ctx->h_err) cudaFreeHost(ctx->h_err);
             shard_destroy(ctx);
             if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -293,7 +294,7 @@ int ensure_scratch(kernel_context_t *ctx, float **buf, size_t *cap, size_t bytes
 // demand; the counters return to zero at the end of every launch, so only new
 // memory needs clearing.  The error word lives in mapped pinned host memory:
 // a kernel writes it only on failure and the host reads it after a sync.
-static int ensure_pipe_scratch(kernel_context_t *ctx, size_t part_floats, size_t cnt_ints) {
+int ensure_pipe_scratch(kernel_context_t *ctx, size_t part_floats, size_t cnt_ints) {
     if (!ctx->h_err) {
         int *h = nullptr;
         CUDA_TRY(ctx, cudaHostAlloc((void **)&h, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable));
@@ -337,7 +338,11 @@ int launch_product(kernel_context_t *ctx, const DevWeight &w, const float *x, in
                    int batch, cudaStream_t st) {
     if (batch == 1) return launch_gemv_best(ctx, w, x, y, st);
     if (w.dtype == DTYPE_F32 || w.dtype == DTYPE_BF16) return launch_gemv(ctx, w, x, x_stride, y, y_stride, batch, st);
-    // Quantized weights: one pipelined pass per activation row.
+    if (gemm_tc_supported(w, batch)) {
+        if (ensure_pipe_scratch(ctx, 0, 0)) return -1;
+        return launch_gemm_tc(ctx, w, x, x_stride, y, y_stride, batch, ctx->d_err, st);
+    }
+    // Other quantized products: one pipelined pass per activation row.
     for (int b = 0; b < batch; ++b)
         if (launch_gemv_best(ctx, w, x + (size_t)b * x_stride, y + (size_t)b * y_stride, st)) return -1;
     return 0;
@@ -346,7 +351,7 @@ int launch_product(kernel_context_t *ctx, const DevWeight &w, const float *x, in
 int check_kernel_error(kernel_context_t *ctx, const char *who) {
     if (ctx->h_err && *reinterpret_cast<volatile int *>(ctx->h_err)) {
         *ctx->h_err = 0;
-        ctx_fail(ctx, who, "a GEMV kernel gave up waiting for its weight copies (bounded wait expired)");
+        ctx_fail(ctx, who, "a kernel gave up waiting for its asynchronous copies (bounded wait expired)");
         return -1;
     }
     return 0;

@@ -298,6 +298,33 @@ extern "C" SAPPHIRE_API int kernel_gemm_device(kernel_context_t *ctx, float *Y, 
     return run_product(ctx, Y, A, X, batch_size, false, true);
 }
 
+extern "C" SAPPHIRE_API int kernel_gemm_device_bf16(kernel_context_t *ctx, float *Y, const tensor_t *A,
+                                                    const void *Xb, int batch_size, int x_stride) {
+    if (!ctx || !Y || !A || !Xb || batch_size <= 0) {
+        LOG_ERROR("kernel_gemm_device_bf16 invalid arguments");
+        return -1;
+    }
+    if (tensor_dtype(A) != DTYPE_Q4_0) {
+        LOG_ERROR("kernel_gemm_device_bf16 needs a Q4_0 weight");
+        return -1;
+    }
+    std::lock_guard<std::recursive_mutex> lk(ctx->exec_mutex);
+    if (!ctx->initialized || ctx->world > 1) {
+        ctx_fail(ctx, "kernel_gemm_device_bf16", "needs an initialized, unsharded context");
+        return -1;
+    }
+    DeviceGuard g(ctx->device);
+    int xdev = -1, ydev = -1;
+    if (!ptr_is_device(Xb, &xdev) || !ptr_is_device(Y, &ydev) || xdev != ctx->device || ydev != ctx->device) {
+        ctx_fail(ctx, "kernel_gemm_device_bf16", "Y and Xb must be device pointers on the context's GPU");
+        return -1;
+    }
+    const DevWeight *w = ctx_weight(ctx, A);
+    if (!w) return -1;
+    if (ensure_pipe_scratch(ctx, 0, 0)) return -1;
+    return launch_gemm_tc_bf16(ctx, *w, Xb, x_stride, Y, w->nrows, batch_size, ctx->d_err, ctx->stream);
+}
+
 // ------------------------------------------------------------ quantisers --
 namespace {
 

@@ -93,6 +93,8 @@ struct sapphire_context {
     float *d_part = nullptr; size_t d_part_cap = 0;
     int *d_cnt = nullptr;    size_t d_cnt_cap = 0;
     int *h_err = nullptr;    int *d_err = nullptr;
+    // bf16 copy of the activations for the tensor-core batched product.
+    float *d_xb = nullptr;   size_t d_xb_cap = 0;
 
     HostPool *pool = nullptr;
 
@@ -157,6 +159,10 @@ int launch_row_dot(kernel_context_t *ctx, tensor_dtype_t dt, const void *row, co
 int launch_axpy(kernel_context_t *ctx, float *y, const float *t, float alpha, size_t n,
                 cudaStream_t stream);
 
+// Error word (mapped host memory) plus split-tile scratch of the pipelined
+// GEMV, grown to at least the given sizes.
+int ensure_pipe_scratch(kernel_context_t *ctx, size_t part_floats, size_t cnt_ints);
+
 // Pipelined batch-1 GEMV (gemv_pipe.cu).
 bool pipe_supported(const DevWeight &w);
 void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints);
@@ -172,6 +178,18 @@ int launch_product(kernel_context_t *ctx, const DevWeight &w, const float *x, in
 // Reads and clears the error word after a synchronisation; -1 if a kernel
 // reported a failed wait.
 int check_kernel_error(kernel_context_t *ctx, const char *who);
+
+// Tensor-core batched product of a Q4_0 weight (gemm_tc.cu), used for
+// batch >= kGemmTcMinBatch: activations rounded to bf16, weights dequantised
+// exactly (hi + lo bf16 halves), fp32 accumulation.  err: error word.
+constexpr int kGemmTcMinBatch = 16;
+bool gemm_tc_supported(const DevWeight &w, int batch);
+int launch_gemm_tc(kernel_context_t *ctx, const DevWeight &w, const float *x, int ldx, float *y, int ldy, int batch,
+                   int *err, cudaStream_t stream);
+// Same product from bf16 activations already on the device: xb [batch][ldxb],
+// ldxb >= 32 * nb and a multiple of 8, 16-byte aligned, zero past the columns.
+int launch_gemm_tc_bf16(kernel_context_t *ctx, const DevWeight &w, const void *xb, int ldxb, float *y, int ldy,
+                        int batch, int *err, cudaStream_t stream);
 
 // Sharded all-gather of per-rank slices (NCCL).  Defined in shard.cu.
 int shard_allgather(kernel_context_t *ctx, const float *send, float *recv, size_t count,
