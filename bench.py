@@ -247,7 +247,7 @@ def run_gpu_arm(args, cfg):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
 
-    ctx = sp.Context(num_threads=1)
+    ctx = sp.Context(num_threads=1, device=local)
     if world > 1:
         uid = torch.zeros(sp.UNIQUE_ID_BYTES, dtype=torch.uint8, device="cuda")
         if rank == 0:
@@ -280,13 +280,15 @@ def run_gpu_arm(args, cfg):
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t_all0 = torch.cuda.Event(enable_timing=True)
     t_all1 = torch.cuda.Event(enable_timing=True)
+    # The clock sampler starts before the barrier so that every rank enters
+    # the timed region together.
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     ctx.synchronize()
-    sampler = ClockSampler(local) if rank == 0 else None
-    if sampler:
-        sampler.__enter__()
     t_all0.record(stream)
     for i in range(args.steps):
         starts[i].record(stream)
@@ -313,7 +315,7 @@ def run_gpu_arm(args, cfg):
     if world == 1:
         kern_ms = float(np.mean(step_ms))
     else:
-        # Sharded step = GEMV + all-gather; time the local GEMV alone too.
+        # Sharded: the timed call is the local GEMV followed by the all-gather.
         kernel_only = []
         ys = torch.zeros((1, (cfg.rows + world - 1) // world), device="cuda")
         torch.cuda.synchronize()
@@ -377,7 +379,8 @@ def run_gpu_arm(args, cfg):
                        "algorithmic_bytes_per_step": bytes_per},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
-                         "kernel_ms": round(kern_ms, 5), "traffic": ncu_traffic(tag), "kernel": tag},
+                         "kernel_ms": round(kern_ms, 5), "traffic": ncu_traffic(tag), "kernel": tag,
+                         "kernel_ms_covers": "GEMV kernel" if world == 1 else "local GEMV + NCCL all-gather"},
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": 4 * cfg.cols,
                     "d2h_bytes_per_step": 4 * cfg.rows, "ms_per_step": round(e2e_ms, 5),
                     "path": "kernel_gemv with pinned host x/y (weights resident after upload)"},
@@ -494,7 +497,7 @@ def run_gpu_prefill(args, cfg):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    ctx = sp.Context(num_threads=1)
+    ctx = sp.Context(num_threads=1, device=local)
     if world > 1:
         uid = torch.zeros(sp.UNIQUE_ID_BYTES, dtype=torch.uint8, device="cuda")
         if rank == 0:
@@ -520,12 +523,12 @@ def run_gpu_prefill(args, cfg):
     ctx.synchronize()
     t0e = torch.cuda.Event(enable_timing=True)
     t1e = torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.__enter__()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     t0e.record(stream)
     for i in range(args.steps):
         ctx.check(step(i), "step")

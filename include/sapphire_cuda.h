@@ -104,6 +104,10 @@ SAPPHIRE_API void* kernel_ctx_get_stream(kernel_context_t *ctx);
 SAPPHIRE_API int kernel_ctx_set_stream(kernel_context_t *ctx, void *stream);
 /** CUDA ordinal the context is bound to, -1 for NULL. */
 SAPPHIRE_API int kernel_ctx_get_device(kernel_context_t *ctx);
+/** Choose the GPU of a context before kernel_ctx_init (default: the calling
+ *  thread's current device at kernel_ctx_create).  -1 after init or when the
+ *  device does not exist. */
+SAPPHIRE_API int kernel_ctx_set_device(kernel_context_t *ctx, int device);
 /** Message of the last error recorded on the context ("" if none). */
 SAPPHIRE_API const char* kernel_ctx_last_error(kernel_context_t *ctx);
 
@@ -144,6 +148,10 @@ SAPPHIRE_API int kernel_shard_unique_id(void *id_out);
 SAPPHIRE_API int kernel_ctx_init_sharded(kernel_context_t *ctx, int rank, int world_size, const void *unique_id);
 /** This context's rank and world size (0 / 1 when not sharded). */
 SAPPHIRE_API int kernel_ctx_shard_info(kernel_context_t *ctx, int *rank, int *world_size);
+/** Rows [*row0, *row0 + *nrows) of a `rows`-row weight owned by `rank` of
+ *  `world_size` (the rule above; *nrows may be 0 for trailing ranks).
+ *  Pure arithmetic, no GPU.  0 on success, -1 on bad arguments. */
+SAPPHIRE_API int sapphire_shard_rows(int rows, int rank, int world_size, int *row0, int *nrows);
 
 #ifdef __cplusplus
 }

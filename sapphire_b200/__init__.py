@@ -44,10 +44,15 @@ def row_bytes(dtype: int, cols: int) -> int:
 class Context:
     """kernel_context_t: one GPU, a stream, resident weights, host workers."""
 
-    def __init__(self, num_threads: int = 0, chunk_size: int = 16, init: bool = True):
+    def __init__(self, num_threads: int = 0, chunk_size: int = 16, init: bool = True, device: int | None = None):
         self.handle = lib.kernel_ctx_create(num_threads, chunk_size)
         if not self.handle:
             raise SapphireError("kernel_ctx_create failed")
+        if device is not None and lib.kernel_ctx_set_device(self.handle, device) != 0:
+            msg = self.last_error
+            lib.kernel_ctx_destroy(self.handle)
+            self.handle = None
+            raise SapphireError(f"kernel_ctx_set_device failed: {msg}")
         if init and lib.kernel_ctx_init(self.handle) != 0:
             msg = self.last_error
             lib.kernel_ctx_destroy(self.handle)
@@ -96,6 +101,14 @@ class Context:
             self.close()
         except Exception:
             pass
+
+
+def shard_rows(rows: int, rank: int, world: int) -> tuple[int, int]:
+    """(row0, nrows) of the rows `rank` of `world` owns (sapphire_shard_rows)."""
+    r0, n = C.c_int(0), C.c_int(0)
+    if lib.sapphire_shard_rows(rows, rank, world, C.byref(r0), C.byref(n)) != 0:
+        raise SapphireError(f"sapphire_shard_rows({rows}, {rank}, {world}) rejected its arguments")
+    return r0.value, n.value
 
 
 def shard_unique_id() -> bytes:

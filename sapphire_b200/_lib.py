@@ -85,7 +85,9 @@ _SIGNATURES = {
     "kernel_gemv_device_noalloc": (i32, [vp, vp, vp, vp]),
     "kernel_gemm_device": (i32, [vp, vp, vp, vp, i32]),
     "kernel_gemm_device_bf16": (i32, [vp, vp, vp, vp, i32, i32]),
+    "sapphire_shard_rows": (i32, [i32, i32, i32, vp, vp]),
     "kernel_ctx_synchronize": (i32, [vp]),
+    "kernel_ctx_set_device": (i32, [vp, i32]),
     "kernel_ctx_get_stream": (vp, [vp]),
     "kernel_ctx_set_stream": (i32, [vp, vp]),
     "kernel_ctx_get_device": (i32, [vp]),

@@ -548,6 +548,26 @@ extern "C" SAPPHIRE_API int kernel_ctx_set_stream(kernel_context_t *ctx, void *s
 
 extern "C" SAPPHIRE_API int kernel_ctx_get_device(kernel_context_t *ctx) { return ctx ? ctx->device : -1; }
 
+extern "C" SAPPHIRE_API int kernel_ctx_set_device(kernel_context_t *ctx, int device) {
+    if (!ctx) return -1;
+    std::lock_guard<std::recursive_mutex> lk(ctx->exec_mutex);
+    if (ctx->initialized) {
+        ctx_fail(ctx, "kernel_ctx_set_device", "context already initialized on device %d", ctx->device);
+        return -1;
+    }
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess) {
+        cudaGetLastError();
+        ndev = 0;
+    }
+    if (device < 0 || device >= ndev) {
+        ctx_fail(ctx, "kernel_ctx_set_device", "no device %d (%d visible)", device, ndev);
+        return -1;
+    }
+    ctx->device = device;
+    return 0;
+}
+
 extern "C" SAPPHIRE_API const char *kernel_ctx_last_error(kernel_context_t *ctx) {
     return ctx ? ctx->last_error.c_str() : "";
 }

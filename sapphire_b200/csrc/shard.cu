@@ -120,6 +120,12 @@ extern "C" SAPPHIRE_API int kernel_ctx_shard_info(kernel_context_t *ctx, int *ra
     return 0;
 }
 
+extern "C" SAPPHIRE_API int sapphire_shard_rows(int rows, int rank, int world_size, int *row0, int *nrows) {
+    if (rows < 0 || world_size < 1 || rank < 0 || rank >= world_size || !row0 || !nrows) return -1;
+    shard_rows(rows, rank, world_size, row0, nrows);
+    return 0;
+}
+
 int shard_allgather(kernel_context_t *ctx, const float *send, float *recv, size_t count, cudaStream_t stream) {
     if (!ctx->nccl_comm) {
         ctx_fail(ctx, "shard_allgather", "context has no communicator");
