@@ -644,6 +644,163 @@ def run_gpu_prefill(args, cfg):
     return 0
 
 
+# -------------------------------------------------------------- decode -----
+DECODE_METRIC = "Gemma-3-270M decode tok/s (greedy, Q4_0 projections and LM head)"
+DECODE_UNIT = "tok/s"
+
+
+def decode_bytes_per_token(cfg, pos: int) -> int:
+    """Algorithmic HBM bytes of one generated token at position `pos`: every
+    packed Q4_0 projection and the LM head, the embedding row, the KV rows the
+    attention reads (the window for local layers) and writes, x/y vectors
+    neglected (< 0.1 %)."""
+    from sapphire_b200 import row_bytes
+    w = 0
+    for _, rows, cols in cfg.projections():
+        w += rows * row_bytes(3, cols)
+    w *= cfg.layers
+    w += cfg.vocab * row_bytes(3, cfg.hidden) + 2 * cfg.hidden
+    kv_row = cfg.kv_heads * cfg.head_dim * 4
+    for layer in range(cfg.layers):
+        n = pos + 1 if cfg.is_global(layer) else min(pos + 1, cfg.sliding_window)
+        w += 2 * n * kv_row + 2 * kv_row
+    return w
+
+
+def decode_cpu_baseline(cfg, model, n_gen=None):
+    from oracle.oracle import ReferenceDecode, available_reference_decode
+    if not available_reference_decode():
+        return None
+    toks, _, _, tp, td = ReferenceDecode().run(cfg, model, n_gen=n_gen)
+    n = len(toks)
+    return {"value": round(n / td, 3), "unit": DECODE_UNIT, "cores": os.cpu_count() or 1, "kind": "reference",
+            "sample": f"one reference decode (its inference_forward per token, Q4_0 kernel_gemv, all host "
+                      f"threads): {cfg.prompt}-token prompt in {tp:.1f} s, then {n} greedy tokens in {td:.2f} s"}
+
+
+def run_reference_decode(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle.oracle import Oracle, available_reference_decode
+    from sapphire_b200 import workloads
+    if not available_reference_decode():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libdecode_ref.so not built "
+                          "(make -C oracle ref needs the reference sources)"}), flush=True)
+        return 0
+    o = Oracle()
+    model = workloads.make_decode_model(cfg, lambda a: o.quantize(3, a), seed=0)
+    n_gen = max(1, min(args.steps, cfg.generate))
+    cb = decode_cpu_baseline(cfg, model, n_gen=n_gen)
+    line = {"impl": "reference", "metric": DECODE_METRIC, "value": cb["value"], "unit": DECODE_UNIT,
+            "n_gpus": args.gpus, "steps": n_gen, "warmup": 0, "ms_per_step": round(1e3 / cb["value"], 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (PCG64 seed 0, random-init Gemma-3-270M)",
+            "config": {"workload": cfg.name, "prompt": cfg.prompt, "generated": n_gen,
+                       "parallelism": "host thread pool"},
+            "cpu_baseline": dict(cb, sample=cb["sample"] + "; a step is one generated token"),
+            "e2e": {"value": cb["value"], "unit": DECODE_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_gpu_decode(args, cfg):
+    """Each step is one full request: the 512-token prompt, then 64 greedy
+    tokens.  `value` is generated tokens per second of the generation phase
+    (device events); N > 1 runs independent replicas (decode does not shard)."""
+    import torch
+    import torch.distributed as dist
+    import sapphire_b200 as sp
+    from sapphire_b200 import workloads
+    from sapphire_b200.decode import Decoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    ctx = sp.Context(num_threads=1, device=local)
+    model = workloads.make_decode_model(cfg, lambda a: sp.quantize(ctx, 3, a), seed=0)
+    dec = Decoder(ctx, cfg, model)
+    prompt = model["prompt"]
+    for _ in range(args.warmup):
+        dec.generate(prompt, cfg.generate)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    gen_ms, prompt_ms, walls = [], [], []
+    ids = None
+    for _ in range(args.steps):
+        w0 = time.perf_counter()
+        ids, _ = dec.generate(prompt, cfg.generate)
+        walls.append(time.perf_counter() - w0)
+        pm, gm = dec.last_times()
+        prompt_ms.append(pm)
+        gen_ms.append(gm)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.__exit__()
+    t = torch.tensor([float(np.sum(gen_ms)), float(np.sum(prompt_ms)), float(np.sum(walls))], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    gen_total, prompt_total, wall_total = (float(v) for v in t.tolist())
+    n_tok = cfg.generate * args.steps
+    value = world * n_tok / (gen_total * 1e-3)
+    result = None
+    if rank == 0:
+        peaks = measured_peaks()
+        bpt = float(np.mean([decode_bytes_per_token(cfg, cfg.prompt - 1 + g) for g in range(cfg.generate)]))
+        ms_tok = gen_total / n_tok
+        achieved = bpt / (ms_tok * 1e-3) / 1e9
+        golden = os.path.join(ROOT, "tests", "golden", "decode_gemma3_270m_seed0.npz")
+        match = None
+        if os.path.exists(golden):
+            match = bool(np.array_equal(ids, np.load(golden)["tokens"]))
+        result = {
+            "metric": DECODE_METRIC, "value": round(value, 2), "unit": DECODE_UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(gen_total / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (PCG64 seed 0; random-init Gemma-3-270M, N(0,0.02) weights, Q4_0 projections "
+                    "and LM head, bf16 embedding, zero norm weights)",
+            "config": {"workload": cfg.name, "prompt": cfg.prompt, "generated": cfg.generate,
+                       "context": cfg.context, "sliding_window": cfg.sliding_window,
+                       "parallelism": f"{world} independent replicas" if world > 1 else "single GPU",
+                       "step": "one request: prompt then greedy generation",
+                       "l2": "inputs larger than L2: 168 MB of weights read per token",
+                       "prompt_tok_s": round((cfg.prompt - 1) * args.steps / (prompt_total * 1e-3), 1),
+                       "tokens_match_reference": match},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"],
+                         "kernel_ms": round(ms_tok, 5), "traffic": None,
+                         "kernel": "decode step graph (generation phase, per token)",
+                         "bytes_per_token": int(bpt)},
+            "e2e": {"value": round(n_tok / wall_total, 2), "unit": DECODE_UNIT,
+                    "h2d_bytes_per_step": 4 * cfg.prompt, "d2h_bytes_per_step": 8 * cfg.generate,
+                    "ms_per_step": round(wall_total / args.steps * 1e3, 3),
+                    "path": "sapphire_decoder_generate with a host prompt and host ids (prompt phase included)"},
+            "gpu_launches": args.steps * (cfg.generate * dec.launches_per_token
+                                          + (cfg.prompt - 1) * (dec.launches_per_token - 1)),
+            "clocks": sampler.summary() if sampler else {},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            cb = decode_cpu_baseline(cfg, model)
+            if cb:
+                result["cpu_baseline"] = cb
+    dec.close()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -656,6 +813,9 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     from sapphire_b200 import workloads
+    if args.config == workloads.C3.name:
+        cfg = workloads.C3
+        return run_reference_decode(args, cfg) if args.impl == "reference" else run_gpu_decode(args, cfg)
     cfg = workloads.CONFIGS[args.config]
     if cfg.batch > 1:
         return run_reference_prefill(args, cfg) if args.impl == "reference" else run_gpu_prefill(args, cfg)

@@ -127,3 +127,50 @@ class Reference:
 
 def available_reference() -> bool:
     return os.path.exists(REF_SO)
+
+
+DECODE_SO = os.path.join(HERE, "_ref", "libdecode_ref.so")
+
+
+def available_reference_decode() -> bool:
+    return os.path.exists(DECODE_SO)
+
+
+class ReferenceDecode:
+    """The reference's Gemma-3 decode (its inference session, layers and
+    Q4_0 kernel_gemv, compiled unmodified) driven by oracle/decode_ref.c."""
+
+    def __init__(self, path: str = DECODE_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle ref`")
+        # Load the reference library first so its log level can be set.
+        ref = C.CDLL(REF_SO)
+        ref.log_set_level.argtypes = [i32]
+        ref.log_set_level(40)  # errors only
+        L = C.CDLL(path)
+        L.decode_ref_run.restype = i32
+        L.decode_ref_run.argtypes = [vp, i32, i32, vp, vp, vp] + [i32] * 9 + [vp, vp, vp, vp, vp]
+        self.L = L
+        self._ref = ref
+
+    def run(self, cfg, model, n_gen: int | None = None, n_prompt: int | None = None, want_logits: bool = False):
+        """(tokens int32 [n_gen], margins f32 [n_gen], logits0 or None,
+        prefill seconds, decode seconds) for a model from
+        sapphire_b200.workloads.make_decode_model."""
+        n_gen = cfg.generate if n_gen is None else n_gen
+        prompt = np.ascontiguousarray(model["prompt"][: (n_prompt or cfg.prompt)], dtype=np.int32)
+        ptrs = []
+        for layer in model["layers"]:
+            for name, _, _ in cfg.projections():
+                ptrs.append(_a(layer[name]))
+        wp = (C.c_void_p * len(ptrs))(*ptrs)
+        toks = np.zeros(n_gen, dtype=np.int32)
+        margins = np.zeros(n_gen, dtype=np.float32)
+        logits = np.zeros(cfg.vocab, dtype=np.float32) if want_logits else None
+        tp, td = C.c_double(0), C.c_double(0)
+        rc = self.L.decode_ref_run(_a(prompt), len(prompt), n_gen, _a(model["embed"]), C.cast(wp, vp),
+                                   _a(model["lm_head"]), cfg.layers, cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads,
+                                   cfg.head_dim, cfg.vocab, cfg.context, cfg.sliding_window, _a(toks), _a(margins),
+                                   _a(logits) if logits is not None else 0, C.addressof(tp), C.addressof(td))
+        assert rc == 0, "reference decode failed"
+        return toks, margins, logits, tp.value, td.value

@@ -101,7 +101,27 @@ _SIGNATURES = {
     "kernel_shard_unique_id": (i32, [vp]),
     "kernel_ctx_init_sharded": (i32, [vp, i32, i32, vp]),
     "kernel_ctx_shard_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32)]),
+    # include/sapphire_decode.h
+    "sapphire_decoder_create": (vp, [vp, vp, vp]),
+    "sapphire_decoder_generate": (i32, [vp, vp, i32, i32, vp, vp]),
+    "sapphire_decoder_last_logits": (i32, [vp, vp]),
+    "sapphire_decoder_last_times": (i32, [vp, C.POINTER(f32), C.POINTER(f32)]),
+    "sapphire_decoder_launches_per_token": (i32, [vp]),
+    "sapphire_decoder_destroy": (None, [vp]),
 }
+
+
+class Gemma3Config(C.Structure):
+    """sapphire_gemma3_config_t (include/sapphire_decode.h)."""
+    _fields_ = [("layers", i32), ("hidden", i32), ("ffn", i32), ("heads", i32), ("kv_heads", i32),
+                ("head_dim", i32), ("vocab", i32), ("context", i32), ("sliding_window", i32),
+                ("rope_theta", f32), ("rope_local_theta", f32), ("query_pre_attn_scalar", f32),
+                ("rms_eps", f32), ("global_mask", C.c_ulonglong)]
+
+
+class Gemma3Weights(C.Structure):
+    """sapphire_gemma3_weights_t (include/sapphire_decode.h)."""
+    _fields_ = [("embed_bf16", vp), ("lm_head", vp), ("final_norm", vp), ("proj", vp), ("norms", vp)]
 
 
 def load(path: str = LIB_PATH) -> C.CDLL:

@@ -1,0 +1,853 @@
+// decode.cu - device-resident Gemma-3 decoder (include/sapphire_decode.h).
+//
+// One token's step mirrors the reference's inference_forward
+// (src/inference/inference.c:616-651) and its layer stages
+// (src/transformer/attention.c:311-375, src/transformer/transformer.c:96-283):
+//
+//   hidden = bf16 embedding row * sqrt(hidden)              (transformer.c:367-380)
+//   per layer:
+//     norm   = rmsnorm_delta(hidden, attn)                   (attention.c:321-325)
+//     qkv    = [Wq; Wk; Wv] . norm        one Q4_0 GEMV over the concatenated rows
+//     q, k   = rmsnorm_delta per head (q_norm / k_norm), RoPE at pos (half split)
+//     K, V cache[pos] = k, v                                 (attention.c:292-309)
+//     attn   = softmax(q . K / sqrt(query_pre_attn_scalar)) . V over the layer's
+//              window (all positions for global layers)      (attention.c:93-163)
+//     hidden += rmsnorm_delta(Wo . attn, attn_post)          (attention.c:348-366)
+//     norm   = rmsnorm_delta(hidden, ffn)                    (transformer.c:119-121)
+//     gu     = [Wgate; Wup] . norm        one Q4_0 GEMV
+//     hidden += rmsnorm_delta(Wdown . (gelu(gate) * up), ffn_post)
+//   logits = Wlm . rmsnorm_delta(hidden, final)              (transformer.c:393-408)
+//   token  = greedy argmax, lowest index on ties             (src/utils/utils.c:145-156)
+//
+// All arithmetic is fp32 like the reference; sums run in a different order, so
+// the results agree to rounding, not bit for bit.  The RoPE tables are
+// computed on the host with the reference's formula and libm calls
+// (src/transformer/rope.c:19-37), so they are the same numbers.
+//
+// The current token, position and output index live in device memory, and a
+// step's kernels (GEMVs of gemv_pipe.cu and the kernels below) are captured
+// once into a CUDA graph per step kind (prompt step, generated step); a
+// generation is then a sequence of graph launches with no host round trip.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "internal.cuh"
+#include "../../include/sapphire_decode.h"
+
+namespace {
+
+constexpr int kNormThreads = 256;
+constexpr int kAttnSplit = 32;        // CTAs per layer's attention
+static_assert(kAttnSplit == 32, "the combine maps one split to one warp lane");
+constexpr int kAttnThreads = 256;
+constexpr int kMaxGroup = 8;          // query heads per KV head
+constexpr int kMaxHeads = 32;
+constexpr int kMaxHeadDim = 256;
+constexpr int kMaxChunk = (4096 + kAttnSplit - 1) / kAttnSplit;   // keys per CTA at the largest context
+constexpr int kMaxContext = 4096;
+constexpr int kArgmaxBlocks = 148;
+constexpr int kArgmaxThreads = 512;
+
+// Device-side step state.
+struct DecState {
+    int pos;            // position of the token being processed
+    int cur_token;      // token being processed
+    int prompt_index;   // index of cur_token in the prompt during the prompt phase
+    int n_prompt;
+    int gen_index;      // next output slot
+};
+
+// ------------------------------------------------------------ reductions --
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// Sum over the block (blockDim.x a multiple of 32, at most 1024); every thread
+// receives the result.  `red` holds 32 floats.
+__device__ float block_sum(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = lane < nw ? red[lane] : 0.0f;
+    return warp_sum(t);
+}
+
+// out[i] = (in[i] * rms_inv) * (1 + w[i]),  rms_inv = 1 / sqrt(mean(in^2) + eps)
+// (rmsnorm_delta, src/transformer/normalization.c:103-116).  One block; in and
+// out may alias.
+__device__ void rms_delta_block(const float *in, const float *w, float *out, int n, float eps, float *red) {
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += in[i] * in[i];
+    ss = block_sum(ss, red);
+    const float rms_inv = 1.0f / sqrtf(ss / (float)n + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float scale = 1.0f + (w ? w[i] : 0.0f);
+        out[i] = (in[i] * rms_inv) * scale;
+    }
+}
+
+// --------------------------------------------------------------- kernels --
+// hidden = embed[token] * sqrt(hidden); norm = rmsnorm_delta(hidden, w).
+__global__ void embed_norm_kernel(const DecState *st, const uint16_t *__restrict__ embed, int vocab, int dim,
+                                  float scale, const float *w, float eps, float *hidden, float *norm, int *err) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float red[32];
+    int tok = st->cur_token;
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0) atomicOr(err, 4);
+        tok = 0;
+    }
+    const uint16_t *row = embed + (size_t)tok * dim;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) hidden[i] = __uint_as_float((uint32_t)row[i] << 16) * scale;
+    __syncthreads();
+    rms_delta_block(hidden, w, norm, dim, eps, red);
+}
+
+// hidden += rmsnorm_delta(t, w_post); norm = rmsnorm_delta(hidden, w_next).
+__global__ void residual_norm_kernel(const float *t, const float *w_post, float *hidden, const float *w_next,
+                                     float *norm, int dim, float eps) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float red[32];
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss += t[i] * t[i];
+    ss = block_sum(ss, red);
+    const float rms_inv = 1.0f / sqrtf(ss / (float)dim + eps);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        const float n = (t[i] * rms_inv) * (1.0f + (w_post ? w_post[i] : 0.0f));
+        hidden[i] = hidden[i] + n;
+    }
+    __syncthreads();
+    rms_delta_block(hidden, w_next, norm, dim, eps, red);
+}
+
+// Per-head QK-norm and RoPE, then the cache write.  Blocks 0..heads-1: query
+// heads (in place in qkv); blocks heads..heads+kv_heads-1: key heads (normed,
+// rotated, written to K) and their value rows (copied to V).  head_dim / 2
+// threads; thread i owns the rotation pair (i, i + head_dim/2)
+// (rope_apply_fast, src/transformer/rope.c:65-80).
+__global__ void qk_rope_kv_kernel(const DecState *st, float *qkv, int heads, int kv_heads, int hd,
+                                  const float *q_norm, const float *k_norm, float eps, const float *rope_cos,
+                                  const float *rope_sin, float *kcache, float *vcache, int context) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float red[32];
+    const int pos = st->pos;
+    const int half = hd >> 1, i = threadIdx.x;
+    const bool is_q = blockIdx.x < heads;
+    const int kh = blockIdx.x - heads;
+    float *x = is_q ? qkv + (size_t)blockIdx.x * hd : qkv + (size_t)heads * hd + (size_t)kh * hd;
+    const float *w = is_q ? q_norm : k_norm;
+    const float x0 = x[i], x1 = x[i + half];
+    const float ss = block_sum(x0 * x0 + x1 * x1, red);
+    const float r = 1.0f / sqrtf(ss / (float)hd + eps);
+    const float y0 = (x0 * r) * (1.0f + (w ? w[i] : 0.0f));
+    const float y1 = (x1 * r) * (1.0f + (w ? w[i + half] : 0.0f));
+    const float c = rope_cos[(size_t)pos * hd + i], s = rope_sin[(size_t)pos * hd + i];
+    const float o0 = y0 * c - y1 * s;
+    const float o1 = y1 * c + y0 * s;
+    if (is_q) {
+        x[i] = o0;
+        x[i + half] = o1;
+    } else {
+        float *krow = kcache + ((size_t)kh * context + pos) * hd;
+        float *vrow = vcache + ((size_t)kh * context + pos) * hd;
+        const float *v = qkv + (size_t)(heads + kv_heads) * hd + (size_t)kh * hd;
+        krow[i] = o0;
+        krow[i + half] = o1;
+        vrow[i] = v[i];
+        vrow[i + half] = v[i + half];
+    }
+}
+
+// Attention of the current token over positions [start, pos] of one layer.
+// Grid: kAttnSplit blocks, each a contiguous key range for every KV head;
+// each block writes per query head its running max m, sum l and unnormalised
+// output acc = sum exp(s - m) v; the last block to finish combines the splits
+// in block order (deterministic) and resets the arrival counter.
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(
+    const DecState *st, const float *qkv, const float *kcache, const float *vcache, float *out, float *part,
+    int *counter, int heads, int kv_heads, int hd, int context, int window, int is_global, float scale) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float qs[kMaxGroup * kMaxHeadDim];
+    __shared__ float sc[kMaxGroup * kMaxChunk];
+    __shared__ float mh[kMaxGroup], lh[kMaxGroup];
+    __shared__ int last;
+    const int pos = st->pos;
+    const int seq = pos + 1;
+    const int start = (!is_global && seq > window) ? seq - window : 0;
+    const int len = seq - start;
+    const int chunk = (len + kAttnSplit - 1) / kAttnSplit;
+    const int k0 = start + blockIdx.x * chunk;
+    const int k1 = min(seq, k0 + chunk);
+    const int n = max(0, k1 - k0);
+    const int group = heads / kv_heads;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const size_t part_stride = (size_t)hd + 2;
+
+    for (int kh = 0; kh < kv_heads; ++kh) {
+        const float *kb = kcache + (size_t)kh * context * hd;
+        const float *vb = vcache + (size_t)kh * context * hd;
+        for (int j = threadIdx.x; j < group * hd; j += blockDim.x) qs[j] = qkv[(size_t)kh * group * hd + j];
+        __syncthreads();
+        // scores[h][t] = (q_h . k_t) * scale
+        for (int t = warp; t < n; t += nwarps) {
+            const float *krow = kb + (size_t)(k0 + t) * hd;
+            float acc[kMaxGroup];
+#pragma unroll
+            for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
+            for (int d = lane; d < hd; d += 32) {
+                const float kv = krow[d];
+#pragma unroll
+                for (int h = 0; h < kMaxGroup; ++h)
+                    if (h < group) acc[h] += qs[h * hd + d] * kv;
+            }
+#pragma unroll
+            for (int h = 0; h < kMaxGroup; ++h) {
+                if (h < group) {
+                    const float v = warp_sum(acc[h]);
+                    if (lane == 0) sc[h * kMaxChunk + t] = v * scale;
+                }
+            }
+        }
+        __syncthreads();
+        // per-head max and exp-sum over this block's keys (one warp per head)
+        for (int h = warp; h < group; h += nwarps) {
+            float m = -INFINITY;
+            for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[h * kMaxChunk + t]);
+            m = warp_max(m);
+            float l = 0.0f;
+            for (int t = lane; t < n; t += 32) {
+                const float p = n ? expf(sc[h * kMaxChunk + t] - m) : 0.0f;
+                sc[h * kMaxChunk + t] = p;
+                l += p;
+            }
+            l = warp_sum(l);
+            if (lane == 0) {
+                mh[h] = m;
+                lh[h] = l;
+            }
+        }
+        __syncthreads();
+        // acc[h][d] = sum_t p[h][t] v_t[d]
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+            float acc[kMaxGroup];
+#pragma unroll
+            for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
+            for (int t = 0; t < n; ++t) {
+                const float v = vb[(size_t)(k0 + t) * hd + d];
+#pragma unroll
+                for (int h = 0; h < kMaxGroup; ++h)
+                    if (h < group) acc[h] += sc[h * kMaxChunk + t] * v;
+            }
+#pragma unroll
+            for (int h = 0; h < kMaxGroup; ++h) {
+                if (h < group) {
+                    float *pp = part + ((size_t)(blockIdx.x * kv_heads + kh) * group + h) * part_stride;
+                    pp[2 + d] = acc[h];
+                }
+            }
+        }
+        if (threadIdx.x < group) {
+            float *pp = part + ((size_t)(blockIdx.x * kv_heads + kh) * group + threadIdx.x) * part_stride;
+            pp[0] = mh[threadIdx.x];
+            pp[1] = lh[threadIdx.x];
+        }
+        __syncthreads();
+    }
+
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // Combine: weight of split b for head h is exp(m_b - M) / sum_b' l_b' exp(m_b' - M)
+    // (one warp per head, lane = split), then out = sum_b weight_b acc_b.
+    __shared__ float wsplit[kMaxHeads * kAttnSplit];
+    for (int h = warp; h < heads; h += nwarps) {
+        const int kh = h / group, hh = h % group;
+        const float *pp = part + ((size_t)(lane * kv_heads + kh) * group + hh) * part_stride;
+        const float m = __ldcg(pp), l = __ldcg(pp + 1);
+        const float M = warp_max(m);
+        const float e = (m == -INFINITY) ? 0.0f : expf(m - M);
+        const float L = warp_sum(l * e);
+        wsplit[h * kAttnSplit + lane] = e / L;
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < heads * hd; j += blockDim.x) {
+        const int h = j / hd, d = j % hd;
+        const int kh = h / group, hh = h % group;
+        float O = 0.0f;
+#pragma unroll 8
+        for (int b = 0; b < kAttnSplit; ++b)
+            O += __ldcg(part + ((size_t)(b * kv_heads + kh) * group + hh) * part_stride + 2 + d) * wsplit[h * kAttnSplit + b];
+        out[j] = O;
+    }
+    if (threadIdx.x == 0) *counter = 0;
+}
+
+// act[i] = gelu(gate[i]) * up[i], tanh form (src/transformer/activations.c:64-82).
+__global__ void geglu_kernel(const float *gu, float *act, int ffn) {
+    pdl_trigger();
+    pdl_wait();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ffn; i += gridDim.x * blockDim.x) {
+        const float x = gu[i];
+        const float y = 0.7978845608f * (x + 0.044715f * x * x * x);
+        const float g = 0.5f * x * (1.0f + tanhf(y));
+        act[i] = g * gu[ffn + i];
+    }
+}
+
+// Top-1 (value, lowest index on ties) and top-2 value.
+struct Top2 {
+    float v1;
+    int i1;
+    float v2;
+};
+__device__ __forceinline__ void top2_push(Top2 &a, float v, int i) {
+    if (v > a.v1 || (v == a.v1 && i < a.i1)) {
+        a.v2 = fmaxf(a.v2, a.v1);
+        a.v1 = v;
+        a.i1 = i;
+    } else if (v > a.v2) {
+        a.v2 = v;
+    }
+}
+__device__ __forceinline__ Top2 top2_merge(const Top2 &a, const Top2 &b) {
+    const bool b_first = b.v1 > a.v1 || (b.v1 == a.v1 && b.i1 < a.i1);
+    Top2 r;
+    if (b_first) {
+        r.v1 = b.v1;
+        r.i1 = b.i1;
+        r.v2 = fmaxf(b.v2, a.v1);
+    } else {
+        r.v1 = a.v1;
+        r.i1 = a.i1;
+        r.v2 = fmaxf(a.v2, b.v1);
+    }
+    return r;
+}
+__device__ Top2 block_top2(Top2 t, Top2 *sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Top2 u;
+        u.v1 = __shfl_xor_sync(0xffffffffu, t.v1, o);
+        u.i1 = __shfl_xor_sync(0xffffffffu, t.i1, o);
+        u.v2 = __shfl_xor_sync(0xffffffffu, t.v2, o);
+        t = top2_merge(t, u);
+    }
+    __syncthreads();
+    if (lane == 0) sh[warp] = t;
+    __syncthreads();
+    Top2 r = sh[0];
+    for (int w = 1; w < nw; ++w) r = top2_merge(r, sh[w]);
+    return r;
+}
+
+// Greedy token of the logits; the last block writes it as the next input,
+// records it (and the top-1 minus top-2 margin) and advances the position.
+__global__ void argmax_advance_kernel(const float *logits, int n, Top2 *part, int *counter, DecState *st,
+                                      int *out_tokens, float *out_margins) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ Top2 sh[32];
+    __shared__ int last;
+    Top2 t{-INFINITY, 0x7fffffff, -INFINITY};
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) top2_push(t, logits[i], i);
+    t = block_top2(t, sh);
+    if (threadIdx.x == 0) {
+        part[blockIdx.x] = t;
+        __threadfence();
+        last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    Top2 r{-INFINITY, 0x7fffffff, -INFINITY};
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
+        Top2 u;
+        u.v1 = __ldcg(&part[b].v1);
+        u.i1 = __ldcg(&part[b].i1);
+        u.v2 = __ldcg(&part[b].v2);
+        r = top2_merge(r, u);
+    }
+    r = block_top2(r, sh);
+    if (threadIdx.x == 0) {
+        const int tok = (r.i1 >= 0 && r.i1 < n) ? r.i1 : 0;
+        const int g = st->gen_index;
+        out_tokens[g] = tok;
+        out_margins[g] = r.v1 - r.v2;
+        st->gen_index = g + 1;
+        st->cur_token = tok;
+        st->pos = st->pos + 1;
+        *counter = 0;
+    }
+}
+
+// Prompt phase: the next prompt token becomes the input at the next position.
+__global__ void prompt_advance_kernel(DecState *st, const int *prompt) {
+    pdl_trigger();
+    pdl_wait();
+    const int i = st->prompt_index + 1;
+    st->prompt_index = i;
+    st->pos = st->pos + 1;
+    if (i < st->n_prompt) st->cur_token = prompt[i];
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- the engine --
+struct sapphire_decoder {
+    kernel_context_t *ctx = nullptr;
+    sapphire_gemma3_config_t cfg{};
+    int q_dim = 0, kv_dim = 0;
+
+    // Host copies backing the uploaded weights (tensor views over them).
+    std::vector<std::vector<uint8_t>> host;
+    std::vector<tensor_t *> tensors;
+    struct Layer {
+        tensor_t *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+        float *w_attn = nullptr, *w_attn_post = nullptr, *w_ffn = nullptr, *w_ffn_post = nullptr;
+        float *w_q = nullptr, *w_k = nullptr;
+        bool global = false;
+    };
+    std::vector<Layer> layers;
+    tensor_t *lm_head = nullptr;
+    float *w_final = nullptr;
+
+    // Device buffers.
+    uint16_t *embed = nullptr;
+    float *rope_cos_g = nullptr, *rope_sin_g = nullptr, *rope_cos_l = nullptr, *rope_sin_l = nullptr;
+    float *kcache = nullptr, *vcache = nullptr;
+    float *hidden = nullptr, *norm = nullptr, *qkv = nullptr, *attn = nullptr, *tmp = nullptr, *gu = nullptr,
+          *act = nullptr, *logits = nullptr, *attn_part = nullptr;
+    void *top2_part = nullptr;
+    int *counters = nullptr;        // [0] attention, [1] argmax
+    DecState *state = nullptr;
+    int *prompt = nullptr, *out_tokens = nullptr;
+    float *out_margins = nullptr;
+    std::vector<void *> allocations;
+
+    cudaGraphExec_t g_prompt = nullptr, g_gen = nullptr;
+    int launches_prompt = 0, launches_gen = 0;
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    float last_prompt_ms = 0, last_gen_ms = 0;
+};
+
+namespace {
+
+int dev_alloc(sapphire_decoder_t *d, void **p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+    if (e != cudaSuccess) {
+        ctx_fail(d->ctx, "sapphire_decoder_create", "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+        return -1;
+    }
+    d->allocations.push_back(*p);
+    return 0;
+}
+
+int upload_floats(sapphire_decoder_t *d, float **dst, const float *src, size_t n) {
+    if (dev_alloc(d, (void **)dst, n * sizeof(float))) return -1;
+    cudaError_t e = src ? cudaMemcpy(*dst, src, n * sizeof(float), cudaMemcpyHostToDevice)
+                        : cudaMemset(*dst, 0, n * sizeof(float));
+    if (e != cudaSuccess) {
+        ctx_fail(d->ctx, "sapphire_decoder_create", "norm weight upload failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+// A Q4_0 tensor over the concatenation of `parts` (rows back to back),
+// uploaded to the context.
+tensor_t *concat_q4(sapphire_decoder_t *d, const std::vector<std::pair<const void *, int>> &parts, int cols) {
+    const size_t rb = sapphire_row_bytes_internal(DTYPE_Q4_0, cols);
+    int rows = 0;
+    for (auto &p : parts) rows += p.second;
+    d->host.emplace_back((size_t)rows * rb);
+    std::vector<uint8_t> &buf = d->host.back();
+    size_t off = 0;
+    for (auto &p : parts) {
+        if (!p.first) {
+            ctx_fail(d->ctx, "sapphire_decoder_create", "a projection pointer is NULL");
+            return nullptr;
+        }
+        memcpy(buf.data() + off, p.first, (size_t)p.second * rb);
+        off += (size_t)p.second * rb;
+    }
+    int shape[2] = {rows, cols};
+    tensor_t *t = tensor_create_view(DTYPE_Q4_0, 2, shape, buf.data());
+    if (!t) {
+        ctx_fail(d->ctx, "sapphire_decoder_create", "tensor_create_view failed");
+        return nullptr;
+    }
+    d->tensors.push_back(t);
+    if (kernel_tensor_upload(d->ctx, t) != 0) return nullptr;
+    return t;
+}
+
+const DevWeight *weight_of(sapphire_decoder_t *d, tensor_t *t) { return ctx_weight(d->ctx, t); }
+
+// The reference's table (rope_precompute_freqs, src/transformer/rope.c:19-37):
+// half-split storage, cos / sin of pos * base^(-2m/d) in float.
+void rope_table(std::vector<float> &c, std::vector<float> &s, int hd, int context, float base) {
+    const int half = hd / 2;
+    c.assign((size_t)context * hd, 0.0f);
+    s.assign((size_t)context * hd, 0.0f);
+    for (int pos = 0; pos < context; ++pos) {
+        for (int m = 0; m < half; ++m) {
+            const float freq = 1.0f / powf(base, 2.0f * (float)m / (float)hd);
+            const float angle = (float)pos * freq;
+            const float cv = cosf(angle), sv = sinf(angle);
+            c[(size_t)pos * hd + m] = cv;
+            c[(size_t)pos * hd + m + half] = cv;
+            s[(size_t)pos * hd + m] = sv;
+            s[(size_t)pos * hd + m + half] = sv;
+        }
+    }
+}
+
+int check_launch(sapphire_decoder_t *d, const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        ctx_fail(d->ctx, "sapphire_decoder", "%s launch failed: %s", what, cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+// Enqueue one step: embedding, the layers and either the prompt advance or
+// the LM head + greedy argmax.  Returns the number of kernels, -1 on error.
+int enqueue_step(sapphire_decoder_t *d, bool generate, cudaStream_t st) {
+    const sapphire_gemma3_config_t &c = d->cfg;
+    kernel_context_t *ctx = d->ctx;
+    int launches = 0;
+    const float eps = c.rms_eps;
+    const float emb_scale = sqrtf((float)c.hidden);
+    const float att_scale = 1.0f / sqrtf(c.query_pre_attn_scalar > 0.0f ? c.query_pre_attn_scalar : (float)c.head_dim);
+
+    launch_pdl(embed_norm_kernel, dim3(1), dim3(kNormThreads), 0, st, (const DecState *)d->state,
+               (const uint16_t *)d->embed, c.vocab, c.hidden, emb_scale, (const float *)d->layers[0].w_attn, eps,
+               d->hidden, d->norm, ctx->d_err);
+    if (check_launch(d, "embedding")) return -1;
+    ++launches;
+    for (int l = 0; l < c.layers; ++l) {
+        sapphire_decoder::Layer &L = d->layers[l];
+        const DevWeight *qkv = weight_of(d, L.qkv), *o = weight_of(d, L.o), *gu = weight_of(d, L.gu),
+                        *down = weight_of(d, L.down);
+        if (!qkv || !o || !gu || !down) return -1;
+        if (launch_gemv_best(ctx, *qkv, d->norm, d->qkv, st)) return -1;
+        launch_pdl(qk_rope_kv_kernel, dim3(c.heads + c.kv_heads), dim3(c.head_dim / 2), 0, st,
+                   (const DecState *)d->state, d->qkv, c.heads, c.kv_heads, c.head_dim, (const float *)L.w_q,
+                   (const float *)L.w_k, eps, (const float *)(L.global ? d->rope_cos_g : d->rope_cos_l),
+                   (const float *)(L.global ? d->rope_sin_g : d->rope_sin_l),
+                   d->kcache + (size_t)l * c.kv_heads * c.context * c.head_dim,
+                   d->vcache + (size_t)l * c.kv_heads * c.context * c.head_dim, c.context);
+        if (check_launch(d, "qk-norm/rope")) return -1;
+        launch_pdl(attention_kernel, dim3(kAttnSplit), dim3(kAttnThreads), 0, st, (const DecState *)d->state,
+                   (const float *)d->qkv, (const float *)(d->kcache + (size_t)l * c.kv_heads * c.context * c.head_dim),
+                   (const float *)(d->vcache + (size_t)l * c.kv_heads * c.context * c.head_dim), d->attn,
+                   d->attn_part, d->counters, c.heads, c.kv_heads, c.head_dim, c.context,
+                   c.sliding_window > 0 ? c.sliding_window : 1024, L.global ? 1 : 0, att_scale);
+        if (check_launch(d, "attention")) return -1;
+        if (launch_gemv_best(ctx, *o, d->attn, d->tmp, st)) return -1;
+        launch_pdl(residual_norm_kernel, dim3(1), dim3(kNormThreads), 0, st, (const float *)d->tmp,
+                   (const float *)L.w_attn_post, d->hidden, (const float *)L.w_ffn, d->norm, c.hidden, eps);
+        if (check_launch(d, "attention residual")) return -1;
+        if (launch_gemv_best(ctx, *gu, d->norm, d->gu, st)) return -1;
+        launch_pdl(geglu_kernel, dim3((c.ffn + 255) / 256), dim3(256), 0, st, (const float *)d->gu, d->act, c.ffn);
+        if (check_launch(d, "geglu")) return -1;
+        if (launch_gemv_best(ctx, *down, d->act, d->tmp, st)) return -1;
+        const float *w_next = (l + 1 < c.layers) ? d->layers[l + 1].w_attn : d->w_final;
+        launch_pdl(residual_norm_kernel, dim3(1), dim3(kNormThreads), 0, st, (const float *)d->tmp,
+                   (const float *)L.w_ffn_post, d->hidden, w_next, d->norm, c.hidden, eps);
+        if (check_launch(d, "ffn residual")) return -1;
+        launches += 9;
+    }
+    if (generate) {
+        const DevWeight *head = weight_of(d, d->lm_head);
+        if (!head) return -1;
+        if (launch_gemv_best(ctx, *head, d->norm, d->logits, st)) return -1;
+        launch_pdl(argmax_advance_kernel, dim3(kArgmaxBlocks), dim3(kArgmaxThreads), 0, st, (const float *)d->logits,
+                   c.vocab, reinterpret_cast<Top2 *>(d->top2_part), d->counters + 1, d->state, d->out_tokens,
+                   d->out_margins);
+        if (check_launch(d, "argmax")) return -1;
+        launches += 2;
+    } else {
+        launch_pdl(prompt_advance_kernel, dim3(1), dim3(1), 0, st, d->state, (const int *)d->prompt);
+        if (check_launch(d, "prompt advance")) return -1;
+        launches += 1;
+    }
+    return launches;
+}
+
+int capture(sapphire_decoder_t *d, bool generate, cudaGraphExec_t *exec, int *launches) {
+    cudaStream_t st = d->ctx->stream;
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) {
+        ctx_fail(d->ctx, "sapphire_decoder_create", "stream capture failed to start: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    const int n = enqueue_step(d, generate, st);
+    e = cudaStreamEndCapture(st, &g);
+    if (n < 0 || e != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        if (n >= 0) ctx_fail(d->ctx, "sapphire_decoder_create", "stream capture failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    e = cudaGraphInstantiate(exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+        ctx_fail(d->ctx, "sapphire_decoder_create", "graph instantiation failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    *launches = n;
+    return 0;
+}
+
+int set_state(sapphire_decoder_t *d, int first_token, int n_prompt, cudaStream_t st) {
+    DecState s{0, first_token, 0, n_prompt, 0};
+    CUDA_TRY(d->ctx, cudaMemcpyAsync(d->state, &s, sizeof s, cudaMemcpyHostToDevice, st));
+    return 0;
+}
+
+}  // namespace
+
+extern "C" SAPPHIRE_API void sapphire_decoder_destroy(sapphire_decoder_t *d) {
+    if (!d) return;
+    {
+        std::lock_guard<std::recursive_mutex> lk(d->ctx->exec_mutex);
+        int prev = -1;
+        cudaGetDevice(&prev);
+        cudaSetDevice(d->ctx->device);
+        cudaStreamSynchronize(d->ctx->stream);
+        if (d->g_prompt) cudaGraphExecDestroy(d->g_prompt);
+        if (d->g_gen) cudaGraphExecDestroy(d->g_gen);
+        for (cudaEvent_t e : d->ev)
+            if (e) cudaEventDestroy(e);
+        for (void *p : d->allocations) cudaFree(p);
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+    for (tensor_t *t : d->tensors) tensor_release(t);   // drops the device copies
+    delete d;
+}
+
+extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_context_t *ctx,
+                                                                    const sapphire_gemma3_config_t *cfg,
+                                                                    const sapphire_gemma3_weights_t *w) {
+    if (!ctx || !cfg || !w || !w->embed_bf16 || !w->lm_head || !w->proj) {
+        LOG_ERROR("sapphire_decoder_create: NULL argument");
+        return nullptr;
+    }
+    const sapphire_gemma3_config_t &c = *cfg;
+    if (c.layers <= 0 || c.hidden <= 0 || c.ffn <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.heads % c.kv_heads ||
+        c.heads / c.kv_heads > kMaxGroup || c.heads > kMaxHeads || c.head_dim <= 0 || c.head_dim > kMaxHeadDim || c.head_dim % 64 ||
+        c.vocab <= 0 || c.context <= 0 || c.context > kMaxContext || c.rms_eps < 0.0f) {
+        ctx_fail(ctx, "sapphire_decoder_create",
+                 "unsupported shape (heads %% kv_heads == 0, group <= %d, head_dim a multiple of 64 up to %d, "
+                 "context <= %d)", kMaxGroup, kMaxHeadDim, kMaxContext);
+        return nullptr;
+    }
+    std::lock_guard<std::recursive_mutex> lk(ctx->exec_mutex);
+    if (!ctx->initialized || ctx->world > 1) {
+        ctx_fail(ctx, "sapphire_decoder_create", "needs an initialized, unsharded context");
+        return nullptr;
+    }
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ctx->device);
+    sapphire_decoder_t *d = new sapphire_decoder();
+    d->ctx = ctx;
+    d->cfg = c;
+    d->q_dim = c.heads * c.head_dim;
+    d->kv_dim = c.kv_heads * c.head_dim;
+    bool ok = false;
+    do {
+        d->layers.resize(c.layers);
+        for (int l = 0; l < c.layers; ++l) {
+            const void *const *p = w->proj + 7 * l;
+            sapphire_decoder::Layer &L = d->layers[l];
+            L.global = c.global_mask ? ((c.global_mask >> l) & 1ULL) != 0 : ((l + 1) % 6 == 0);
+            if (!(L.qkv = concat_q4(d, {{p[0], d->q_dim}, {p[1], d->kv_dim}, {p[2], d->kv_dim}}, c.hidden))) break;
+            if (!(L.o = concat_q4(d, {{p[3], c.hidden}}, d->q_dim))) break;
+            if (!(L.gu = concat_q4(d, {{p[4], c.ffn}, {p[5], c.ffn}}, c.hidden))) break;
+            if (!(L.down = concat_q4(d, {{p[6], c.hidden}}, c.ffn))) break;
+            const float *const *nw = w->norms ? w->norms + 6 * l : nullptr;
+            if (upload_floats(d, &L.w_attn, nw ? nw[0] : nullptr, c.hidden) ||
+                upload_floats(d, &L.w_attn_post, nw ? nw[1] : nullptr, c.hidden) ||
+                upload_floats(d, &L.w_ffn, nw ? nw[2] : nullptr, c.hidden) ||
+                upload_floats(d, &L.w_ffn_post, nw ? nw[3] : nullptr, c.hidden) ||
+                upload_floats(d, &L.w_q, nw ? nw[4] : nullptr, c.head_dim) ||
+                upload_floats(d, &L.w_k, nw ? nw[5] : nullptr, c.head_dim))
+                break;
+            if (l + 1 == c.layers) ok = true;
+        }
+        if (!ok) break;
+        ok = false;
+        if (!(d->lm_head = concat_q4(d, {{w->lm_head, c.vocab}}, c.hidden))) break;
+        if (upload_floats(d, &d->w_final, w->final_norm, c.hidden)) break;
+        const size_t emb = (size_t)c.vocab * c.hidden;
+        if (dev_alloc(d, (void **)&d->embed, emb * 2)) break;
+        if (cudaMemcpy(d->embed, w->embed_bf16, emb * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
+            ctx_fail(ctx, "sapphire_decoder_create", "embedding upload failed");
+            break;
+        }
+        std::vector<float> cs, sn;
+        const size_t rope_n = (size_t)c.context * c.head_dim;
+        rope_table(cs, sn, c.head_dim, c.context, c.rope_theta);
+        if (upload_floats(d, &d->rope_cos_g, cs.data(), rope_n) || upload_floats(d, &d->rope_sin_g, sn.data(), rope_n))
+            break;
+        rope_table(cs, sn, c.head_dim, c.context, c.rope_local_theta);
+        if (upload_floats(d, &d->rope_cos_l, cs.data(), rope_n) || upload_floats(d, &d->rope_sin_l, sn.data(), rope_n))
+            break;
+        const size_t kv = (size_t)c.layers * c.kv_heads * c.context * c.head_dim;
+        if (upload_floats(d, &d->kcache, nullptr, kv) || upload_floats(d, &d->vcache, nullptr, kv)) break;
+        if (dev_alloc(d, (void **)&d->hidden, c.hidden * 4) || dev_alloc(d, (void **)&d->norm, c.hidden * 4) ||
+            dev_alloc(d, (void **)&d->qkv, (size_t)(d->q_dim + 2 * d->kv_dim) * 4) ||
+            dev_alloc(d, (void **)&d->attn, (size_t)d->q_dim * 4) ||
+            dev_alloc(d, (void **)&d->tmp, (size_t)c.hidden * 4) ||
+            dev_alloc(d, (void **)&d->gu, (size_t)2 * c.ffn * 4) || dev_alloc(d, (void **)&d->act, (size_t)c.ffn * 4) ||
+            dev_alloc(d, (void **)&d->logits, (size_t)c.vocab * 4) ||
+            dev_alloc(d, (void **)&d->attn_part, (size_t)kAttnSplit * c.heads * (c.head_dim + 2) * 4) ||
+            dev_alloc(d, &d->top2_part, (size_t)kArgmaxBlocks * sizeof(Top2)) ||
+            dev_alloc(d, (void **)&d->state, sizeof(DecState)) ||
+            dev_alloc(d, (void **)&d->prompt, (size_t)c.context * 4) ||
+            dev_alloc(d, (void **)&d->out_tokens, (size_t)c.context * 4) ||
+            dev_alloc(d, (void **)&d->out_margins, (size_t)c.context * 4))
+            break;
+        if (dev_alloc(d, (void **)&d->counters, 16) || cudaMemset(d->counters, 0, 16) != cudaSuccess) break;
+        // Scratch of the GEMVs sized for the largest weight, before capture.
+        size_t pf = 0, ci = 0;
+        std::vector<tensor_t *> all = {d->lm_head};
+        for (auto &L : d->layers) all.insert(all.end(), {L.qkv, L.o, L.gu, L.down});
+        for (tensor_t *t : all) {
+            const DevWeight *dw = weight_of(d, t);
+            if (!dw) break;
+            size_t a = 0, b = 0;
+            pipe_scratch_size(ctx, *dw, &a, &b);
+            pf = std::max(pf, a);
+            ci = std::max(ci, b);
+        }
+        if (ensure_pipe_scratch(ctx, pf, ci)) break;
+        // One eager pass of each step kind (also checks every launch), then capture.
+        cudaStream_t st = ctx->stream;
+        if (set_state(d, 0, 1, st) || enqueue_step(d, false, st) < 0 || enqueue_step(d, true, st) < 0) break;
+        if (cudaStreamSynchronize(st) != cudaSuccess || check_kernel_error(ctx, "sapphire_decoder_create")) {
+            ctx_fail(ctx, "sapphire_decoder_create", "warm-up step failed");
+            break;
+        }
+        if (capture(d, false, &d->g_prompt, &d->launches_prompt) ||
+            capture(d, true, &d->g_gen, &d->launches_gen))
+            break;
+        bool evs = true;
+        for (cudaEvent_t &e : d->ev) evs = evs && cudaEventCreate(&e) == cudaSuccess;
+        if (!evs) break;
+        ok = true;
+    } while (false);
+    if (prev >= 0) cudaSetDevice(prev);
+    if (!ok) {
+        cudaGetLastError();
+        sapphire_decoder_destroy(d);
+        return nullptr;
+    }
+    return d;
+}
+
+extern "C" SAPPHIRE_API int sapphire_decoder_generate(sapphire_decoder_t *d, const int *prompt, int n_prompt,
+                                                      int n_gen, int *out_ids, float *out_margins) {
+    if (!d || !prompt || n_prompt < 1 || n_gen < 0 || (n_gen && !out_ids)) {
+        LOG_ERROR("sapphire_decoder_generate: bad arguments");
+        return -1;
+    }
+    kernel_context_t *ctx = d->ctx;
+    std::lock_guard<std::recursive_mutex> lk(ctx->exec_mutex);
+    if (n_prompt + n_gen > d->cfg.context) {
+        ctx_fail(ctx, "sapphire_decoder_generate", "prompt %d + generated %d exceed the context %d", n_prompt, n_gen,
+                 d->cfg.context);
+        return -1;
+    }
+    for (int i = 0; i < n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= d->cfg.vocab) {
+            ctx_fail(ctx, "sapphire_decoder_generate", "prompt token %d out of range", prompt[i]);
+            return -1;
+        }
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ctx->device);
+    cudaStream_t st = ctx->stream;
+    int rc = -1;
+    do {
+        if (cudaMemcpyAsync(d->prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) break;
+        if (set_state(d, prompt[0], n_prompt, st)) break;
+        if (cudaEventRecord(d->ev[0], st) != cudaSuccess) break;
+        bool ok = true;
+        for (int i = 0; ok && i + 1 < n_prompt; ++i) ok = cudaGraphLaunch(d->g_prompt, st) == cudaSuccess;
+        ok = ok && cudaEventRecord(d->ev[1], st) == cudaSuccess;
+        for (int i = 0; ok && i < n_gen; ++i) ok = cudaGraphLaunch(d->g_gen, st) == cudaSuccess;
+        ok = ok && cudaEventRecord(d->ev[2], st) == cudaSuccess;
+        if (!ok) {
+            ctx_fail(ctx, "sapphire_decoder_generate", "graph launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+            break;
+        }
+        if (n_gen) {
+            if (cudaMemcpyAsync(out_ids, d->out_tokens, (size_t)n_gen * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                break;
+            if (out_margins &&
+                cudaMemcpyAsync(out_margins, d->out_margins, (size_t)n_gen * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                break;
+        }
+        cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) {
+            ctx_fail(ctx, "sapphire_decoder_generate", "GPU execution failed: %s", cudaGetErrorString(e));
+            break;
+        }
+        if (check_kernel_error(ctx, "sapphire_decoder_generate")) break;
+        cudaEventElapsedTime(&d->last_prompt_ms, d->ev[0], d->ev[1]);
+        cudaEventElapsedTime(&d->last_gen_ms, d->ev[1], d->ev[2]);
+        rc = 0;
+    } while (false);
+    if (rc) cudaGetLastError();
+    if (prev >= 0) cudaSetDevice(prev);
+    return rc;
+}
+
+extern "C" SAPPHIRE_API int sapphire_decoder_last_logits(sapphire_decoder_t *d, float *out) {
+    if (!d || !out) return -1;
+    std::lock_guard<std::recursive_mutex> lk(d->ctx->exec_mutex);
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(d->ctx->device);
+    cudaError_t e = cudaMemcpyAsync(out, d->logits, (size_t)d->cfg.vocab * 4, cudaMemcpyDefault, d->ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->ctx->stream);
+    if (prev >= 0) cudaSetDevice(prev);
+    if (e != cudaSuccess) {
+        ctx_fail(d->ctx, "sapphire_decoder_last_logits", "copy failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+extern "C" SAPPHIRE_API int sapphire_decoder_last_times(sapphire_decoder_t *d, float *prompt_ms, float *generate_ms) {
+    if (!d) return -1;
+    if (prompt_ms) *prompt_ms = d->last_prompt_ms;
+    if (generate_ms) *generate_ms = d->last_gen_ms;
+    return 0;
+}
+
+extern "C" SAPPHIRE_API int sapphire_decoder_launches_per_token(sapphire_decoder_t *d) {
+    return d ? d->launches_gen : -1;
+}

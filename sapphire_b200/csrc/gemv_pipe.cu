@@ -685,14 +685,18 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_pipe(const PipeParams p) {
         if (sbytes) bulk_g2s(dst + code_bytes<DT>(), p.scales + ((size_t)tile * p.nb + u0) * 32, sbytes, bars + stage);
     };
 
+    pdl_trigger();
     if (threadIdx.x == 0) s_nonfinite = 0;
     if (lane == 0) {
         for (int s = 0; s < NS; ++s) mbar_init(bars + s, 1);
         fence_mbar_init();
     }
     __syncwarp();
+    // The weight copies do not depend on earlier kernels: they start before
+    // the wait for the kernel that produced x.
     if (lane == 0)
         for (int j = 0; j < NS && j < n_items; ++j) issue(j);
+    pdl_wait();
     __syncthreads();   // s_nonfinite initialised before x preparation writes it
 
     // x image, built once per CTA while the first copies are in flight.
@@ -808,16 +812,34 @@ int sm_count(int dev) {
     return cached[dev];
 }
 
+// Raises a kernel's dynamic shared-memory opt-in on the context's device only
+// when a launch needs more than was set before, so repeated launches (and
+// launches recorded into a CUDA graph after a first eager one) make no
+// attribute call.
+template <typename K>
+cudaError_t ensure_smem_optin(K kernel, int device, size_t smem) {
+    static std::mutex mu;
+    static std::unordered_map<const void *, size_t> set[64];
+    if (device < 0 || device >= 64)
+        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    std::lock_guard<std::mutex> lk(mu);
+    size_t &cur = set[device][reinterpret_cast<const void *>(kernel)];
+    if (smem <= cur) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) cur = smem;
+    return e;
+}
+
 template <tensor_dtype_t DT>
 int launch_cfg(kernel_context_t *ctx, const PipeParams &p, PipeCfg c, int grid, size_t smem, cudaStream_t st) {
     auto run = [&](auto kernel, int threads) -> int {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = ensure_smem_optin(kernel, ctx->device, smem);
         if (e != cudaSuccess) {
             ctx_fail(ctx, "launch_gemv_pipe", "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
             return -1;
         }
-        kernel<<<grid, threads, smem, st>>>(p);
-        e = cudaGetLastError();
+        e = launch_pdl(kernel, dim3(grid), dim3(threads), smem, st, p);
+        if (e == cudaSuccess) e = cudaGetLastError();
         if (e != cudaSuccess) {
             ctx_fail(ctx, "launch_gemv_pipe", "launch failed: %s", cudaGetErrorString(e));
             return -1;
@@ -881,7 +903,10 @@ int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, 
     p.kchunks = w.kchunks;
     p.nseg = item_nseg(w);
     p.total_items = (long long)w.ntiles * p.nseg;
-    const int grid = sm_count(ctx->device);
+    // One CTA per SM, or fewer when the weight has fewer items than a full
+    // grid has warps (small decode projections): every warp gets work.
+    const long long want = (p.total_items + c.nw - 1) / c.nw;
+    const int grid = (int)std::min<long long>(sm_count(ctx->device), std::max<long long>(1, want));
     p.total_warps = grid * c.nw;
     p.kmax = pipe_kmax(p.total_items, p.total_warps, p.nseg);
     const size_t smem = pipe_smem(w.dtype, w.nb, w.kchunks, c);

@@ -10,6 +10,7 @@
 #include <thread>
 #include <condition_variable>
 #include <atomic>
+#include <utility>
 
 #include "common.h"
 
@@ -104,6 +105,35 @@ struct sapphire_context {
 
     std::string last_error;
 };
+
+// ------------------------------------------------ programmatic dependent launch
+// Kernels launched with launch_pdl may start while the previous kernel on the
+// stream is still running.  Each such kernel calls pdl_trigger() early (its
+// own dependents may then be scheduled) and pdl_wait() before it reads what an
+// earlier kernel wrote or writes what one may still read; pdl_wait returns
+// once the previous grid has completed and its memory is visible.  Every
+// kernel launched this way calls pdl_wait (so completion is transitive).
+// Outside such a launch both are no-ops.
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+#endif
 
 // ------------------------------------------------------------------ helpers
 // Record an error on the context (if any) and log it.

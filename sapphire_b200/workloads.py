@@ -8,6 +8,7 @@ U(0.01, 0.1).  No dataset is involved.
 """
 from __future__ import annotations
 
+import hashlib
 from dataclasses import dataclass
 
 import numpy as np
@@ -70,3 +71,84 @@ def pad_cols(x: np.ndarray, cols: int) -> np.ndarray:
     out = np.zeros(x.shape[:-1] + (padded,), dtype=np.float32)
     out[..., :x.shape[-1]] = x
     return out
+
+
+# ------------------------------------------------------------------ decode --
+@dataclass(frozen=True)
+class DecodeConfig:
+    """Gemma-3-270M decode workload (random-init).  Shapes follow the model:
+    18 layers, hidden 640, FFN 2048 (GeGLU), 4 query heads / 1 KV head of
+    dimension 256, vocabulary 262144.  sliding_window is chosen here (the
+    model's own 512; the benchmark names none) so the last generated tokens
+    of the local layers attend to a window."""
+    name: str = "gemma3_270m_decode"
+    layers: int = 18
+    hidden: int = 640
+    ffn: int = 2048
+    heads: int = 4
+    kv_heads: int = 1
+    head_dim: int = 256
+    vocab: int = 262144
+    prompt: int = 512
+    generate: int = 64
+    context: int = 2048
+    sliding_window: int = 512
+    rope_theta: float = 1.0e6
+    rope_local_theta: float = 1.0e4
+    query_pre_attn_scalar: float = 256.0
+    rms_eps: float = 1e-6
+
+    def is_global(self, layer: int) -> bool:
+        return (layer + 1) % 6 == 0
+
+    def projections(self):
+        """(name, rows, cols) of one layer's Q4_0 projections, in draw order."""
+        q = self.heads * self.head_dim
+        kv = self.kv_heads * self.head_dim
+        return [("q", q, self.hidden), ("k", kv, self.hidden), ("v", kv, self.hidden),
+                ("o", self.hidden, q), ("gate", self.ffn, self.hidden), ("up", self.ffn, self.hidden),
+                ("down", self.hidden, self.ffn)]
+
+
+C3 = DecodeConfig()
+
+
+def bf16_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bit patterns (uint16), round to nearest even (finite values)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def make_decode_model(cfg: DecodeConfig, quantize, seed: int = 0):
+    """Seeded random-init Gemma-3 weights and prompt.
+
+    Draw order (PCG64 `seed`): prompt ids (cfg.prompt integers in [0, vocab)),
+    the embedding table N(0, 0.02) [vocab, hidden] stored as bf16, then for
+    each layer q, k, v, o, gate, up, down N(0, 0.02) [rows, cols], then the LM
+    head N(0, 0.02) [vocab, hidden].  Projections and LM head are packed Q4_0
+    by `quantize(fp32 [rows, cols]) -> packed bytes`.  Norm weights are zero
+    (RMSNorm with (1 + w) scaling: scale 1).
+
+    Returns dict(prompt=int32 [prompt], embed=uint16 [vocab*hidden],
+    layers=[{name: packed bytes}], lm_head=packed bytes)."""
+    rng = np.random.default_rng(seed)
+    prompt = rng.integers(0, cfg.vocab, size=cfg.prompt, dtype=np.int64).astype(np.int32)
+    embed = bf16_bits(normal_weights(rng, cfg.vocab, cfg.hidden)).reshape(-1)
+    layers = []
+    for _ in range(cfg.layers):
+        layers.append({name: quantize(normal_weights(rng, rows, cols)) for name, rows, cols in cfg.projections()})
+    lm_head = quantize(normal_weights(rng, cfg.vocab, cfg.hidden))
+    return {"prompt": prompt, "embed": embed, "layers": layers, "lm_head": lm_head}
+
+
+def model_digest(model) -> str:
+    """sha256 over the prompt and samples of the model's bytes (embedding head,
+    first and last projection, LM head tail): detects a change of the
+    generator or the quantiser."""
+    h = hashlib.sha256()
+    h.update(model["prompt"].tobytes())
+    h.update(model["embed"][:1 << 20].tobytes())
+    h.update(model["layers"][0]["q"].tobytes())
+    h.update(model["layers"][-1]["down"].tobytes())
+    h.update(model["lm_head"][-(1 << 20):].tobytes())
+    return h.hexdigest()

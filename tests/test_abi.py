@@ -4,6 +4,7 @@ like the reference (src/tensor/tensor.c, src/kernels/dispatch.c)."""
 from __future__ import annotations
 
 import ctypes as C
+import glob
 import os
 import re
 import subprocess
@@ -13,7 +14,7 @@ import pytest
 
 from conftest import ROOT
 
-HEADERS = [os.path.join(ROOT, "include", h) for h in ("tensor.h", "kernels.h", "sapphire_cuda.h")]
+HEADERS = sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 # Every function of the reference's hot-path headers (include/kernels.h:56-166,
 # include/tensor.h:60-208) that a drop-in must export.
