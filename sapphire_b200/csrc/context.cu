@@ -322,6 +322,7 @@ int ensure_pipe_scratch(kernel_context_t *ctx, size_t part_floats, size_t cnt_in
 }
 
 int launch_gemv_best(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t st) {
+    if (w.ntiles <= kDirectMaxTiles && direct_supported(w)) return launch_gemv_direct(ctx, w, x, y, st);
     if (pipe_supported(w)) {
         size_t pf = 0, ci = 0;
         pipe_scratch_size(ctx, w, &pf, &ci);

@@ -44,7 +44,6 @@ constexpr int kAttnThreads = 256;
 constexpr int kMaxGroup = 8;          // query heads per KV head
 constexpr int kMaxHeads = 32;
 constexpr int kMaxHeadDim = 256;
-constexpr int kMaxChunk = (4096 + kAttnSplit - 1) / kAttnSplit;   // keys per CTA at the largest context
 constexpr int kMaxContext = 4096;
 constexpr int kArgmaxBlocks = 148;
 constexpr int kArgmaxThreads = 512;
@@ -171,18 +170,24 @@ __global__ void qk_rope_kv_kernel(const DecState *st, float *qkv, int heads, int
 }
 
 // Attention of the current token over positions [start, pos] of one layer.
-// Grid: kAttnSplit blocks, each a contiguous key range for every KV head;
-// each block writes per query head its running max m, sum l and unnormalised
-// output acc = sum exp(s - m) v; the last block to finish combines the splits
-// in block order (deterministic) and resets the arrival counter.
+// Grid: kAttnSplit blocks, each a contiguous key range for every KV head.  A
+// block stages its keys kSub at a time (K and V rows into shared memory, all
+// loads in flight together), scores them for the KV head's query group and
+// keeps a running max m, sum l and unnormalised output acc = sum exp(s - m) v
+// per query head; the last block to finish combines the splits in block order
+// (deterministic) and resets the arrival counter.
+constexpr int kSub = 16;
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const DecState *st, const float *qkv, const float *kcache, const float *vcache, float *out, float *part,
     int *counter, int heads, int kv_heads, int hd, int context, int window, int is_global, float scale) {
     pdl_trigger();
     pdl_wait();
-    __shared__ float qs[kMaxGroup * kMaxHeadDim];
-    __shared__ float sc[kMaxGroup * kMaxChunk];
-    __shared__ float mh[kMaxGroup], lh[kMaxGroup];
+    __shared__ __align__(16) float qs[kMaxGroup * kMaxHeadDim];
+    __shared__ __align__(16) float ks[kSub * kMaxHeadDim];
+    __shared__ __align__(16) float vs[kSub * kMaxHeadDim];
+    __shared__ float sc[kMaxGroup * kSub];
+    __shared__ float mh[kMaxGroup], lh[kMaxGroup], ch[kMaxGroup];
+    __shared__ float wsplit[kMaxHeads * kAttnSplit];
     __shared__ int last;
     const int pos = st->pos;
     const int seq = pos + 1;
@@ -195,62 +200,81 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const int group = heads / kv_heads;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     const size_t part_stride = (size_t)hd + 2;
+    const int d = threadIdx.x;                  // output dimension of this thread (hd <= blockDim)
 
     for (int kh = 0; kh < kv_heads; ++kh) {
         const float *kb = kcache + (size_t)kh * context * hd;
         const float *vb = vcache + (size_t)kh * context * hd;
         for (int j = threadIdx.x; j < group * hd; j += blockDim.x) qs[j] = qkv[(size_t)kh * group * hd + j];
+        if (threadIdx.x < group) {
+            mh[threadIdx.x] = -INFINITY;
+            lh[threadIdx.x] = 0.0f;
+        }
+        float acc[kMaxGroup];
+#pragma unroll
+        for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
         __syncthreads();
-        // scores[h][t] = (q_h . k_t) * scale
-        for (int t = warp; t < n; t += nwarps) {
-            const float *krow = kb + (size_t)(k0 + t) * hd;
-            float acc[kMaxGroup];
-#pragma unroll
-            for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
-            for (int d = lane; d < hd; d += 32) {
-                const float kv = krow[d];
-#pragma unroll
-                for (int h = 0; h < kMaxGroup; ++h)
-                    if (h < group) acc[h] += qs[h * hd + d] * kv;
+        for (int t0 = 0; t0 < n; t0 += kSub) {
+            const int ns = min(kSub, n - t0);
+            // Stage ns rows of K and V (all loads issued before any use).
+            const float4 *k4 = reinterpret_cast<const float4 *>(kb + (size_t)(k0 + t0) * hd);
+            const float4 *v4 = reinterpret_cast<const float4 *>(vb + (size_t)(k0 + t0) * hd);
+            const int nv = ns * hd / 4;
+            for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+                const float4 a = __ldg(k4 + i), b = __ldg(v4 + i);
+                reinterpret_cast<float4 *>(ks)[i] = a;
+                reinterpret_cast<float4 *>(vs)[i] = b;
             }
+            __syncthreads();
+            // scores of the staged keys (one warp per key)
+            for (int t = warp; t < ns; t += nwarps) {
+                float a[kMaxGroup];
 #pragma unroll
-            for (int h = 0; h < kMaxGroup; ++h) {
-                if (h < group) {
-                    const float v = warp_sum(acc[h]);
-                    if (lane == 0) sc[h * kMaxChunk + t] = v * scale;
+                for (int h = 0; h < kMaxGroup; ++h) a[h] = 0.0f;
+                for (int dd = lane; dd < hd; dd += 32) {
+                    const float kv = ks[t * hd + dd];
+#pragma unroll
+                    for (int h = 0; h < kMaxGroup; ++h)
+                        if (h < group) a[h] += qs[h * hd + dd] * kv;
+                }
+#pragma unroll
+                for (int h = 0; h < kMaxGroup; ++h) {
+                    if (h < group) {
+                        const float v = warp_sum(a[h]);
+                        if (lane == 0) sc[h * kSub + t] = v * scale;
+                    }
                 }
             }
-        }
-        __syncthreads();
-        // per-head max and exp-sum over this block's keys (one warp per head)
-        for (int h = warp; h < group; h += nwarps) {
-            float m = -INFINITY;
-            for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[h * kMaxChunk + t]);
-            m = warp_max(m);
-            float l = 0.0f;
-            for (int t = lane; t < n; t += 32) {
-                const float p = n ? expf(sc[h * kMaxChunk + t] - m) : 0.0f;
-                sc[h * kMaxChunk + t] = p;
-                l += p;
+            __syncthreads();
+            // running max / sum per head (one warp per head, lane = key)
+            for (int h = warp; h < group; h += nwarps) {
+                const float sv = lane < ns ? sc[h * kSub + lane] : -INFINITY;
+                const float m_old = mh[h];
+                const float m_new = fmaxf(m_old, warp_max(sv));
+                const float p = lane < ns ? expf(sv - m_new) : 0.0f;
+                const float psum = warp_sum(p);
+                const float c = expf(m_old - m_new);     // 0 while m_old is -inf
+                if (lane < ns) sc[h * kSub + lane] = p;
+                if (lane == 0) {
+                    ch[h] = c;
+                    mh[h] = m_new;
+                    lh[h] = lh[h] * c + psum;
+                }
             }
-            l = warp_sum(l);
-            if (lane == 0) {
-                mh[h] = m;
-                lh[h] = l;
-            }
-        }
-        __syncthreads();
-        // acc[h][d] = sum_t p[h][t] v_t[d]
-        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-            float acc[kMaxGroup];
+            __syncthreads();
+            if (d < hd) {
 #pragma unroll
-            for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
-            for (int t = 0; t < n; ++t) {
-                const float v = vb[(size_t)(k0 + t) * hd + d];
-#pragma unroll
-                for (int h = 0; h < kMaxGroup; ++h)
-                    if (h < group) acc[h] += sc[h * kMaxChunk + t] * v;
+                for (int h = 0; h < kMaxGroup; ++h) {
+                    if (h < group) {
+                        float a = acc[h] * ch[h];
+                        for (int t = 0; t < ns; ++t) a += sc[h * kSub + t] * vs[t * hd + d];
+                        acc[h] = a;
+                    }
+                }
             }
+            __syncthreads();
+        }
+        if (d < hd) {
 #pragma unroll
             for (int h = 0; h < kMaxGroup; ++h) {
                 if (h < group) {
@@ -275,7 +299,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     __threadfence();
     // Combine: weight of split b for head h is exp(m_b - M) / sum_b' l_b' exp(m_b' - M)
     // (one warp per head, lane = split), then out = sum_b weight_b acc_b.
-    __shared__ float wsplit[kMaxHeads * kAttnSplit];
     for (int h = warp; h < heads; h += nwarps) {
         const int kh = h / group, hh = h % group;
         const float *pp = part + ((size_t)(lane * kv_heads + kh) * group + hh) * part_stride;
@@ -287,12 +310,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     }
     __syncthreads();
     for (int j = threadIdx.x; j < heads * hd; j += blockDim.x) {
-        const int h = j / hd, d = j % hd;
+        const int h = j / hd, dd = j % hd;
         const int kh = h / group, hh = h % group;
         float O = 0.0f;
 #pragma unroll 8
         for (int b = 0; b < kAttnSplit; ++b)
-            O += __ldcg(part + ((size_t)(b * kv_heads + kh) * group + hh) * part_stride + 2 + d) * wsplit[h * kAttnSplit + b];
+            O += __ldcg(part + ((size_t)(b * kv_heads + kh) * group + hh) * part_stride + 2 + dd) *
+                 wsplit[h * kAttnSplit + b];
         out[j] = O;
     }
     if (threadIdx.x == 0) *counter = 0;

@@ -851,7 +851,121 @@ int launch_cfg(kernel_context_t *ctx, const PipeParams &p, PipeCfg c, int grid, 
     return run(gemv_pipe<DT, 12, 3>, 12 * 32);
 }
 
+// --------------------------------------------------- latency-bound GEMV --
+// Small weights (decode projections, a few hundred KB to a few MB) are bound
+// by latency, not bandwidth: gemv_direct gives each 32-row tile one CTA whose
+// kDirectWarps warps split the tile's items (at most two per warp), loads
+// every item straight into registers before waiting for the kernel that
+// produces x (programmatic dependent launch), and reduces the warps' row sums
+// in shared memory in warp order - no ring, no split-tile atomics.
+constexpr int kDirectWarps = 8;
+constexpr int kDirectMaxItems = 2;
+
+template <tensor_dtype_t DT>
+__device__ __forceinline__ void load_item_global(ItemRegs<DT> &R, const PipeParams &p, int tile, int u0, int nblk,
+                                                 int lane) {
+    const int g = lane >> 2;
+    const uint8_t *codes = p.codes + (size_t)tile * p.kchunks * 512 + (size_t)u0 * Geo<DT>::kCodeBpb;
+    const float *sc = p.scales + ((size_t)tile * p.nb + u0) * 32 + g * 4;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const bool ok = u < nblk;
+        if constexpr (DT == DTYPE_Q8_0) {
+            R.a[u][0] = ok ? __ldg(reinterpret_cast<const uint4 *>(codes + u * 1024 + lane * 16)) : make_uint4(0, 0, 0, 0);
+            R.a[u][1] = ok ? __ldg(reinterpret_cast<const uint4 *>(codes + u * 1024 + 512 + lane * 16))
+                           : make_uint4(0, 0, 0, 0);
+        } else {
+            R.a[u] = ok ? __ldg(reinterpret_cast<const uint4 *>(codes + u * 512 + lane * 16)) : make_uint4(0, 0, 0, 0);
+        }
+        R.s[u] = ok ? __ldg(reinterpret_cast<const float4 *>(sc + (size_t)u * 32)) : make_float4(0, 0, 0, 0);
+    }
+}
+
+template <tensor_dtype_t DT>
+__global__ void __launch_bounds__(kDirectWarps * 32) gemv_direct(const PipeParams p) {
+    static_assert(DT == DTYPE_Q8_0 || DT == DTYPE_Q4_0, "per-block-scale formats only");
+    static_assert(Geo<DT>::kBpi == 4, "items of four blocks");
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float part[kDirectWarps][32];
+    __shared__ int s_nonfinite;
+    pdl_trigger();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = blockIdx.x;
+    ItemRegs<DT> R[kDirectMaxItems];
+#pragma unroll
+    for (int k = 0; k < kDirectMaxItems; ++k) {
+        const int seg = warp + k * kDirectWarps;
+        if (seg < p.nseg) load_item_global<DT>(R[k], p, tile, seg * 4, min(4, p.nb - seg * 4), lane);
+    }
+    if (threadIdx.x == 0) s_nonfinite = 0;
+    pdl_wait();
+    __syncthreads();
+    XPrep xp;
+    xp.digits = smem;
+    const size_t dig_bytes = align16((size_t)p.nb * kDigitBytesPerBlock + 16);
+    xp.pexp = reinterpret_cast<float *>(smem + dig_bytes);
+    xp.corr = reinterpret_cast<int *>(smem + dig_bytes + align16((size_t)p.nb * 4));
+    xp.nonfinite = &s_nonfinite;
+    prepare_x<DT, kDirectWarps>(p, xp);
+    __syncthreads();
+    MmaAcc acc;
+    acc.reset();
+#pragma unroll
+    for (int k = 0; k < kDirectMaxItems; ++k) {
+        const int seg = warp + k * kDirectWarps;
+        if (seg < p.nseg) compute_item(R[k], seg * 4, p.nb, lane, xp, nullptr, acc);
+    }
+    unsigned long long v[4];
+    tile_rows<DT>(acc, v);
+    if ((lane & 3) == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) part[warp][(lane >> 2) + 8 * i] = __uint_as_float((uint32_t)v[i]);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kDirectWarps; ++w) sum += part[w][lane];
+        const int row = tile * 32 + lane;
+        if (row < p.nrows) p.y[row] = s_nonfinite ? __int_as_float(0x7FC00000) : sum;
+    }
+}
+
 }  // namespace
+
+bool direct_supported(const DevWeight &w) {
+    if (w.dtype != DTYPE_Q8_0 && w.dtype != DTYPE_Q4_0) return false;
+    return w.ntiles > 0 && (w.nb + 3) / 4 <= kDirectWarps * kDirectMaxItems &&
+           ximage_bytes(w.dtype, w.nb, w.kchunks) <= 48 * 1024;
+}
+
+// y = W . x for a small Q8_0 / Q4_0 weight (direct_supported), one CTA per tile.
+int launch_gemv_direct(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t st) {
+    if (w.ntiles == 0) return 0;
+    PipeParams p{};
+    p.codes = reinterpret_cast<const uint8_t *>(w.codes);
+    p.scales = w.scales;
+    p.x = x;
+    p.y = y;
+    p.nrows = w.nrows;
+    p.cols = w.cols;
+    p.nb = w.nb;
+    p.ntiles = w.ntiles;
+    p.kchunks = w.kchunks;
+    p.nseg = (w.nb + 3) / 4;
+    const size_t smem = ximage_bytes(w.dtype, w.nb, w.kchunks);
+    cudaError_t e;
+    if (w.dtype == DTYPE_Q8_0)
+        e = launch_pdl(gemv_direct<DTYPE_Q8_0>, dim3(w.ntiles), dim3(kDirectWarps * 32), smem, st, p);
+    else
+        e = launch_pdl(gemv_direct<DTYPE_Q4_0>, dim3(w.ntiles), dim3(kDirectWarps * 32), smem, st, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        ctx_fail(ctx, "launch_gemv_direct", "launch failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
 
 // Largest number of warps that can share one tile: ranges hold at least
 // floor(T/W) items each, so nseg consecutive items meet at most

@@ -199,6 +199,12 @@ void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_f
 int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part,
                      int *cnt, int *err, cudaStream_t stream);
 int pipe_kmax(long long T, long long W, int nseg);
+// Latency-bound GEMV of a small Q8_0 / Q4_0 weight (gemv_pipe.cu): one CTA per
+// 32-row tile, no scratch.
+bool direct_supported(const DevWeight &w);
+int launch_gemv_direct(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t stream);
+// Weights of at most this many 32-row tiles take the direct kernel.
+constexpr int kDirectMaxTiles = 512;
 // Batch-1 product through the pipelined kernel when it applies, else the
 // tile kernel; checks nothing on the host (asynchronous).
 int launch_gemv_best(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t stream);
