@@ -255,8 +255,10 @@ __device__ __forceinline__ int digit_slot(int p) {
     }
 }
 
+// x comes from global memory (p.x), or from an fp32 vector in shared memory
+// when xs_smem is given (the fused producers of gemv_direct).
 template <tensor_dtype_t DT, int NW>
-__device__ void prepare_x(const PipeParams &p, XPrep xp) {
+__device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = nullptr) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ float s_red[kMaxPipeWarps];
     int gexp = 0;
@@ -288,7 +290,7 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp) {
 #pragma unroll
         for (int u = 0; u < kGroup; ++u) {
             const int c = (b0 + u * NW) * 32 + lane;
-            vg[u] = (b0 + u * NW < p.nb && c < p.cols) ? __ldg(p.x + c) : 0.0f;
+            vg[u] = (b0 + u * NW < p.nb && c < p.cols) ? (xs_smem ? xs_smem[c] : __ldg(p.x + c)) : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < kGroup; ++u) {
@@ -881,12 +883,73 @@ __device__ __forceinline__ void load_item_global(ItemRegs<DT> &R, const PipePara
     }
 }
 
-template <tensor_dtype_t DT>
-__global__ void __launch_bounds__(kDirectWarps * 32) gemv_direct(const PipeParams p) {
+// Producer of x inside gemv_direct.
+enum DirectX : int {
+    kXPlain = 0,     // x read from p.x
+    kXResNorm = 1,   // h' = h_in + rmsnorm_delta(t, w_post); x = rmsnorm_delta(h', w_next); block 0 stores h'
+    kXGeGLU = 2,     // x[i] = gelu(gu[i]) * gu[cols + i]
+};
+struct DirectFuse {
+    const float *t, *w_post, *h_in, *w_next, *gu;
+    float *h_out;
+    float eps;
+};
+
+__device__ __forceinline__ float direct_block_sum(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = lane < kDirectWarps ? red[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    return t;
+}
+
+// Builds the fp32 x vector of a fused producer in shared memory.  The
+// arithmetic is the reference's rmsnorm_delta (src/transformer/normalization.c:
+// 103-116) and GeGLU (src/transformer/activations.c:64-82, transformer.c:150-157).
+template <int XM>
+__device__ void produce_x(const PipeParams &p, const DirectFuse &f, float *xs, float *red) {
+    const int n = p.cols;
+    if constexpr (XM == kXResNorm) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const float v = f.t[i];
+            xs[i] = v;
+            ss += v * v;
+        }
+        ss = direct_block_sum(ss, red);
+        const float r1 = 1.0f / sqrtf(ss / (float)n + f.eps);
+        float hh = 0.0f;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const float h = f.h_in[i] + (xs[i] * r1) * (1.0f + (f.w_post ? f.w_post[i] : 0.0f));
+            xs[i] = h;
+            hh += h * h;
+            if (blockIdx.x == 0) f.h_out[i] = h;
+        }
+        hh = direct_block_sum(hh, red);
+        const float r2 = 1.0f / sqrtf(hh / (float)n + f.eps);
+        for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = (xs[i] * r2) * (1.0f + (f.w_next ? f.w_next[i] : 0.0f));
+    } else if constexpr (XM == kXGeGLU) {
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const float x = f.gu[i];
+            const float y = 0.7978845608f * (x + 0.044715f * x * x * x);
+            xs[i] = (0.5f * x * (1.0f + tanhf(y))) * f.gu[n + i];
+        }
+    }
+    __syncthreads();
+}
+
+template <tensor_dtype_t DT, int XM>
+__global__ void __launch_bounds__(kDirectWarps * 32) gemv_direct(const PipeParams p, const DirectFuse f) {
     static_assert(DT == DTYPE_Q8_0 || DT == DTYPE_Q4_0, "per-block-scale formats only");
     static_assert(Geo<DT>::kBpi == 4, "items of four blocks");
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float part[kDirectWarps][32];
+    __shared__ float red[32];
     __shared__ int s_nonfinite;
     pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -906,7 +969,12 @@ __global__ void __launch_bounds__(kDirectWarps * 32) gemv_direct(const PipeParam
     xp.pexp = reinterpret_cast<float *>(smem + dig_bytes);
     xp.corr = reinterpret_cast<int *>(smem + dig_bytes + align16((size_t)p.nb * 4));
     xp.nonfinite = &s_nonfinite;
-    prepare_x<DT, kDirectWarps>(p, xp);
+    float *xs = nullptr;
+    if constexpr (XM != kXPlain) {
+        xs = reinterpret_cast<float *>(smem + ((ximage_bytes(DT, p.nb, p.kchunks) + 15) & ~(size_t)15));
+        produce_x<XM>(p, f, xs, red);
+    }
+    prepare_x<DT, kDirectWarps>(p, xp, xs);
     __syncthreads();
     MmaAcc acc;
     acc.reset();
@@ -939,8 +1007,16 @@ bool direct_supported(const DevWeight &w) {
            ximage_bytes(w.dtype, w.nb, w.kchunks) <= 48 * 1024;
 }
 
-// y = W . x for a small Q8_0 / Q4_0 weight (direct_supported), one CTA per tile.
-int launch_gemv_direct(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t st) {
+namespace {
+template <int XM>
+cudaError_t direct_launch(const DevWeight &w, const PipeParams &p, const DirectFuse &f, size_t smem, cudaStream_t st) {
+    if (w.dtype == DTYPE_Q8_0)
+        return launch_pdl(gemv_direct<DTYPE_Q8_0, XM>, dim3(w.ntiles), dim3(kDirectWarps * 32), smem, st, p, f);
+    return launch_pdl(gemv_direct<DTYPE_Q4_0, XM>, dim3(w.ntiles), dim3(kDirectWarps * 32), smem, st, p, f);
+}
+
+int direct_common(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, int mode, const DirectFuse &f,
+                  cudaStream_t st) {
     if (w.ntiles == 0) return 0;
     PipeParams p{};
     p.codes = reinterpret_cast<const uint8_t *>(w.codes);
@@ -953,18 +1029,42 @@ int launch_gemv_direct(kernel_context_t *ctx, const DevWeight &w, const float *x
     p.ntiles = w.ntiles;
     p.kchunks = w.kchunks;
     p.nseg = (w.nb + 3) / 4;
-    const size_t smem = ximage_bytes(w.dtype, w.nb, w.kchunks);
-    cudaError_t e;
-    if (w.dtype == DTYPE_Q8_0)
-        e = launch_pdl(gemv_direct<DTYPE_Q8_0>, dim3(w.ntiles), dim3(kDirectWarps * 32), smem, st, p);
-    else
-        e = launch_pdl(gemv_direct<DTYPE_Q4_0>, dim3(w.ntiles), dim3(kDirectWarps * 32), smem, st, p);
+    size_t smem = ximage_bytes(w.dtype, w.nb, w.kchunks);
+    if (mode != kXPlain) smem = ((smem + 15) & ~(size_t)15) + (size_t)w.nb * 32 * sizeof(float);
+    cudaError_t e = mode == kXResNorm ? direct_launch<kXResNorm>(w, p, f, smem, st)
+                  : mode == kXGeGLU   ? direct_launch<kXGeGLU>(w, p, f, smem, st)
+                                      : direct_launch<kXPlain>(w, p, f, smem, st);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         ctx_fail(ctx, "launch_gemv_direct", "launch failed: %s", cudaGetErrorString(e));
         return -1;
     }
     return 0;
+}
+}  // namespace
+
+// y = W . x for a small Q8_0 / Q4_0 weight (direct_supported), one CTA per tile.
+int launch_gemv_direct(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t st) {
+    return direct_common(ctx, w, x, y, kXPlain, DirectFuse{}, st);
+}
+
+int launch_gemv_direct_resnorm(kernel_context_t *ctx, const DevWeight &w, const float *t, const float *w_post,
+                               const float *h_in, const float *w_next, float *h_out, float eps, float *y,
+                               cudaStream_t st) {
+    DirectFuse f{};
+    f.t = t;
+    f.w_post = w_post;
+    f.h_in = h_in;
+    f.w_next = w_next;
+    f.h_out = h_out;
+    f.eps = eps;
+    return direct_common(ctx, w, nullptr, y, kXResNorm, f, st);
+}
+
+int launch_gemv_direct_geglu(kernel_context_t *ctx, const DevWeight &w, const float *gu, float *y, cudaStream_t st) {
+    DirectFuse f{};
+    f.gu = gu;
+    return direct_common(ctx, w, nullptr, y, kXGeGLU, f, st);
 }
 
 // Largest number of warps that can share one tile: ranges hold at least
