@@ -24,10 +24,17 @@
 // computed on the host with the reference's formula and libm calls
 // (src/transformer/rope.c:19-37), so they are the same numbers.
 //
-// The current token, position and output index live in device memory, and a
-// step's kernels (GEMVs of gemv_pipe.cu and the kernels below) are captured
-// once into a CUDA graph per step kind (prompt step, generated step); a
-// generation is then a sequence of graph launches with no host round trip.
+// Kernels of one token (5 per layer): the QKV GEMV (whose x stage also applies
+// the previous layer's FFN residual and this layer's pre-attention norm), the
+// attention (with QK-norm, RoPE and the KV-cache write), the O GEMV, the
+// gate/up GEMV (attention residual + pre-FFN norm in its x stage) and the down
+// GEMV (GeGLU in its x stage); then, for a generated token, the final norm,
+// the LM-head GEMV and the argmax.  Every kernel is launched with programmatic
+// dependent launch, so each GEMV streams its weights while the previous kernel
+// runs.  The current token, position and output index live in device memory,
+// and a step is captured once into a CUDA graph per step kind (prompt step,
+// generated step); a generation is a sequence of graph launches with no host
+// round trip.
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -130,45 +137,6 @@ __global__ void residual_norm_kernel(const float *t, const float *w_post, float 
     rms_delta_block(hidden, w_next, norm, dim, eps, red);
 }
 
-// Per-head QK-norm and RoPE, then the cache write.  Blocks 0..heads-1: query
-// heads (in place in qkv); blocks heads..heads+kv_heads-1: key heads (normed,
-// rotated, written to K) and their value rows (copied to V).  head_dim / 2
-// threads; thread i owns the rotation pair (i, i + head_dim/2)
-// (rope_apply_fast, src/transformer/rope.c:65-80).
-__global__ void qk_rope_kv_kernel(const DecState *st, float *qkv, int heads, int kv_heads, int hd,
-                                  const float *q_norm, const float *k_norm, float eps, const float *rope_cos,
-                                  const float *rope_sin, float *kcache, float *vcache, int context) {
-    pdl_trigger();
-    pdl_wait();
-    __shared__ float red[32];
-    const int pos = st->pos;
-    const int half = hd >> 1, i = threadIdx.x;
-    const bool is_q = blockIdx.x < heads;
-    const int kh = blockIdx.x - heads;
-    float *x = is_q ? qkv + (size_t)blockIdx.x * hd : qkv + (size_t)heads * hd + (size_t)kh * hd;
-    const float *w = is_q ? q_norm : k_norm;
-    const float x0 = x[i], x1 = x[i + half];
-    const float ss = block_sum(x0 * x0 + x1 * x1, red);
-    const float r = 1.0f / sqrtf(ss / (float)hd + eps);
-    const float y0 = (x0 * r) * (1.0f + (w ? w[i] : 0.0f));
-    const float y1 = (x1 * r) * (1.0f + (w ? w[i + half] : 0.0f));
-    const float c = rope_cos[(size_t)pos * hd + i], s = rope_sin[(size_t)pos * hd + i];
-    const float o0 = y0 * c - y1 * s;
-    const float o1 = y1 * c + y0 * s;
-    if (is_q) {
-        x[i] = o0;
-        x[i + half] = o1;
-    } else {
-        float *krow = kcache + ((size_t)kh * context + pos) * hd;
-        float *vrow = vcache + ((size_t)kh * context + pos) * hd;
-        const float *v = qkv + (size_t)(heads + kv_heads) * hd + (size_t)kh * hd;
-        krow[i] = o0;
-        krow[i + half] = o1;
-        vrow[i] = v[i];
-        vrow[i + half] = v[i + half];
-    }
-}
-
 // Attention of the current token over positions [start, pos] of one layer.
 // Grid: kAttnSplit blocks, each a contiguous key range for every KV head.  A
 // block stages its keys kSub at a time (K and V rows into shared memory, all
@@ -176,15 +144,53 @@ __global__ void qk_rope_kv_kernel(const DecState *st, float *qkv, int heads, int
 // keeps a running max m, sum l and unnormalised output acc = sum exp(s - m) v
 // per query head; the last block to finish combines the splits in block order
 // (deterministic) and resets the arrival counter.
+//
+// The block also finishes the projections of the current token first (what
+// the reference does in attention_apply_rope_cache, attention.c:292-309):
+// rmsnorm_delta per head with q_norm / k_norm, RoPE at pos (rope_apply_fast,
+// src/transformer/rope.c:65-80), and block 0 writes the new K and V rows;
+// the block whose range holds pos reads them from shared memory.
 constexpr int kSub = 16;
+
+// rmsnorm_delta of one head (hd values at x) then the half-split rotation, by
+// one warp; lane owns the pairs (i, i + hd/2) for i = lane + 32 j.
+__device__ __forceinline__ void warp_norm_rope(const float *x, const float *w, float eps, const float *cs,
+                                               const float *sn, int hd, float *dst) {
+    const int lane = threadIdx.x & 31, half = hd >> 1;
+    float a[kMaxHeadDim / 64], b[kMaxHeadDim / 64];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxHeadDim / 64; ++j) {
+        const int i = lane + 32 * j;
+        a[j] = i < half ? x[i] : 0.0f;
+        b[j] = i < half ? x[i + half] : 0.0f;
+        ss += a[j] * a[j] + b[j] * b[j];
+    }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss / (float)hd + eps);
+#pragma unroll
+    for (int j = 0; j < kMaxHeadDim / 64; ++j) {
+        const int i = lane + 32 * j;
+        if (i < half) {
+            const float y0 = (a[j] * r) * (1.0f + (w ? w[i] : 0.0f));
+            const float y1 = (b[j] * r) * (1.0f + (w ? w[i + half] : 0.0f));
+            const float c = cs[i], sv = sn[i];
+            dst[i] = y0 * c - y1 * sv;
+            dst[i + half] = y1 * c + y0 * sv;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
-    const DecState *st, const float *qkv, const float *kcache, const float *vcache, float *out, float *part,
-    int *counter, int heads, int kv_heads, int hd, int context, int window, int is_global, float scale) {
+    const DecState *st, const float *qkv, float *kcache, float *vcache, float *out, float *part, int *counter,
+    int heads, int kv_heads, int hd, int context, int window, int is_global, float scale, const float *q_norm,
+    const float *k_norm, float eps, const float *rope_cos, const float *rope_sin) {
     pdl_trigger();
     pdl_wait();
     __shared__ __align__(16) float qs[kMaxGroup * kMaxHeadDim];
     __shared__ __align__(16) float ks[kSub * kMaxHeadDim];
     __shared__ __align__(16) float vs[kSub * kMaxHeadDim];
+    __shared__ __align__(16) float kpos[kMaxHeadDim], vpos[kMaxHeadDim];
     __shared__ float sc[kMaxGroup * kSub];
     __shared__ float mh[kMaxGroup], lh[kMaxGroup], ch[kMaxGroup];
     __shared__ float wsplit[kMaxHeads * kAttnSplit];
@@ -193,7 +199,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const int seq = pos + 1;
     const int start = (!is_global && seq > window) ? seq - window : 0;
     const int len = seq - start;
-    const int chunk = (len + kAttnSplit - 1) / kAttnSplit;
+    // Keys per block: a multiple of kSub, so short sequences use few blocks
+    // (one block, and no combine, up to kSub keys).
+    const int chunk = max(kSub, ((len + kAttnSplit - 1) / kAttnSplit + kSub - 1) / kSub * kSub);
+    const int nsplit = (len + chunk - 1) / chunk;
     const int k0 = start + blockIdx.x * chunk;
     const int k1 = min(seq, k0 + chunk);
     const int n = max(0, k1 - k0);
@@ -202,10 +211,21 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const size_t part_stride = (size_t)hd + 2;
     const int d = threadIdx.x;                  // output dimension of this thread (hd <= blockDim)
 
+    const float *cs = rope_cos + (size_t)pos * hd, *sn = rope_sin + (size_t)pos * hd;
     for (int kh = 0; kh < kv_heads; ++kh) {
-        const float *kb = kcache + (size_t)kh * context * hd;
-        const float *vb = vcache + (size_t)kh * context * hd;
-        for (int j = threadIdx.x; j < group * hd; j += blockDim.x) qs[j] = qkv[(size_t)kh * group * hd + j];
+        float *kb = kcache + (size_t)kh * context * hd;
+        float *vb = vcache + (size_t)kh * context * hd;
+        // Normed, rotated q of the group, k and v of the current token.
+        for (int h = warp; h < group + 2; h += nwarps) {
+            if (h < group) {
+                warp_norm_rope(qkv + (size_t)(kh * group + h) * hd, q_norm, eps, cs, sn, hd, qs + h * hd);
+            } else if (h == group) {
+                warp_norm_rope(qkv + (size_t)(heads + kh) * hd, k_norm, eps, cs, sn, hd, kpos);
+            } else {
+                const float *v = qkv + (size_t)(heads + kv_heads + kh) * hd;
+                for (int i = lane; i < hd; i += 32) vpos[i] = v[i];
+            }
+        }
         if (threadIdx.x < group) {
             mh[threadIdx.x] = -INFINITY;
             lh[threadIdx.x] = 0.0f;
@@ -214,14 +234,28 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
 #pragma unroll
         for (int h = 0; h < kMaxGroup; ++h) acc[h] = 0.0f;
         __syncthreads();
+        if (blockIdx.x == 0) {
+            for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+                kb[(size_t)pos * hd + i] = kpos[i];
+                vb[(size_t)pos * hd + i] = vpos[i];
+            }
+        }
         for (int t0 = 0; t0 < n; t0 += kSub) {
             const int ns = min(kSub, n - t0);
             // Stage ns rows of K and V (all loads issued before any use).
             const float4 *k4 = reinterpret_cast<const float4 *>(kb + (size_t)(k0 + t0) * hd);
             const float4 *v4 = reinterpret_cast<const float4 *>(vb + (size_t)(k0 + t0) * hd);
             const int nv = ns * hd / 4;
+            const int row4 = hd / 4;
             for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-                const float4 a = __ldg(k4 + i), b = __ldg(v4 + i);
+                float4 a, b;
+                if (k0 + t0 + i / row4 == pos) {          // written by this kernel: take it from shared memory
+                    a = reinterpret_cast<const float4 *>(kpos)[i % row4];
+                    b = reinterpret_cast<const float4 *>(vpos)[i % row4];
+                } else {
+                    a = __ldcg(k4 + i);
+                    b = __ldcg(v4 + i);
+                }
                 reinterpret_cast<float4 *>(ks)[i] = a;
                 reinterpret_cast<float4 *>(vs)[i] = b;
             }
@@ -291,9 +325,21 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
         __syncthreads();
     }
 
+    if (nsplit == 1) {
+        // A single block holds every key: normalise and store directly.
+        if (blockIdx.x == 0) {
+            for (int j = threadIdx.x; j < heads * hd; j += blockDim.x) {
+                const int h = j / hd, kh = h / group, hh = h % group;
+                const float *pp = part + ((size_t)kh * group + hh) * part_stride;
+                out[j] = __ldcg(pp + 2 + j % hd) / __ldcg(pp + 1);
+            }
+        }
+        return;
+    }
+    if ((int)blockIdx.x >= nsplit) return;
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
+    if (threadIdx.x == 0) last = (atomicAdd(counter, 1) == nsplit - 1);
     __syncthreads();
     if (!last) return;
     __threadfence();
@@ -301,37 +347,44 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     // (one warp per head, lane = split), then out = sum_b weight_b acc_b.
     for (int h = warp; h < heads; h += nwarps) {
         const int kh = h / group, hh = h % group;
-        const float *pp = part + ((size_t)(lane * kv_heads + kh) * group + hh) * part_stride;
-        const float m = __ldcg(pp), l = __ldcg(pp + 1);
+        float m = -INFINITY, l = 0.0f;
+        if (lane < nsplit) {
+            const float *pp = part + ((size_t)(lane * kv_heads + kh) * group + hh) * part_stride;
+            m = __ldcg(pp);
+            l = __ldcg(pp + 1);
+        }
         const float M = warp_max(m);
         const float e = (m == -INFINITY) ? 0.0f : expf(m - M);
         const float L = warp_sum(l * e);
         wsplit[h * kAttnSplit + lane] = e / L;
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < heads * hd; j += blockDim.x) {
-        const int h = j / hd, dd = j % hd;
-        const int kh = h / group, hh = h % group;
-        float O = 0.0f;
-#pragma unroll 8
-        for (int b = 0; b < kAttnSplit; ++b)
-            O += __ldcg(part + ((size_t)(b * kv_heads + kh) * group + hh) * part_stride + 2 + dd) *
-                 wsplit[h * kAttnSplit + b];
-        out[j] = O;
+    // Each thread sums its outputs over the splits; the loads of kOut outputs
+    // of one split are independent, so several splits' loads are in flight.
+    constexpr int kOut = 4;
+    for (int j0 = threadIdx.x; j0 < heads * hd; j0 += blockDim.x * kOut) {
+        float O[kOut];
+        int base[kOut], wrow[kOut];
+#pragma unroll
+        for (int k = 0; k < kOut; ++k) {
+            const int j = j0 + k * blockDim.x;
+            const int h = j / hd, kh = h / group, hh = h % group;
+            O[k] = 0.0f;
+            base[k] = j < heads * hd ? (int)(((size_t)kh * group + hh) * part_stride + 2 + j % hd) : -1;
+            wrow[k] = h * kAttnSplit;
+        }
+#pragma unroll 4
+        for (int b = 0; b < nsplit; ++b) {
+            const size_t boff = (size_t)b * kv_heads * group * part_stride;
+#pragma unroll
+            for (int k = 0; k < kOut; ++k)
+                if (base[k] >= 0) O[k] += __ldcg(part + boff + base[k]) * wsplit[wrow[k] + b];
+        }
+#pragma unroll
+        for (int k = 0; k < kOut; ++k)
+            if (base[k] >= 0) out[j0 + k * blockDim.x] = O[k];
     }
     if (threadIdx.x == 0) *counter = 0;
-}
-
-// act[i] = gelu(gate[i]) * up[i], tanh form (src/transformer/activations.c:64-82).
-__global__ void geglu_kernel(const float *gu, float *act, int ffn) {
-    pdl_trigger();
-    pdl_wait();
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ffn; i += gridDim.x * blockDim.x) {
-        const float x = gu[i];
-        const float y = 0.7978845608f * (x + 0.044715f * x * x * x);
-        const float g = 0.5f * x * (1.0f + tanhf(y));
-        act[i] = g * gu[ffn + i];
-    }
 }
 
 // Top-1 (value, lowest index on ties) and top-2 value.
@@ -456,8 +509,8 @@ struct sapphire_decoder {
     uint16_t *embed = nullptr;
     float *rope_cos_g = nullptr, *rope_sin_g = nullptr, *rope_cos_l = nullptr, *rope_sin_l = nullptr;
     float *kcache = nullptr, *vcache = nullptr;
-    float *hidden = nullptr, *norm = nullptr, *qkv = nullptr, *attn = nullptr, *tmp = nullptr, *gu = nullptr,
-          *act = nullptr, *logits = nullptr, *attn_part = nullptr;
+    float *hidden = nullptr, *hidden2 = nullptr, *norm = nullptr, *qkv = nullptr, *attn = nullptr, *tmp = nullptr,
+          *gu = nullptr, *logits = nullptr, *attn_part = nullptr;
     void *top2_part = nullptr;
     int *counters = nullptr;        // [0] attention, [1] argmax
     DecState *state = nullptr;
@@ -567,40 +620,47 @@ int enqueue_step(sapphire_decoder_t *d, bool generate, cudaStream_t st) {
                d->hidden, d->norm, ctx->d_err);
     if (check_launch(d, "embedding")) return -1;
     ++launches;
+    // The residual stream alternates between two buffers: a fused GEMV reads
+    // one and its first block writes the updated stream to the other.
+    float *cur = d->hidden, *other = d->hidden2;
     for (int l = 0; l < c.layers; ++l) {
         sapphire_decoder::Layer &L = d->layers[l];
         const DevWeight *qkv = weight_of(d, L.qkv), *o = weight_of(d, L.o), *gu = weight_of(d, L.gu),
                         *down = weight_of(d, L.down);
         if (!qkv || !o || !gu || !down) return -1;
-        if (launch_gemv_best(ctx, *qkv, d->norm, d->qkv, st)) return -1;
-        launch_pdl(qk_rope_kv_kernel, dim3(c.heads + c.kv_heads), dim3(c.head_dim / 2), 0, st,
-                   (const DecState *)d->state, d->qkv, c.heads, c.kv_heads, c.head_dim, (const float *)L.w_q,
-                   (const float *)L.w_k, eps, (const float *)(L.global ? d->rope_cos_g : d->rope_cos_l),
-                   (const float *)(L.global ? d->rope_sin_g : d->rope_sin_l),
-                   d->kcache + (size_t)l * c.kv_heads * c.context * c.head_dim,
-                   d->vcache + (size_t)l * c.kv_heads * c.context * c.head_dim, c.context);
-        if (check_launch(d, "qk-norm/rope")) return -1;
+        // qkv = W_qkv . rmsnorm_delta(h, attn); for l > 0, h = h + rmsnorm_delta(down_out, ffn_post) first.
+        if (l == 0) {
+            if (launch_gemv_direct(ctx, *qkv, d->norm, d->qkv, st)) return -1;
+        } else {
+            if (launch_gemv_direct_resnorm(ctx, *qkv, d->tmp, d->layers[l - 1].w_ffn_post, cur, L.w_attn, other,
+                                           eps, d->qkv, st))
+                return -1;
+            std::swap(cur, other);
+        }
+        float *kc = d->kcache + (size_t)l * c.kv_heads * c.context * c.head_dim;
+        float *vc = d->vcache + (size_t)l * c.kv_heads * c.context * c.head_dim;
         launch_pdl(attention_kernel, dim3(kAttnSplit), dim3(kAttnThreads), 0, st, (const DecState *)d->state,
-                   (const float *)d->qkv, (const float *)(d->kcache + (size_t)l * c.kv_heads * c.context * c.head_dim),
-                   (const float *)(d->vcache + (size_t)l * c.kv_heads * c.context * c.head_dim), d->attn,
-                   d->attn_part, d->counters, c.heads, c.kv_heads, c.head_dim, c.context,
-                   c.sliding_window > 0 ? c.sliding_window : 1024, L.global ? 1 : 0, att_scale);
+                   (const float *)d->qkv, kc, vc, d->attn, d->attn_part, d->counters, c.heads, c.kv_heads,
+                   c.head_dim, c.context, c.sliding_window > 0 ? c.sliding_window : 1024, L.global ? 1 : 0,
+                   att_scale, (const float *)L.w_q, (const float *)L.w_k, eps,
+                   (const float *)(L.global ? d->rope_cos_g : d->rope_cos_l),
+                   (const float *)(L.global ? d->rope_sin_g : d->rope_sin_l));
         if (check_launch(d, "attention")) return -1;
-        if (launch_gemv_best(ctx, *o, d->attn, d->tmp, st)) return -1;
-        launch_pdl(residual_norm_kernel, dim3(1), dim3(kNormThreads), 0, st, (const float *)d->tmp,
-                   (const float *)L.w_attn_post, d->hidden, (const float *)L.w_ffn, d->norm, c.hidden, eps);
-        if (check_launch(d, "attention residual")) return -1;
-        if (launch_gemv_best(ctx, *gu, d->norm, d->gu, st)) return -1;
-        launch_pdl(geglu_kernel, dim3((c.ffn + 255) / 256), dim3(256), 0, st, (const float *)d->gu, d->act, c.ffn);
-        if (check_launch(d, "geglu")) return -1;
-        if (launch_gemv_best(ctx, *down, d->act, d->tmp, st)) return -1;
-        const float *w_next = (l + 1 < c.layers) ? d->layers[l + 1].w_attn : d->w_final;
-        launch_pdl(residual_norm_kernel, dim3(1), dim3(kNormThreads), 0, st, (const float *)d->tmp,
-                   (const float *)L.w_ffn_post, d->hidden, w_next, d->norm, c.hidden, eps);
-        if (check_launch(d, "ffn residual")) return -1;
-        launches += 9;
+        if (launch_gemv_direct(ctx, *o, d->attn, d->tmp, st)) return -1;
+        // gu = W_gu . rmsnorm_delta(h + rmsnorm_delta(o_out, attn_post), ffn)
+        if (launch_gemv_direct_resnorm(ctx, *gu, d->tmp, L.w_attn_post, cur, L.w_ffn, other, eps, d->gu, st))
+            return -1;
+        std::swap(cur, other);
+        // down_out = W_down . (gelu(gate) * up)
+        if (launch_gemv_direct_geglu(ctx, *down, d->gu, d->tmp, st)) return -1;
+        launches += 5;
     }
     if (generate) {
+        // h = h + rmsnorm_delta(down_out, ffn_post); logits = W_lm . rmsnorm_delta(h, final)
+        launch_pdl(residual_norm_kernel, dim3(1), dim3(kNormThreads), 0, st, (const float *)d->tmp,
+                   (const float *)d->layers[c.layers - 1].w_ffn_post, cur, (const float *)d->w_final, d->norm,
+                   c.hidden, eps);
+        if (check_launch(d, "final norm")) return -1;
         const DevWeight *head = weight_of(d, d->lm_head);
         if (!head) return -1;
         if (launch_gemv_best(ctx, *head, d->norm, d->logits, st)) return -1;
@@ -608,7 +668,7 @@ int enqueue_step(sapphire_decoder_t *d, bool generate, cudaStream_t st) {
                    c.vocab, reinterpret_cast<Top2 *>(d->top2_part), d->counters + 1, d->state, d->out_tokens,
                    d->out_margins);
         if (check_launch(d, "argmax")) return -1;
-        launches += 2;
+        launches += 3;
     } else {
         launch_pdl(prompt_advance_kernel, dim3(1), dim3(1), 0, st, d->state, (const int *)d->prompt);
         if (check_launch(d, "prompt advance")) return -1;
@@ -722,6 +782,18 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
         }
         if (!ok) break;
         ok = false;
+        bool direct = true;
+        for (auto &L : d->layers)
+            for (tensor_t *t : {L.qkv, L.o, L.gu, L.down}) {
+                const DevWeight *dw = weight_of(d, t);
+                direct = direct && dw && dw->ntiles <= kDirectMaxTiles && direct_supported(*dw);
+            }
+        if (!direct) {
+            ctx_fail(ctx, "sapphire_decoder_create",
+                     "projection shapes outside the fused decode GEMV (at most %d rows and 2048 columns)",
+                     kDirectMaxTiles * 32);
+            break;
+        }
         if (!(d->lm_head = concat_q4(d, {{w->lm_head, c.vocab}}, c.hidden))) break;
         if (upload_floats(d, &d->w_final, w->final_norm, c.hidden)) break;
         const size_t emb = (size_t)c.vocab * c.hidden;
@@ -740,11 +812,12 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             break;
         const size_t kv = (size_t)c.layers * c.kv_heads * c.context * c.head_dim;
         if (upload_floats(d, &d->kcache, nullptr, kv) || upload_floats(d, &d->vcache, nullptr, kv)) break;
-        if (dev_alloc(d, (void **)&d->hidden, c.hidden * 4) || dev_alloc(d, (void **)&d->norm, c.hidden * 4) ||
+        if (dev_alloc(d, (void **)&d->hidden, c.hidden * 4) || dev_alloc(d, (void **)&d->hidden2, c.hidden * 4) ||
+            dev_alloc(d, (void **)&d->norm, c.hidden * 4) ||
             dev_alloc(d, (void **)&d->qkv, (size_t)(d->q_dim + 2 * d->kv_dim) * 4) ||
             dev_alloc(d, (void **)&d->attn, (size_t)d->q_dim * 4) ||
             dev_alloc(d, (void **)&d->tmp, (size_t)c.hidden * 4) ||
-            dev_alloc(d, (void **)&d->gu, (size_t)2 * c.ffn * 4) || dev_alloc(d, (void **)&d->act, (size_t)c.ffn * 4) ||
+            dev_alloc(d, (void **)&d->gu, (size_t)2 * c.ffn * 4) ||
             dev_alloc(d, (void **)&d->logits, (size_t)c.vocab * 4) ||
             dev_alloc(d, (void **)&d->attn_part, (size_t)kAttnSplit * c.heads * (c.head_dim + 2) * 4) ||
             dev_alloc(d, &d->top2_part, (size_t)kArgmaxBlocks * sizeof(Top2)) ||

@@ -203,6 +203,14 @@ int pipe_kmax(long long T, long long W, int nseg);
 // 32-row tile, no scratch.
 bool direct_supported(const DevWeight &w);
 int launch_gemv_direct(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t stream);
+// The same with x produced inside the kernel (decode fusion): the residual
+// update h_out = h_in + rmsnorm_delta(t, w_post) (stored by block 0) and
+// x = rmsnorm_delta(h_out, w_next); or x = gelu(gu[:cols]) * gu[cols:].
+int launch_gemv_direct_resnorm(kernel_context_t *ctx, const DevWeight &w, const float *t, const float *w_post,
+                               const float *h_in, const float *w_next, float *h_out, float eps, float *y,
+                               cudaStream_t stream);
+int launch_gemv_direct_geglu(kernel_context_t *ctx, const DevWeight &w, const float *gu, float *y,
+                             cudaStream_t stream);
 // Weights of at most this many 32-row tiles take the direct kernel.
 constexpr int kDirectMaxTiles = 512;
 // Batch-1 product through the pipelined kernel when it applies, else the
