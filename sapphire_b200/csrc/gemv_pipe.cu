@@ -963,28 +963,81 @@ __global__ void __launch_bounds__(kDirectWarps * 32) gemv_direct(const PipeParam
     if (threadIdx.x == 0) s_nonfinite = 0;
     pdl_wait();
     __syncthreads();
-    XPrep xp;
-    xp.digits = smem;
-    const size_t dig_bytes = align16((size_t)p.nb * kDigitBytesPerBlock + 16);
-    xp.pexp = reinterpret_cast<float *>(smem + dig_bytes);
-    xp.corr = reinterpret_cast<int *>(smem + dig_bytes + align16((size_t)p.nb * 4));
-    xp.nonfinite = &s_nonfinite;
-    float *xs = nullptr;
-    if constexpr (XM != kXPlain) {
-        xs = reinterpret_cast<float *>(smem + ((ximage_bytes(DT, p.nb, p.kchunks) + 15) & ~(size_t)15));
-        produce_x<XM>(p, f, xs, red);
-    }
-    prepare_x<DT, kDirectWarps>(p, xp, xs);
-    __syncthreads();
-    MmaAcc acc;
-    acc.reset();
-#pragma unroll
-    for (int k = 0; k < kDirectMaxItems; ++k) {
-        const int seg = warp + k * kDirectWarps;
-        if (seg < p.nseg) compute_item(R[k], seg * 4, p.nb, lane, xp, nullptr, acc);
-    }
     unsigned long long v[4];
-    tile_rows<DT>(acc, v);
+    if constexpr (DT == DTYPE_Q4_0) {
+        // Q4_0: fp32 x in shared memory and FFMA dot products: per block and
+        // row sum_j (q_j - 8) x_j, then one multiply by the block scale.  No
+        // digit image is built, which is what bounds a GEMV this small.
+        float *xs = reinterpret_cast<float *>(smem);
+        if constexpr (XM != kXPlain) {
+            produce_x<XM>(p, f, xs, red);
+        } else {
+            // Non-finite x values propagate through the fp32 arithmetic as in
+            // the reference's row kernels.
+            for (int i = threadIdx.x; i < p.nb * 32; i += blockDim.x) xs[i] = i < p.cols ? __ldg(p.x + i) : 0.0f;
+            __syncthreads();
+        }
+        const int tig = lane & 3;
+        float r[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int k = 0; k < kDirectMaxItems; ++k) {
+            const int seg = warp + k * kDirectWarps;
+            if (seg >= p.nseg) continue;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int b = seg * 4 + u;
+                if (b >= p.nb) break;
+                const float4 x0 = *reinterpret_cast<const float4 *>(xs + b * 32 + tig * 8);
+                const float4 x1 = *reinterpret_cast<const float4 *>(xs + b * 32 + tig * 8 + 4);
+                const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const uint32_t w[4] = {R[k].a[u].x, R[k].a[u].y, R[k].a[u].z, R[k].a[u].w};
+                const float sc[4] = {R[k].s[u].x, R[k].s[u].y, R[k].s[u].z, R[k].s[u].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
+                    float dot = 0.0f;
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        // 0x4B0000nn is the float 2^23 + n; subtracting 2^23 + 8 leaves n - 8 exactly.
+                        const float q0 = __int_as_float((int)__byte_perm(lo, 0x4B000000u, 0x7440u | m)) - 8388616.0f;
+                        const float q1 = __int_as_float((int)__byte_perm(hi, 0x4B000000u, 0x7440u | m)) - 8388616.0f;
+                        dot = fmaf(q0, xv[2 * m], dot);
+                        dot = fmaf(q1, xv[2 * m + 1], dot);
+                    }
+                    r[i] = fmaf(sc[i], dot, r[i]);
+                }
+            }
+        }
+        // rows g + 8i: sum the four lanes of the row group
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            r[i] += __shfl_xor_sync(0xffffffffu, r[i], 1);
+            r[i] += __shfl_xor_sync(0xffffffffu, r[i], 2);
+            v[i] = __float_as_uint(r[i]);
+        }
+    } else {
+        XPrep xp;
+        xp.digits = smem;
+        const size_t dig_bytes = align16((size_t)p.nb * kDigitBytesPerBlock + 16);
+        xp.pexp = reinterpret_cast<float *>(smem + dig_bytes);
+        xp.corr = reinterpret_cast<int *>(smem + dig_bytes + align16((size_t)p.nb * 4));
+        xp.nonfinite = &s_nonfinite;
+        float *xs = nullptr;
+        if constexpr (XM != kXPlain) {
+            xs = reinterpret_cast<float *>(smem + ((ximage_bytes(DT, p.nb, p.kchunks) + 15) & ~(size_t)15));
+            produce_x<XM>(p, f, xs, red);
+        }
+        prepare_x<DT, kDirectWarps>(p, xp, xs);
+        __syncthreads();
+        MmaAcc acc;
+        acc.reset();
+#pragma unroll
+        for (int k = 0; k < kDirectMaxItems; ++k) {
+            const int seg = warp + k * kDirectWarps;
+            if (seg < p.nseg) compute_item(R[k], seg * 4, p.nb, lane, xp, nullptr, acc);
+        }
+        tile_rows<DT>(acc, v);
+    }
     if ((lane & 3) == 0) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) part[warp][(lane >> 2) + 8 * i] = __uint_as_float((uint32_t)v[i]);
@@ -1029,8 +1082,12 @@ int direct_common(kernel_context_t *ctx, const DevWeight &w, const float *x, flo
     p.ntiles = w.ntiles;
     p.kchunks = w.kchunks;
     p.nseg = (w.nb + 3) / 4;
-    size_t smem = ximage_bytes(w.dtype, w.nb, w.kchunks);
-    if (mode != kXPlain) smem = ((smem + 15) & ~(size_t)15) + (size_t)w.nb * 32 * sizeof(float);
+    // Q4_0: the fp32 x vector only; Q8_0: the digit image (+ the fp32 vector of a fused producer).
+    size_t smem = (size_t)w.nb * 32 * sizeof(float);
+    if (w.dtype != DTYPE_Q4_0) {
+        smem = ximage_bytes(w.dtype, w.nb, w.kchunks);
+        if (mode != kXPlain) smem = ((smem + 15) & ~(size_t)15) + (size_t)w.nb * 32 * sizeof(float);
+    }
     cudaError_t e = mode == kXResNorm ? direct_launch<kXResNorm>(w, p, f, smem, st)
                   : mode == kXGeGLU   ? direct_launch<kXGeGLU>(w, p, f, smem, st)
                                       : direct_launch<kXPlain>(w, p, f, smem, st);
