@@ -231,12 +231,23 @@ __device__ __forceinline__ void digits3(int X, int &d0, int &d1, int &d2) {
     d2 = (X1 - d1) >> 8;
 }
 
-// Exponent e with max|x| * 2^e < 2^22 (0 for an all-zero block).
+// Exponent e with max|x| * 2^e < 2^22 (0 for an all-zero block).  For a
+// normal m the frexp exponent is the biased exponent field minus 126.
 __device__ __forceinline__ int block_exponent(float m) {
     if (!(m > 0.0f)) return 0;
+    const int be = (__float_as_int(m) >> 23) & 0xFF;
     int E;
-    frexpf(m, &E);
+    if (be != 0) {
+        E = be - 126;
+    } else {
+        frexpf(m, &E);
+    }
     return 22 - E;
+}
+
+// v * 2^e, exact: a multiply by the power of two while 2^e is a normal float.
+__device__ __forceinline__ float mul_pow2(float v, int e) {
+    return (e >= -126 && e <= 127) ? v * __int_as_float((e + 127) << 23) : ldexpf(v, e);
 }
 
 // Byte offset of x position p (0..31) of a block inside its 32-byte digit
@@ -280,7 +291,7 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = 
         m = 0.0f;
         for (int i = 0; i < NW; ++i) m = fmaxf(m, s_red[i]);
         gexp = block_exponent(isfinite(m) ? m : FLT_MAX);
-        if (threadIdx.x == 0) xp.pexp[0] = ldexpf(1.0f, -gexp);
+        if (threadIdx.x == 0) xp.pexp[0] = mul_pow2(1.0f, -gexp);
     }
     // Blocks b = warp + NW*u: the loads of kGroup blocks are issued together,
     // then each block is converted.
@@ -303,9 +314,9 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = 
                 float m = fabsf(v);
                 for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
                 e = block_exponent(isfinite(m) ? m : FLT_MAX);
-                if (lane == 0) xp.pexp[b] = ldexpf(1.0f, -e);
+                if (lane == 0) xp.pexp[b] = mul_pow2(1.0f, -e);
             }
-            const int X = isfinite(v) ? __float2int_rn(ldexpf(v, e)) : 0;
+            const int X = isfinite(v) ? __float2int_rn(mul_pow2(v, e)) : 0;
             int d0, d1, d2;
             digits3(X, d0, d1, d2);
             uint8_t *row = xp.digits + (size_t)b * kDigitBytesPerBlock;
