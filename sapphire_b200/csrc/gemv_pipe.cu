@@ -54,6 +54,7 @@ constexpr PipeCfg kPipeConfigs[] = {{12, 3}, {8, 4}, {16, 2}};
 constexpr int kMaxPipeWarps = 16;
 constexpr unsigned kWaitLimit = 1u << 26;
 constexpr int kDigitBytesPerBlock = 96;       // 3 digit rows x 4 lanes x 8 bytes
+constexpr int kTq2RegBlocks = 48;             // ternary x blocks per warp held in registers
 
 // ------------------------------------------------------------ PTX helpers --
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -273,9 +274,53 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ float s_red[kMaxPipeWarps];
     int gexp = 0;
-    if (DT == DTYPE_TQ2_0) {
+    if (DT == DTYPE_TQ2_0 && !xs_smem && (p.nb + NW - 1) / NW <= kTq2RegBlocks) {
         // One exponent for the whole row (the ternary sum runs over all of K
-        // in int32).  Loads are unrolled so each thread has 8 in flight.
+        // in int32).  Lane `lane` of warp w needs element `lane` of blocks
+        // w + NW*k: all of them are loaded into registers at once (one L2
+        // round trip), reduced for the exponent and converted from registers.
+        float v[kTq2RegBlocks];
+        const int per = (p.nb + NW - 1) / NW;
+        float m = 0.0f;
+        bool bad = false;
+#pragma unroll
+        for (int k = 0; k < kTq2RegBlocks; ++k) {
+            const int c = (warp + NW * k) * 32 + lane;
+            v[k] = (k < per && c < p.cols) ? __ldg(p.x + c) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < kTq2RegBlocks; ++k) {
+            bad |= !isfinite(v[k]);
+            m = fmaxf(m, fabsf(v[k]));
+        }
+        if (bad) *xp.nonfinite = 1;
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_red[warp] = m;
+        __syncthreads();
+        m = 0.0f;
+        for (int i = 0; i < NW; ++i) m = fmaxf(m, s_red[i]);
+        gexp = block_exponent(isfinite(m) ? m : FLT_MAX);
+        if (threadIdx.x == 0) xp.pexp[0] = mul_pow2(1.0f, -gexp);
+        const int off = digit_slot<DT>(lane);
+#pragma unroll
+        for (int k = 0; k < kTq2RegBlocks; ++k) {
+            const int b = warp + NW * k;
+            if (k < per && b < p.nb) {
+                const int X = isfinite(v[k]) ? __float2int_rn(mul_pow2(v[k], gexp)) : 0;
+                int d0, d1, d2;
+                digits3(X, d0, d1, d2);
+                uint8_t *row = xp.digits + (size_t)b * kDigitBytesPerBlock;
+                row[0 * 32 + off] = (uint8_t)(int8_t)d0;
+                row[1 * 32 + off] = (uint8_t)(int8_t)d1;
+                row[2 * 32 + off] = (uint8_t)(int8_t)d2;
+            }
+        }
+        if (threadIdx.x < 4) reinterpret_cast<uint32_t *>(xp.digits + (size_t)p.nb * kDigitBytesPerBlock)[threadIdx.x] = 0;
+        return;
+    }
+    if (DT == DTYPE_TQ2_0) {
+        // Rows too long for the register path: loads unrolled so each thread
+        // has 8 in flight.
         float m = 0.0f;
         bool bad = false;
 #pragma unroll 8
