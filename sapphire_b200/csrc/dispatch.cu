@@ -86,8 +86,17 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
         float *recv = ctx->d_g + slice;
         if (w->nrows < per) CUDA_TRY(ctx, cudaMemsetAsync(send, 0, slice * sizeof(float), st));
         if (launch_product(ctx, *w, xd, cols, send, per, batch, st)) return -1;
-        if (shard_allgather(ctx, send, recv, slice, st)) return -1;
         const cudaMemcpyKind kind = y_on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+        if (batch == 1) {
+            // Rank r's rows start at r * per, its slot in the gathered buffer:
+            // gather straight into y when it holds world * per rows, else copy
+            // the first `rows` values once.
+            const bool direct = y_on_dev && (size_t)per * ctx->world == (size_t)rows;
+            if (shard_allgather(ctx, send, direct ? Y : recv, slice, st)) return -1;
+            if (!direct) CUDA_TRY(ctx, cudaMemcpyAsync(Y, recv, (size_t)rows * sizeof(float), kind, st));
+            goto gathered;
+        }
+        if (shard_allgather(ctx, send, recv, slice, st)) return -1;
         for (int r = 0; r < ctx->world; ++r) {
             int row0 = 0, nr = 0;
             shard_rows(rows, r, ctx->world, &row0, &nr);
@@ -95,6 +104,7 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
             CUDA_TRY(ctx, cudaMemcpy2DAsync(Y + row0, (size_t)rows * sizeof(float), recv + (size_t)r * slice,
                                             (size_t)per * sizeof(float), (size_t)nr * sizeof(float), batch, kind, st));
         }
+    gathered:;
     }
     if (sync) {
         cudaError_t e = cudaStreamSynchronize(st);
