@@ -84,27 +84,33 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
         if (ensure_scratch(ctx, &ctx->d_g, &ctx->d_g_cap, (slice * (ctx->world + 1)) * sizeof(float))) return -1;
         float *send = ctx->d_g;
         float *recv = ctx->d_g + slice;
-        if (w->nrows < per) CUDA_TRY(ctx, cudaMemsetAsync(send, 0, slice * sizeof(float), st));
-        if (launch_product(ctx, *w, xd, cols, send, per, batch, st)) return -1;
+        int prc = 0;
         const cudaMemcpyKind kind = y_on_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
-        if (batch == 1) {
-            // Rank r's rows start at r * per, its slot in the gathered buffer:
-            // gather straight into y when it holds world * per rows, else copy
-            // the first `rows` values once.
-            const bool direct = y_on_dev && (size_t)per * ctx->world == (size_t)rows;
-            if (shard_allgather(ctx, send, direct ? Y : recv, slice, st)) return -1;
-            if (!direct) CUDA_TRY(ctx, cudaMemcpyAsync(Y, recv, (size_t)rows * sizeof(float), kind, st));
-            goto gathered;
+        if (batch == 1 && shard_peer_product(ctx, *w, xd, Y, rows, per, y_on_dev, &prc)) {
+            // gathered over peer memory by the GEMV itself
+            if (prc) return -1;
+        } else {
+            if (w->nrows < per) CUDA_TRY(ctx, cudaMemsetAsync(send, 0, slice * sizeof(float), st));
+            if (launch_product(ctx, *w, xd, cols, send, per, batch, st)) return -1;
+            if (batch == 1) {
+                // Rank r's rows start at r * per, its slot in the gathered
+                // buffer: gather straight into y when it holds world * per
+                // rows, else copy the first `rows` values once.
+                const bool direct = y_on_dev && (size_t)per * ctx->world == (size_t)rows;
+                if (shard_allgather(ctx, send, direct ? Y : recv, slice, st)) return -1;
+                if (!direct) CUDA_TRY(ctx, cudaMemcpyAsync(Y, recv, (size_t)rows * sizeof(float), kind, st));
+            } else {
+                if (shard_allgather(ctx, send, recv, slice, st)) return -1;
+                for (int r = 0; r < ctx->world; ++r) {
+                    int row0 = 0, nr = 0;
+                    shard_rows(rows, r, ctx->world, &row0, &nr);
+                    if (nr == 0) continue;
+                    CUDA_TRY(ctx, cudaMemcpy2DAsync(Y + row0, (size_t)rows * sizeof(float), recv + (size_t)r * slice,
+                                                    (size_t)per * sizeof(float), (size_t)nr * sizeof(float), batch,
+                                                    kind, st));
+                }
+            }
         }
-        if (shard_allgather(ctx, send, recv, slice, st)) return -1;
-        for (int r = 0; r < ctx->world; ++r) {
-            int row0 = 0, nr = 0;
-            shard_rows(rows, r, ctx->world, &row0, &nr);
-            if (nr == 0) continue;
-            CUDA_TRY(ctx, cudaMemcpy2DAsync(Y + row0, (size_t)rows * sizeof(float), recv + (size_t)r * slice,
-                                            (size_t)per * sizeof(float), (size_t)nr * sizeof(float), batch, kind, st));
-        }
-    gathered:;
     }
     if (sync) {
         cudaError_t e = cudaStreamSynchronize(st);

@@ -179,7 +179,25 @@ struct PipeParams {
     int *err;                   // error word
     long long total_items;
     int nrows, cols, nb, ntiles, kchunks, nseg, kmax, total_warps;
+    // Row-sharded products gathered over peer memory: when ll_n > 0 row r is
+    // not stored at y[r] but sent to every rank k as the 8-byte word
+    // (ll_epoch << 32 | bits of the value) at ll[k][ll_off + r] (NVLink stores;
+    // an aligned 8-byte store arrives whole, so the epoch marks the value
+    // valid and no fence is needed).
+    int ll_n, ll_off;
+    unsigned ll_epoch;
+    unsigned long long *ll[kMaxPeers];
 };
+
+__device__ __forceinline__ void store_y(const PipeParams &p, size_t r, float v) {
+    if (p.ll_n) {
+        const unsigned long long word = ((unsigned long long)p.ll_epoch << 32) | __float_as_uint(v);
+        for (int k = 0; k < p.ll_n; ++k)
+            asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p.ll[k] + (size_t)p.ll_off + r), "l"(word) : "memory");
+    } else {
+        p.y[r] = v;
+    }
+}
 
 __device__ __forceinline__ long long range_begin(long long w, long long T, long long W) { return (w * T) / W; }
 __device__ __forceinline__ int item_owner(long long i, long long T, long long W) {
@@ -643,7 +661,7 @@ __device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int l
 #pragma unroll
             for (int i = 0; i < kRows; ++i) {
                 const int r = row_of(i);
-                if (tile * 32 + r < p.nrows) p.y[(size_t)tile * 32 + r] = finish_row<DT>(p, xp, tile, r, v[i], nonfinite);
+                if (tile * 32 + r < p.nrows) store_y(p, (size_t)tile * 32 + r, finish_row<DT>(p, xp, tile, r, v[i], nonfinite));
             }
         }
         return;
@@ -688,7 +706,7 @@ __device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int l
                     for (int j = 0; j < k; ++j) s += __ldcg(base32 + (size_t)j * 32 + r);
                     sum = __float_as_uint(s);
                 }
-                if (tile * 32 + r < p.nrows) p.y[(size_t)tile * 32 + r] = finish_row<DT>(p, xp, tile, r, sum, nonfinite);
+                if (tile * 32 + r < p.nrows) store_y(p, (size_t)tile * 32 + r, finish_row<DT>(p, xp, tile, r, sum, nonfinite));
             }
         }
         __syncwarp();
@@ -1213,9 +1231,23 @@ void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_f
 // err: scratch sized by pipe_scratch_size (counters zero), error word.
 int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
                      int *err, cudaStream_t st) {
+    return launch_gemv_pipe_ll(ctx, w, x, y, part, cnt, err, nullptr, 0, 0, 0u, st);
+}
+
+int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
+                        int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
+                        cudaStream_t st) {
     if (w.ntiles == 0) return 0;
+    if (ll_n < 0 || ll_n > kMaxPeers) {
+        ctx_fail(ctx, "launch_gemv_pipe", "%d gather targets (at most %d)", ll_n, kMaxPeers);
+        return -1;
+    }
     const PipeCfg c = pipe_cfg();
     PipeParams p;
+    p.ll_n = ll_n;
+    p.ll_off = ll_off;
+    p.ll_epoch = ll_epoch;
+    for (int k = 0; k < kMaxPeers; ++k) p.ll[k] = k < ll_n ? ll[k] : nullptr;
     p.codes = reinterpret_cast<const uint8_t *>(w.codes);
     p.scales = w.scales;
     p.x = x;

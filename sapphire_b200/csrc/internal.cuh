@@ -16,6 +16,20 @@
 
 // Rows per tile of the GEMV device layout: one warp lane owns one row.
 constexpr int kTileRows = 32;
+// Most ranks a peer-memory gather serves.
+constexpr int kMaxPeers = 8;
+
+// Peer-memory gather of row-sharded batch-1 products (shard.cu): each rank's
+// allocation holds two buffers of cap_rows 8-byte words (value | epoch << 32),
+// used alternately by epoch parity; peer[k] maps rank k's allocation.
+struct PeerGather {
+    bool tried = false, ready = false;
+    size_t cap_rows = 0;
+    unsigned long long *local = nullptr;
+    unsigned long long *peer[kMaxPeers] = {};
+    unsigned epoch = 0;
+};
+
 
 // Device copy of one weight tensor, re-laid out for the GEMV kernels.
 //
@@ -102,6 +116,7 @@ struct sapphire_context {
     // Row sharding (NCCL); world == 1 means unsharded.
     int rank = 0, world = 1;
     void *nccl_comm = nullptr;   // ncclComm_t
+    PeerGather *pg = nullptr;    // peer-memory gather, set up on first use
 
     std::string last_error;
 };
@@ -199,6 +214,11 @@ void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_f
 int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part,
                      int *cnt, int *err, cudaStream_t stream);
 int pipe_kmax(long long T, long long W, int nseg);
+// The pipelined GEMV sending each row r as (epoch << 32 | value bits) to
+// ll[k][ll_off + r] for the ll_n ranks of a peer-memory gather (ll_n == 0: y[r]).
+int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
+                        int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
+                        cudaStream_t stream);
 // Latency-bound GEMV of a small Q8_0 / Q4_0 weight (gemv_pipe.cu): one CTA per
 // 32-row tile, no scratch.
 bool direct_supported(const DevWeight &w);
@@ -239,6 +259,11 @@ int launch_gemm_tc_bf16(kernel_context_t *ctx, const DevWeight &w, const void *x
 int shard_allgather(kernel_context_t *ctx, const float *send, float *recv, size_t count,
                     cudaStream_t stream);
 void shard_destroy(kernel_context_t *ctx);
+// Batch-1 sharded product gathered over peer memory into y[0, rows): true if
+// it ran (every rank decides the same from the arguments); false means use the
+// NCCL path.  -1 through *rc on error.
+bool shard_peer_product(kernel_context_t *ctx, const DevWeight &w, const float *x, float *Y, int rows, int per,
+                        bool y_on_dev, int *rc);
 
 // Rows owned by `rank` of `world` for a tensor of `rows` rows.
 inline void shard_rows(int rows, int rank, int world, int *row0, int *nrows) {

@@ -9,6 +9,7 @@
 // bundled with PyTorch) reuses that copy instead of pinning a second one.
 #include <cstring>
 #include <dlfcn.h>
+#include <vector>
 #include <mutex>
 #include <nccl.h>
 
@@ -20,6 +21,8 @@ struct NcclApi {
     ncclResult_t (*getUniqueId)(ncclUniqueId *) = nullptr;
     ncclResult_t (*commInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*allGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*allReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
     ncclResult_t (*commDestroy)(ncclComm_t) = nullptr;
     const char *(*getErrorString)(ncclResult_t) = nullptr;
 };
@@ -38,9 +41,11 @@ const NcclApi &nccl() {
         api.getUniqueId = (decltype(api.getUniqueId))dlsym(h, "ncclGetUniqueId");
         api.commInitRank = (decltype(api.commInitRank))dlsym(h, "ncclCommInitRank");
         api.allGather = (decltype(api.allGather))dlsym(h, "ncclAllGather");
+        api.allReduce = (decltype(api.allReduce))dlsym(h, "ncclAllReduce");
         api.commDestroy = (decltype(api.commDestroy))dlsym(h, "ncclCommDestroy");
         api.getErrorString = (decltype(api.getErrorString))dlsym(h, "ncclGetErrorString");
-        api.ok = api.getUniqueId && api.commInitRank && api.allGather && api.commDestroy && api.getErrorString;
+        api.ok = api.getUniqueId && api.commInitRank && api.allGather && api.allReduce && api.commDestroy &&
+                  api.getErrorString;
         if (!api.ok) LOG_ERROR("NCCL library lacks an expected entry point");
     });
     return api;
@@ -140,7 +145,160 @@ int shard_allgather(kernel_context_t *ctx, const float *send, float *recv, size_
     return 0;
 }
 
+// ---------------------------------------------------- peer-memory gather --
+// A row-sharded batch-1 product gathered without NCCL, in the manner of a
+// low-latency protocol: the GEMV of every rank sends each finished row to all
+// ranks as one 8-byte word (value | epoch << 32) over NVLink; an aligned
+// 8-byte store arrives whole, so a word carrying the current epoch holds the
+// current value and no fence or barrier is needed.  ll_pull_kernel then waits
+// for each word of the rank's own buffer to carry the epoch (bounded by time;
+// one that expires sets bit 3 of *err and leaves NaN) and writes the values to
+// y.  Two buffers alternate by epoch parity: a rank writes the buffer of epoch
+// e + 2 only after its pull of e + 1, which waited for every rank's GEMV of
+// e + 1, which each rank started after its own pull of epoch e had finished.
+namespace {
+constexpr unsigned long long kPeerWaitNs = 2000000000ull;
+constexpr int kPullThreads = 256;
+
+__global__ void __launch_bounds__(kPullThreads) ll_pull_kernel(const unsigned long long *ll, long long rows,
+                                                               unsigned epoch, float *y, int *err) {
+    pdl_trigger();
+    pdl_wait();
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < rows; i += stride) {
+        unsigned long long w;
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(ll + i) : "memory");
+        if ((unsigned)(w >> 32) != epoch) {
+            uint64_t t0;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+            for (;;) {
+                __nanosleep(64);
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(ll + i) : "memory");
+                if ((unsigned)(w >> 32) == epoch) break;
+                uint64_t t;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                if (t - t0 > kPeerWaitNs) {
+                    atomicOr(err, 8);
+                    w = 0x7FC00000ull;   // NaN
+                    break;
+                }
+            }
+        }
+        y[i] = __uint_as_float((unsigned)(w & 0xFFFFFFFFull));
+    }
+}
+
+int nccl_allgather_bytes(kernel_context_t *ctx, const void *mine, void *all, size_t bytes) {
+    uint8_t *d = nullptr;
+    CUDA_TRY(ctx, cudaMalloc(&d, bytes * (ctx->world + 1)));
+    int rc = -1;
+    do {
+        if (cudaMemcpy(d, mine, bytes, cudaMemcpyHostToDevice) != cudaSuccess) break;
+        if (nccl().allGather(d, d + bytes, bytes, ncclUint8, (ncclComm_t)ctx->nccl_comm, ctx->stream) != ncclSuccess)
+            break;
+        if (cudaMemcpyAsync(all, d + bytes, bytes * ctx->world, cudaMemcpyDeviceToHost, ctx->stream) != cudaSuccess)
+            break;
+        if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) break;
+        rc = 0;
+    } while (false);
+    cudaFree(d);
+    cudaGetLastError();
+    return rc;
+}
+
+// Collective: every rank of the group calls it at the same product.  The
+// gather is used only if every rank mapped every peer (agreed over NCCL).
+void peer_gather_setup(kernel_context_t *ctx) {
+    PeerGather *g = new PeerGather();
+    ctx->pg = g;
+    g->tried = true;
+    if (ctx->world > kMaxPeers) return;
+    g->cap_rows = (size_t)4 << 20;   // y of up to 4M rows; 2 x 32 MB per rank
+    const size_t bytes = 2 * g->cap_rows * sizeof(unsigned long long);
+    int ok = 1;
+    cudaIpcMemHandle_t mine{};
+    if (cudaMalloc(&g->local, bytes) != cudaSuccess || cudaMemset(g->local, 0, bytes) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&mine, g->local) != cudaSuccess)
+        ok = 0;
+    cudaGetLastError();
+    std::vector<cudaIpcMemHandle_t> all(ctx->world);
+    if (nccl_allgather_bytes(ctx, &mine, all.data(), sizeof mine)) return;   // no agreement possible: NCCL path
+    for (int k = 0; k < ctx->world && ok; ++k) {
+        if (k == ctx->rank) {
+            g->peer[k] = g->local;
+        } else if (cudaIpcOpenMemHandle(reinterpret_cast<void **>(&g->peer[k]), all[k],
+                                        cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            g->peer[k] = nullptr;
+            ok = 0;
+        }
+    }
+    cudaGetLastError();
+    // Every rank must agree (a mixed decision would leave ranks waiting on
+    // each other): AND of the ranks' results.
+    std::vector<int> oks(ctx->world, 0);
+    if (nccl_allgather_bytes(ctx, &ok, oks.data(), sizeof ok)) return;
+    bool all_ok = true;
+    for (int v : oks) all_ok = all_ok && v == 1;
+    g->ready = all_ok;
+    if (!all_ok) LOG_WARN("peer-memory gather unavailable; sharded products use NCCL");
+}
+}  // namespace
+
+bool shard_peer_product(kernel_context_t *ctx, const DevWeight &w, const float *x, float *Y, int rows, int per,
+                        bool y_on_dev, int *rc) {
+    *rc = 0;
+    // The decision depends only on arguments every rank shares (the pipelined
+    // kernel is used on every rank, whatever its local row count).
+    if (ctx->world > kMaxPeers || (size_t)per * ctx->world > ((size_t)4 << 20) || !pipe_supported(w)) return false;
+    if (!ctx->pg) peer_gather_setup(ctx);
+    PeerGather &g = *ctx->pg;
+    if (!g.ready || (size_t)per * ctx->world > g.cap_rows) return false;
+    *rc = -1;
+    cudaStream_t st = ctx->stream;
+    const unsigned epoch = ++g.epoch;
+    const size_t buf = (size_t)(epoch & 1u) * g.cap_rows;
+    unsigned long long *targets[kMaxPeers];
+    for (int k = 0; k < ctx->world; ++k) targets[k] = g.peer[k] + buf;
+    size_t pf = 0, ci = 0;
+    pipe_scratch_size(ctx, w, &pf, &ci);
+    if (ensure_pipe_scratch(ctx, pf, ci)) return true;
+    if (w.ntiles > 0 && launch_gemv_pipe_ll(ctx, w, x, nullptr, ctx->d_part, ctx->d_cnt, ctx->d_err, targets,
+                                            ctx->world, w.row0, epoch, st))
+        return true;
+    float *yd = Y;
+    if (!y_on_dev) {
+        if (ensure_scratch(ctx, &ctx->d_y, &ctx->d_y_cap, (size_t)rows * sizeof(float))) return true;
+        yd = ctx->d_y;
+    }
+    const int grid = (int)std::max<long long>(1, std::min<long long>(4 * 148, ((long long)rows + kPullThreads - 1) / kPullThreads));
+    cudaError_t e = launch_pdl(ll_pull_kernel, dim3(grid), dim3(kPullThreads), 0, st,
+                               (const unsigned long long *)(g.local + buf), (long long)rows, epoch, yd, ctx->d_err);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        ctx_fail(ctx, "kernel_gemv", "gather launch failed: %s", cudaGetErrorString(e));
+        return true;
+    }
+    if (!y_on_dev) {
+        e = cudaMemcpyAsync(Y, yd, (size_t)rows * sizeof(float), cudaMemcpyDeviceToHost, st);
+        if (e != cudaSuccess) {
+            ctx_fail(ctx, "kernel_gemv", "gather copy-out failed: %s", cudaGetErrorString(e));
+            return true;
+        }
+    }
+    *rc = 0;
+    return true;
+}
+
 void shard_destroy(kernel_context_t *ctx) {
+    if (ctx->pg) {
+        cudaDeviceSynchronize();
+        for (int k = 0; k < kMaxPeers; ++k)
+            if (ctx->pg->peer[k] && k != ctx->rank) cudaIpcCloseMemHandle(ctx->pg->peer[k]);
+        if (ctx->pg->local) cudaFree(ctx->pg->local);
+        cudaGetLastError();
+        delete ctx->pg;
+        ctx->pg = nullptr;
+    }
     if (ctx->nccl_comm) {
         nccl().commDestroy((ncclComm_t)ctx->nccl_comm);
         ctx->nccl_comm = nullptr;

@@ -5,7 +5,8 @@ Each rank binds its context to its GPU, joins the NCCL group (unique id from
 rank 0, passed over a gloo group), and runs the same calls an unsharded
 context would: every rank receives the full result, which must match the
 oracle (the reference row kernels) within the GEMV bar and be the same bytes
-on both ranks.
+on both ranks.  Batch-1 products of the pipelined GEMV are gathered over peer
+memory (NVLink stores and an epoch-flag barrier); batched products over NCCL.
 """
 from __future__ import annotations
 
@@ -23,7 +24,8 @@ Q4_0, Q8_0, TQ2_0 = 3, 4, 5
 
 CASES = [
     # (dtype, rows, cols, batch)
-    (Q8_0, 32768, 640, 1),      # LM-head width, pipelined GEMV per rank
+    (Q8_0, 32768, 640, 1),      # LM-head width, pipelined GEMV per rank, gathered over peer memory
+    (Q8_0, 3001, 640, 1),       # ragged rows: the last rank holds one row fewer
     (TQ2_0, 4096, 4096, 1),     # ternary
     (Q4_0, 3000, 640, 3),       # batched, per-token GEMV; rows not divisible by 2
     (Q4_0, 2048, 2560, 64),     # tensor-core prefill product per rank
@@ -73,6 +75,10 @@ def _rank_main(rank, world, port, out):
             packed, X = _case(o, dtype, rows, cols, batch, seed=100 + i)
             A = sp.Tensor(dtype, (rows, cols), packed)
             Y = sp.gemm(ctx, A, np.ascontiguousarray(X[:, :cols]), batch)
+            # Repeated products alternate the two gather buffers.
+            for _ in range(3):
+                Y2 = sp.gemm(ctx, A, np.ascontiguousarray(X[:, :cols]), batch)
+                assert np.array_equal(Y, Y2)
             A.release()
             mine = torch.from_numpy(Y.copy())
             other = [torch.zeros_like(mine) for _ in range(world)]
