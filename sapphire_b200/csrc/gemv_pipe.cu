@@ -657,13 +657,17 @@ __device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int l
     constexpr int kRows = kMma ? 4 : 1;
     auto row_of = [&](int i) { return kMma ? ((lane >> 2) + 8 * i) : lane; };
     if (whole) {
-        if (owner_lane) {
+        // One row per lane (a warp's stores are 32 consecutive rows): lane l
+        // takes row l = g + 8i from the lane holding it, (l % 8) * 4.
+        unsigned long long mine = v[0];
+        if constexpr (kMma) {
 #pragma unroll
-            for (int i = 0; i < kRows; ++i) {
-                const int r = row_of(i);
-                if (tile * 32 + r < p.nrows) store_y(p, (size_t)tile * 32 + r, finish_row<DT>(p, xp, tile, r, v[i], nonfinite));
+            for (int i = 0; i < 4; ++i) {
+                const unsigned long long t = __shfl_sync(0xffffffffu, v[i], (lane & 7) * 4);
+                if ((lane >> 3) == i) mine = t;
             }
         }
+        if (tile * 32 + lane < p.nrows) store_y(p, (size_t)tile * 32 + lane, finish_row<DT>(p, xp, tile, lane, mine, nonfinite));
         return;
     }
     const long long first = (long long)tile * p.nseg;
@@ -692,23 +696,19 @@ __device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int l
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old == k - 1) {
         __threadfence();
-        if (owner_lane) {
-#pragma unroll
-            for (int i = 0; i < kRows; ++i) {
-                const int r = row_of(i);
-                unsigned long long sum;
-                if (DT == DTYPE_TQ2_0) {
-                    long long s = 0;
-                    for (int j = 0; j < k; ++j) s += __ldcg(base64 + (size_t)j * 32 + r);
-                    sum = (unsigned long long)s;
-                } else {
-                    float s = 0.0f;
-                    for (int j = 0; j < k; ++j) s += __ldcg(base32 + (size_t)j * 32 + r);
-                    sum = __float_as_uint(s);
-                }
-                if (tile * 32 + r < p.nrows) store_y(p, (size_t)tile * 32 + r, finish_row<DT>(p, xp, tile, r, sum, nonfinite));
-            }
+        // The last contributor sums the slots in slot order, one row per lane.
+        const int r = lane;
+        unsigned long long sum;
+        if (DT == DTYPE_TQ2_0) {
+            long long s = 0;
+            for (int j = 0; j < k; ++j) s += __ldcg(base64 + (size_t)j * 32 + r);
+            sum = (unsigned long long)s;
+        } else {
+            float s = 0.0f;
+            for (int j = 0; j < k; ++j) s += __ldcg(base32 + (size_t)j * 32 + r);
+            sum = __float_as_uint(s);
         }
+        if (tile * 32 + r < p.nrows) store_y(p, (size_t)tile * 32 + r, finish_row<DT>(p, xp, tile, r, sum, nonfinite));
         __syncwarp();
         if (lane == 0) p.cnt[tile] = 0;
     }
