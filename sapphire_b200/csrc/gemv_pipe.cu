@@ -859,16 +859,19 @@ size_t pipe_smem(tensor_dtype_t dt, int nb, int kchunks, PipeCfg c) {
     return ximage_bytes(dt, nb, kchunks) + (size_t)c.nw * c.ns * stage + (size_t)c.nw * c.ns * 8;
 }
 
-// The configuration this process uses: SAPPHIRE_PIPE_CFG = index into
-// kPipeConfigs (default 0).
-PipeCfg pipe_cfg() {
+// The configuration of a format: 16 warps x 2 slots for TQ2_0 (its 4 KB
+// items carry four times the weights of a Q8_0 item, so more warps decoding
+// beat deeper rings), 12 x 3 otherwise.  SAPPHIRE_PIPE_CFG = an index into
+// kPipeConfigs selects one for every format (tuning runs).
+PipeCfg pipe_cfg(tensor_dtype_t dt) {
     static const int idx = [] {
         const char *v = getenv("SAPPHIRE_PIPE_CFG");
-        int i = v ? atoi(v) : 0;
+        int i = v ? atoi(v) : -1;
         const int n = (int)(sizeof(kPipeConfigs) / sizeof(kPipeConfigs[0]));
-        return (i >= 0 && i < n) ? i : 0;
+        return (i >= 0 && i < n) ? i : -1;
     }();
-    return kPipeConfigs[idx];
+    if (idx >= 0) return kPipeConfigs[idx];
+    return dt == DTYPE_TQ2_0 ? kPipeConfigs[2] : kPipeConfigs[0];
 }
 
 int item_nseg(const DevWeight &w) {
@@ -1214,7 +1217,7 @@ bool pipe_supported(const DevWeight &w) {
     if (w.dtype != DTYPE_Q8_0 && w.dtype != DTYPE_Q4_0 && w.dtype != DTYPE_TQ2_0 && w.dtype != DTYPE_F32 &&
         w.dtype != DTYPE_BF16)
         return false;
-    return pipe_smem(w.dtype, w.nb, w.kchunks, pipe_cfg()) <= 227 * 1024;
+    return pipe_smem(w.dtype, w.nb, w.kchunks, pipe_cfg(w.dtype)) <= 227 * 1024;
 }
 
 // Scratch in float units: partials [ntiles][kmax][32] (two floats per entry
@@ -1222,7 +1225,7 @@ bool pipe_supported(const DevWeight &w) {
 void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints) {
     const int nseg = item_nseg(w);
     const long long T = (long long)w.ntiles * nseg;
-    const long long W = (long long)sm_count(ctx->device) * pipe_cfg().nw;
+    const long long W = (long long)sm_count(ctx->device) * pipe_cfg(w.dtype).nw;
     *part_floats = (size_t)w.ntiles * pipe_kmax(T, W, nseg) * 32 * (w.dtype == DTYPE_TQ2_0 ? 2 : 1);
     *cnt_ints = (size_t)w.ntiles;
 }
@@ -1242,7 +1245,7 @@ int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *
         ctx_fail(ctx, "launch_gemv_pipe", "%d gather targets (at most %d)", ll_n, kMaxPeers);
         return -1;
     }
-    const PipeCfg c = pipe_cfg();
+    const PipeCfg c = pipe_cfg(w.dtype);
     PipeParams p;
     p.ll_n = ll_n;
     p.ll_off = ll_off;
