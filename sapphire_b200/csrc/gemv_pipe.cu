@@ -294,22 +294,36 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = 
     int gexp = 0;
     if (DT == DTYPE_TQ2_0 && !xs_smem && (p.nb + NW - 1) / NW <= kTq2RegBlocks) {
         // One exponent for the whole row (the ternary sum runs over all of K
-        // in int32).  Lane `lane` of warp w needs element `lane` of blocks
-        // w + NW*k: all of them are loaded into registers at once (one L2
-        // round trip), reduced for the exponent and converted from registers.
-        float v[kTq2RegBlocks];
+        // in int32).  Warp w converts blocks w + NW*k.  Lane `lane` takes
+        // k = 4i + lane/8 and word W = lane%8 of the block's digit rows: the
+        // four x positions whose digits share that word (digit_slot), so the
+        // rows are written as whole words with the 32 lanes on 32 banks.
+        // All values are loaded into registers at once (one L2 round trip),
+        // reduced for the exponent and converted from registers.
+        constexpr int kIter = kTq2RegBlocks / 4;
+        float v[kIter][4];
         const int per = (p.nb + NW - 1) / NW;
+        const int W = lane & 7, sub = lane >> 3;
+        const int s0 = 4 * (W >> 1) + (W & 1);
+        const int src[4] = {s0, s0 + 2, s0 + 16, s0 + 18};
         float m = 0.0f;
         bool bad = false;
 #pragma unroll
-        for (int k = 0; k < kTq2RegBlocks; ++k) {
-            const int c = (warp + NW * k) * 32 + lane;
-            v[k] = (k < per && c < p.cols) ? __ldg(p.x + c) : 0.0f;
+        for (int i = 0; i < kIter; ++i) {
+            const int k = 4 * i + sub, b = warp + NW * k;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int c = b * 32 + src[j];
+                v[i][j] = (k < per && b < p.nb && c < p.cols) ? __ldg(p.x + c) : 0.0f;
+            }
         }
 #pragma unroll
-        for (int k = 0; k < kTq2RegBlocks; ++k) {
-            bad |= !isfinite(v[k]);
-            m = fmaxf(m, fabsf(v[k]));
+        for (int i = 0; i < kIter; ++i) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                bad |= !isfinite(v[i][j]);
+                m = fmaxf(m, fabsf(v[i][j]));
+            }
         }
         if (bad) *xp.nonfinite = 1;
         for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -319,18 +333,32 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = 
         for (int i = 0; i < NW; ++i) m = fmaxf(m, s_red[i]);
         gexp = block_exponent(isfinite(m) ? m : FLT_MAX);
         if (threadIdx.x == 0) xp.pexp[0] = mul_pow2(1.0f, -gexp);
-        const int off = digit_slot<DT>(lane);
+        // x * 2^gexp as two exact multiplies by normal powers of two
+        // (gexp <= 170, so the second factor is at most 2^43).
+        const int e1 = min(max(gexp, -126), 127);
+        const float f1 = __int_as_float((e1 + 127) << 23), f2 = __int_as_float((gexp - e1 + 127) << 23);
 #pragma unroll
-        for (int k = 0; k < kTq2RegBlocks; ++k) {
-            const int b = warp + NW * k;
+        for (int i = 0; i < kIter; ++i) {
+            const int k = 4 * i + sub, b = warp + NW * k;
             if (k < per && b < p.nb) {
-                const int X = isfinite(v[k]) ? __float2int_rn(mul_pow2(v[k], gexp)) : 0;
-                int d0, d1, d2;
-                digits3(X, d0, d1, d2);
-                uint8_t *row = xp.digits + (size_t)b * kDigitBytesPerBlock;
-                row[0 * 32 + off] = (uint8_t)(int8_t)d0;
-                row[1 * 32 + off] = (uint8_t)(int8_t)d1;
-                row[2 * 32 + off] = (uint8_t)(int8_t)d2;
+                // Low bytes of the balanced digits (digits3): X, (X + 128) >> 8,
+                // and that plus 128, >> 8 again.
+                uint32_t b0[4], b1[4], b2[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int X = isfinite(v[i][j]) ? __float2int_rn(v[i][j] * f1 * f2) : 0;
+                    const int X1 = (X + 0x80) >> 8;
+                    b0[j] = (uint32_t)X;
+                    b1[j] = (uint32_t)X1;
+                    b2[j] = (uint32_t)((X1 + 0x80) >> 8);
+                }
+                const uint32_t w0 = __byte_perm(__byte_perm(b0[0], b0[1], 0x40), __byte_perm(b0[2], b0[3], 0x40), 0x5410);
+                const uint32_t w1 = __byte_perm(__byte_perm(b1[0], b1[1], 0x40), __byte_perm(b1[2], b1[3], 0x40), 0x5410);
+                const uint32_t w2 = __byte_perm(__byte_perm(b2[0], b2[1], 0x40), __byte_perm(b2[2], b2[3], 0x40), 0x5410);
+                uint32_t *row = reinterpret_cast<uint32_t *>(xp.digits + (size_t)b * kDigitBytesPerBlock);
+                row[0 * 8 + W] = w0;
+                row[1 * 8 + W] = w1;
+                row[2 * 8 + W] = w2;
             }
         }
         if (threadIdx.x < 4) reinterpret_cast<uint32_t *>(xp.digits + (size_t)p.nb * kDigitBytesPerBlock)[threadIdx.x] = 0;
@@ -670,14 +698,24 @@ __device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int l
         if (tile * 32 + lane < p.nrows) store_y(p, (size_t)tile * 32 + lane, finish_row<DT>(p, xp, tile, lane, mine, nonfinite));
         return;
     }
+    // k = contributors of the tile, slot = this warp's rank among them.
     const long long first = (long long)tile * p.nseg;
-    int k = 0, slot = -1, prev = -1;
-    for (int s = 0; s < p.nseg; ++s) {
-        const int o = item_owner(first + s, p.total_items, p.total_warps);
-        if (o != prev) {
-            if (o == my_warp) slot = k;
-            ++k;
-            prev = o;
+    int k = 0, slot = -1;
+    const int o0 = item_owner(first, p.total_items, p.total_warps);
+    if (p.total_items >= p.total_warps) {
+        // Every warp owns at least one item, so the tile's owners are the
+        // consecutive warps o0..o1 (two 64-bit divisions instead of nseg).
+        k = item_owner(first + p.nseg - 1, p.total_items, p.total_warps) - o0 + 1;
+        slot = my_warp - o0;
+    } else {
+        int prev = -1;
+        for (int s = 0; s < p.nseg; ++s) {
+            const int o = s == 0 ? o0 : item_owner(first + s, p.total_items, p.total_warps);
+            if (o != prev) {
+                if (o == my_warp) slot = k;
+                ++k;
+                prev = o;
+            }
         }
     }
     long long *base64 = reinterpret_cast<long long *>(p.part) + (size_t)tile * p.kmax * 32;
