@@ -285,14 +285,24 @@ __device__ __forceinline__ int digit_slot(int p) {
     }
 }
 
+// The ternary register path (below) reads a long x with one load per element
+// and per lane; `after_loads` runs once those loads are issued.
+template <tensor_dtype_t DT, int NW>
+__host__ __device__ constexpr bool tq2_reg_path(int nb) {
+    return DT == DTYPE_TQ2_0 && (nb + NW - 1) / NW <= kTq2RegBlocks;
+}
+struct NoHook {
+    __device__ void operator()() const {}
+};
+
 // x comes from global memory (p.x), or from an fp32 vector in shared memory
 // when xs_smem is given (the fused producers of gemv_direct).
-template <tensor_dtype_t DT, int NW>
-__device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = nullptr) {
+template <tensor_dtype_t DT, int NW, typename Hook = NoHook>
+__device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = nullptr, Hook after_loads = Hook()) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ float s_red[kMaxPipeWarps];
     int gexp = 0;
-    if (DT == DTYPE_TQ2_0 && !xs_smem && (p.nb + NW - 1) / NW <= kTq2RegBlocks) {
+    if (!xs_smem && tq2_reg_path<DT, NW>(p.nb)) {
         // One exponent for the whole row (the ternary sum runs over all of K
         // in int32).  Warp w converts blocks w + NW*k.  Lane `lane` takes
         // k = 4i + lane/8 and word W = lane%8 of the block's digit rows: the
@@ -317,6 +327,7 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = 
                 v[i][j] = (k < per && b < p.nb && c < p.cols) ? __ldg(p.x + c) : 0.0f;
             }
         }
+        after_loads();
 #pragma unroll
         for (int i = 0; i < kIter; ++i) {
 #pragma unroll
@@ -807,15 +818,22 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_pipe(const PipeParams p) {
     }
     __syncwarp();
     // The weight copies do not depend on earlier kernels: they start before
-    // the wait for the kernel that produced x.
-    if (lane == 0)
-        for (int j = 0; j < NS && j < n_items; ++j) issue(j);
+    // the wait for the kernel that produced x - except on the ternary
+    // register path, whose x loads (a whole long row per CTA) would queue
+    // behind them: there they follow the x loads.
+    auto issue_first = [&]() {
+        if (lane == 0)
+            for (int j = 0; j < NS && j < n_items; ++j) issue(j);
+    };
+    const bool late_issue = tq2_reg_path<DT, NW>(p.nb);
+    if (!late_issue) issue_first();
     pdl_wait();
     __syncthreads();   // s_nonfinite initialised before x preparation writes it
 
     // x image, built once per CTA while the first copies are in flight.
     if (G::kMma) {
-        prepare_x<DT, NW>(p, xp);
+        if (late_issue) prepare_x<DT, NW>(p, xp, nullptr, issue_first);
+        else prepare_x<DT, NW>(p, xp);
     } else {
         const int xpad = dense_xpad(DT, p.kchunks);
         for (int i = threadIdx.x; i < xpad; i += blockDim.x) xs[i] = (i < p.cols) ? p.x[i] : 0.0f;
