@@ -50,7 +50,7 @@ namespace {
 struct PipeCfg {
     int nw, ns;
 };
-constexpr PipeCfg kPipeConfigs[] = {{12, 3}, {8, 4}, {16, 2}};
+constexpr PipeCfg kPipeConfigs[] = {{12, 3}, {8, 4}, {16, 2}, {16, 4}, {12, 6}};
 constexpr int kMaxPipeWarps = 16;
 constexpr unsigned kWaitLimit = 1u << 26;
 constexpr int kDigitBytesPerBlock = 96;       // 3 digit rows x 4 lanes x 8 bytes
@@ -917,9 +917,11 @@ size_t pipe_smem(tensor_dtype_t dt, int nb, int kchunks, PipeCfg c) {
 
 // The configuration of a format: 16 warps x 2 slots for TQ2_0 (its 4 KB
 // items carry four times the weights of a Q8_0 item, so more warps decoding
-// beat deeper rings), 12 x 3 otherwise.  SAPPHIRE_PIPE_CFG = an index into
-// kPipeConfigs selects one for every format (tuning runs).
-PipeCfg pipe_cfg(tensor_dtype_t dt) {
+// beat deeper rings), 16 x 4 for Q4_0 (2.5 KB items) while its rings and x
+// image fit in shared memory, 12 x 3 otherwise.  SAPPHIRE_PIPE_CFG = an index
+// into kPipeConfigs selects one for every format (tuning runs).
+PipeCfg pipe_cfg(const DevWeight &w) {
+    const tensor_dtype_t dt = w.dtype;
     static const int idx = [] {
         const char *v = getenv("SAPPHIRE_PIPE_CFG");
         int i = v ? atoi(v) : -1;
@@ -927,7 +929,9 @@ PipeCfg pipe_cfg(tensor_dtype_t dt) {
         return (i >= 0 && i < n) ? i : -1;
     }();
     if (idx >= 0) return kPipeConfigs[idx];
-    return dt == DTYPE_TQ2_0 ? kPipeConfigs[2] : kPipeConfigs[0];
+    if (dt == DTYPE_TQ2_0) return kPipeConfigs[2];
+    if (dt == DTYPE_Q4_0 && pipe_smem(dt, w.nb, w.kchunks, kPipeConfigs[3]) <= 227 * 1024) return kPipeConfigs[3];
+    return kPipeConfigs[0];
 }
 
 int item_nseg(const DevWeight &w) {
@@ -983,6 +987,8 @@ int launch_cfg(kernel_context_t *ctx, const PipeParams &p, PipeCfg c, int grid, 
     };
     if (c.nw == 8 && c.ns == 4) return run(gemv_pipe<DT, 8, 4>, 8 * 32);
     if (c.nw == 16 && c.ns == 2) return run(gemv_pipe<DT, 16, 2>, 16 * 32);
+    if (c.nw == 16 && c.ns == 4) return run(gemv_pipe<DT, 16, 4>, 16 * 32);
+    if (c.nw == 12 && c.ns == 6) return run(gemv_pipe<DT, 12, 6>, 12 * 32);
     return run(gemv_pipe<DT, 12, 3>, 12 * 32);
 }
 
@@ -1273,7 +1279,7 @@ bool pipe_supported(const DevWeight &w) {
     if (w.dtype != DTYPE_Q8_0 && w.dtype != DTYPE_Q4_0 && w.dtype != DTYPE_TQ2_0 && w.dtype != DTYPE_F32 &&
         w.dtype != DTYPE_BF16)
         return false;
-    return pipe_smem(w.dtype, w.nb, w.kchunks, pipe_cfg(w.dtype)) <= 227 * 1024;
+    return pipe_smem(w.dtype, w.nb, w.kchunks, pipe_cfg(w)) <= 227 * 1024;
 }
 
 // Scratch in float units: partials [ntiles][kmax][32] (two floats per entry
@@ -1281,7 +1287,7 @@ bool pipe_supported(const DevWeight &w) {
 void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints) {
     const int nseg = item_nseg(w);
     const long long T = (long long)w.ntiles * nseg;
-    const long long W = (long long)sm_count(ctx->device) * pipe_cfg(w.dtype).nw;
+    const long long W = (long long)sm_count(ctx->device) * pipe_cfg(w).nw;
     *part_floats = (size_t)w.ntiles * pipe_kmax(T, W, nseg) * 32 * (w.dtype == DTYPE_TQ2_0 ? 2 : 1);
     *cnt_ints = (size_t)w.ntiles;
 }
@@ -1301,7 +1307,7 @@ int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *
         ctx_fail(ctx, "launch_gemv_pipe", "%d gather targets (at most %d)", ll_n, kMaxPeers);
         return -1;
     }
-    const PipeCfg c = pipe_cfg(w.dtype);
+    const PipeCfg c = pipe_cfg(w);
     PipeParams p;
     p.ll_n = ll_n;
     p.ll_off = ll_off;

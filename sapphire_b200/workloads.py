@@ -31,7 +31,11 @@ C1 = GemvConfig("q4_0_ffn_up_2048x640", DTYPE_Q4_0, 2048, 640)
 C2 = GemvConfig("q8_0_lm_head_262144x640", DTYPE_Q8_0, 262144, 640)
 C4 = GemvConfig("tq2_0_16384x16384", DTYPE_TQ2_0, 16384, 16384)
 C5 = GemvConfig("q4_0_prefill_10240x2560_x2048", DTYPE_Q4_0, 10240, 2560, batch=2048)
-CONFIGS = {c.name: c for c in (C1, C2, C4, C5)}
+# The LM-head shape in the other two formats (the bandwidth target names all
+# three on this shape).
+C2_Q4 = GemvConfig("q4_0_lm_head_262144x640", DTYPE_Q4_0, 262144, 640)
+C2_TQ2 = GemvConfig("tq2_0_lm_head_262144x640", DTYPE_TQ2_0, 262144, 640)
+CONFIGS = {c.name: c for c in (C1, C2, C4, C5, C2_Q4, C2_TQ2)}
 
 
 def normal_weights(rng: np.random.Generator, rows: int, cols: int, std: float = 0.02) -> np.ndarray:
