@@ -104,13 +104,21 @@ __device__ __forceinline__ void mma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-// D += A(16x32, u8 row) * B(32x8, s8 col)
-__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
+// D = A * B + (c0, c1, c0, c1): the start value as the MMA's own C operand
+// (no copies into the accumulator registers first).
+__device__ __forceinline__ void mma_s8s8_c(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                           uint32_t b1, int c0, int c1) {
     asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+}
+__device__ __forceinline__ void mma_u8s8_c(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                           uint32_t b1, int c0, int c1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
 }
 
 template <typename T>
@@ -549,14 +557,12 @@ __device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_Q8_0> &R, int 
         for (int u = 0; u < 2; ++u) {
             B[u] = load_b(xp, nb, blk0 + u0 + u, lane);
             pe[u] = xp.pexp[min(blk0 + u0 + u, nb - 1)];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) D[u][0][i] = D[u][1][i] = 0;
         }
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const uint4 a0 = R.a[u0 + u][0], a1 = R.a[u0 + u][1];
-            mma_s8s8(D[u][0], a0.x, a0.y, a0.z, a0.w, B[u].x, B[u].y);
-            mma_s8s8(D[u][1], a1.x, a1.y, a1.z, a1.w, B[u].x, B[u].y);
+            mma_s8s8_c(D[u][0], a0.x, a0.y, a0.z, a0.w, B[u].x, B[u].y, 0, 0);
+            mma_s8s8_c(D[u][1], a1.x, a1.y, a1.z, a1.w, B[u].x, B[u].y, 0, 0);
         }
 #pragma unroll
         for (int u = 0; u < 2; ++u) scale_acc(acc, D[u][0], D[u][1], R.s[u0 + u], pe[u]);
@@ -585,10 +591,8 @@ __device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_Q4_0> &R, int 
         const uint32_t lo2 = A.z & 0x0F0F0F0Fu, hi2 = (A.z >> 4) & 0x0F0F0F0Fu;
         const uint32_t lo3 = A.w & 0x0F0F0F0Fu, hi3 = (A.w >> 4) & 0x0F0F0F0Fu;
         // Start from the -8 offset correction of the unsigned codes.
-        D[u][0][0] = D[u][0][2] = D[u][1][0] = D[u][1][2] = C[u].x;
-        D[u][0][1] = D[u][0][3] = D[u][1][1] = D[u][1][3] = C[u].y;
-        mma_u8s8(D[u][0], lo0, lo1, hi0, hi1, B[u].x, B[u].y);
-        mma_u8s8(D[u][1], lo2, lo3, hi2, hi3, B[u].x, B[u].y);
+        mma_u8s8_c(D[u][0], lo0, lo1, hi0, hi1, B[u].x, B[u].y, C[u].x, C[u].y);
+        mma_u8s8_c(D[u][1], lo2, lo3, hi2, hi3, B[u].x, B[u].y, C[u].x, C[u].y);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) scale_acc(acc, D[u][0], D[u][1], R.s[u], pe[u]);
