@@ -218,7 +218,8 @@ __device__ __forceinline__ int item_owner(long long i, long long T, long long W)
 //   digits[nb][3][4][8]  B fragments (digit rows 0..2, per lane-in-group tig:
 //                        word 0 then word 1), a 16-byte zero word after them
 //                        for lanes whose B column is 3..7;
-//   pexp[nb]             2^-e_b per block (TQ2_0: one global value in [0]);
+//   pexp[0]              2^-e, the one exponent of all of x (room for nb
+//                        values is kept);
 //   corr[nb][4][2]       Q4_0 only: -8 * (sum of the block's digits of row
 //                        2*tig+j), the correction of the unsigned codes.
 struct XPrep {
@@ -383,14 +384,15 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = 
         if (threadIdx.x < 4) reinterpret_cast<uint32_t *>(xp.digits + (size_t)p.nb * kDigitBytesPerBlock)[threadIdx.x] = 0;
         return;
     }
-    if (DT == DTYPE_TQ2_0) {
-        // Rows too long for the register path: loads unrolled so each thread
-        // has 8 in flight.
+    {
+        // One exponent for all of x (every format; the ternary rows here are
+        // too long for the register path): loads unrolled so each thread has
+        // 8 in flight.
         float m = 0.0f;
         bool bad = false;
 #pragma unroll 8
         for (int i = threadIdx.x; i < p.cols; i += blockDim.x) {
-            const float v = __ldg(p.x + i);
+            const float v = xs_smem ? xs_smem[i] : __ldg(p.x + i);
             bad |= !isfinite(v);
             m = fmaxf(m, fabsf(v));
         }
@@ -403,6 +405,9 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = 
         gexp = block_exponent(isfinite(m) ? m : FLT_MAX);
         if (threadIdx.x == 0) xp.pexp[0] = mul_pow2(1.0f, -gexp);
     }
+    // x * 2^gexp as two exact multiplies by normal powers of two.
+    const int e1 = min(max(gexp, -126), 127);
+    const float f1 = __int_as_float((e1 + 127) << 23), f2 = __int_as_float((gexp - e1 + 127) << 23);
     // Blocks b = warp + NW*u: the loads of kGroup blocks are issued together,
     // then each block is converted.
     constexpr int kGroup = 8;
@@ -418,15 +423,7 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = 
             const int b = b0 + u * NW;
             if (b >= p.nb) break;
             const float v = vg[u];
-            int e = gexp;
-            if (DT != DTYPE_TQ2_0) {
-                if (!isfinite(v)) *xp.nonfinite = 1;
-                float m = fabsf(v);
-                for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                e = block_exponent(isfinite(m) ? m : FLT_MAX);
-                if (lane == 0) xp.pexp[b] = mul_pow2(1.0f, -e);
-            }
-            const int X = isfinite(v) ? __float2int_rn(mul_pow2(v, e)) : 0;
+            const int X = isfinite(v) ? __float2int_rn(v * f1 * f2) : 0;
             int d0, d1, d2;
             digits3(X, d0, d1, d2);
             uint8_t *row = xp.digits + (size_t)b * kDigitBytesPerBlock;
@@ -534,16 +531,17 @@ __device__ __forceinline__ uint2 load_b(const XPrep &xp, int nb, int b, int lane
 }
 
 // Scaled epilogue of one block's two D tiles (rows g, g+8 | g+16, g+24).
-__device__ __forceinline__ void scale_acc(MmaAcc &acc, const int (&D0)[4], const int (&D1)[4], float4 S, float pe) {
-    const float s0 = S.x * pe, s1 = S.y * pe, s2 = S.z * pe, s3 = S.w * pe;
-    acc.f[0][0] = fmaf(s0, (float)D0[0], acc.f[0][0]);
-    acc.f[0][1] = fmaf(s0, (float)D0[1], acc.f[0][1]);
-    acc.f[0][2] = fmaf(s1, (float)D0[2], acc.f[0][2]);
-    acc.f[0][3] = fmaf(s1, (float)D0[3], acc.f[0][3]);
-    acc.f[1][0] = fmaf(s2, (float)D1[0], acc.f[1][0]);
-    acc.f[1][1] = fmaf(s2, (float)D1[1], acc.f[1][1]);
-    acc.f[1][2] = fmaf(s3, (float)D1[2], acc.f[1][2]);
-    acc.f[1][3] = fmaf(s3, (float)D1[3], acc.f[1][3]);
+// A lane holds D columns 2tig, 2tig+1 (digits 2tig, 2tig+1; digit 3 is a
+// zero column) of rows g, g+8 of each 16-row half.  Digits 0 and 1 are joined
+// in integer arithmetic, d0 + 256 d1 (below 2^28: each block sum is below
+// 2^22), so a block costs one conversion and one FMA per row and lane; lane
+// tig = 1 carries digit 2, weighted by 65536 in tile_rows.  The one exponent
+// of x is applied there too.
+__device__ __forceinline__ void scale_acc(MmaAcc &acc, const int (&D0)[4], const int (&D1)[4], float4 S) {
+    acc.f[0][0] = fmaf(S.x, (float)(D0[0] + 256 * D0[1]), acc.f[0][0]);
+    acc.f[0][2] = fmaf(S.y, (float)(D0[2] + 256 * D0[3]), acc.f[0][2]);
+    acc.f[1][0] = fmaf(S.z, (float)(D1[0] + 256 * D1[1]), acc.f[1][0]);
+    acc.f[1][2] = fmaf(S.w, (float)(D1[2] + 256 * D1[3]), acc.f[1][2]);
 }
 
 __device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_Q8_0> &R, int blk0, int nb, int lane,
@@ -551,13 +549,9 @@ __device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_Q8_0> &R, int 
 #pragma unroll
     for (int u0 = 0; u0 < 4; u0 += 2) {
         uint2 B[2];
-        float pe[2];
         int D[2][2][4];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            B[u] = load_b(xp, nb, blk0 + u0 + u, lane);
-            pe[u] = xp.pexp[min(blk0 + u0 + u, nb - 1)];
-        }
+        for (int u = 0; u < 2; ++u) B[u] = load_b(xp, nb, blk0 + u0 + u, lane);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
             const uint4 a0 = R.a[u0 + u][0], a1 = R.a[u0 + u][1];
@@ -565,7 +559,7 @@ __device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_Q8_0> &R, int 
             mma_s8s8_c(D[u][1], a1.x, a1.y, a1.z, a1.w, B[u].x, B[u].y, 0, 0);
         }
 #pragma unroll
-        for (int u = 0; u < 2; ++u) scale_acc(acc, D[u][0], D[u][1], R.s[u0 + u], pe[u]);
+        for (int u = 0; u < 2; ++u) scale_acc(acc, D[u][0], D[u][1], R.s[u0 + u]);
     }
 }
 
@@ -574,13 +568,11 @@ __device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_Q4_0> &R, int 
     const int tig = lane & 3;
     uint2 B[4];
     int2 C[4];
-    float pe[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
         const int b = min(blk0 + u, nb - 1);
         B[u] = load_b(xp, nb, b, lane);
         C[u] = lds<int2>(reinterpret_cast<const uint8_t *>(xp.corr) + (size_t)b * 32 + tig * 8);
-        pe[u] = xp.pexp[b];
     }
     int D[4][2][4];
 #pragma unroll
@@ -595,7 +587,7 @@ __device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_Q4_0> &R, int 
         mma_u8s8_c(D[u][1], lo2, lo3, hi2, hi3, B[u].x, B[u].y, C[u].x, C[u].y);
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) scale_acc(acc, D[u][0], D[u][1], R.s[u], pe[u]);
+    for (int u = 0; u < 4; ++u) scale_acc(acc, D[u][0], D[u][1], R.s[u]);
 }
 
 __device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_TQ2_0> &R, int blk0, int nb, int lane,
@@ -652,8 +644,10 @@ __device__ __forceinline__ void compute_item(const ItemRegs<DTYPE_BF16> &R, int 
 // Per-row results of a tile.  MMA formats: lanes with tig == 0 hold rows
 // g + 8*i (i = 0..3) as 8-byte values (fp32 bits for Q8_0 / Q4_0, the exact
 // int64 sum for TQ2_0); all lanes must call (shuffles).  Dense: row = lane.
+// Row values of a lane's accumulators: ternary exact int64 sums; Q8_0 / Q4_0
+// floats scaled by pe, the x exponent factor 2^-e.
 template <tensor_dtype_t DT>
-__device__ __forceinline__ void tile_rows(const MmaAcc &acc, unsigned long long (&v)[4]) {
+__device__ __forceinline__ void tile_rows(const MmaAcc &acc, unsigned long long (&v)[4], float pe) {
     if constexpr (!Geo<DT>::kMma) {
         v[0] = __float_as_uint(acc.dense);
         return;
@@ -671,8 +665,8 @@ __device__ __forceinline__ void tile_rows(const MmaAcc &acc, unsigned long long 
         } else {
             const float up0 = __shfl_down_sync(0xffffffffu, acc.f[h][0], 1);
             const float up2 = __shfl_down_sync(0xffffffffu, acc.f[h][2], 1);
-            v[2 * h] = __float_as_uint((float)((double)acc.f[h][0] + 256.0 * acc.f[h][1] + 65536.0 * up0));
-            v[2 * h + 1] = __float_as_uint((float)((double)acc.f[h][2] + 256.0 * acc.f[h][3] + 65536.0 * up2));
+            v[2 * h] = __float_as_uint((float)(((double)acc.f[h][0] + 65536.0 * up0) * pe));
+            v[2 * h + 1] = __float_as_uint((float)(((double)acc.f[h][2] + 65536.0 * up2) * pe));
         }
     }
     }
@@ -844,6 +838,7 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_pipe(const PipeParams p) {
     }
     __syncthreads();
     const bool nonfinite = G::kMma && s_nonfinite != 0;
+    const float x_scale = (G::kMma && DT != DTYPE_TQ2_0) ? xp.pexp[0] : 1.0f;
 
     int cur_tile = -1, c_tile = tile0, c_seg = seg0;
     bool cur_whole = false;
@@ -874,7 +869,7 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_pipe(const PipeParams p) {
         if (tile != cur_tile) {
             if (cur_tile >= 0) {
                 unsigned long long v[4] = {0, 0, 0, 0};
-                tile_rows<DT>(acc, v);
+                tile_rows<DT>(acc, v, x_scale);
                 flush_tile<DT>(p, xp, cur_tile, lane, gw, cur_whole, v, nonfinite);
             }
             cur_tile = tile;
@@ -885,7 +880,7 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_pipe(const PipeParams p) {
     }
     if (cur_tile >= 0) {
         unsigned long long v[4] = {0, 0, 0, 0};
-        tile_rows<DT>(acc, v);
+        tile_rows<DT>(acc, v, x_scale);
         flush_tile<DT>(p, xp, cur_tile, lane, gw, cur_whole, v, nonfinite);
     }
 }
@@ -1179,7 +1174,7 @@ __global__ void __launch_bounds__(kDirectWarps * 32) gemv_direct(const PipeParam
             const int seg = warp + k * kDirectWarps;
             if (seg < p.nseg) compute_item(R[k], seg * 4, p.nb, lane, xp, nullptr, acc);
         }
-        tile_rows<DT>(acc, v);
+        tile_rows<DT>(acc, v, xp.pexp[0]);
     }
     if ((lane & 3) == 0) {
 #pragma unroll
