@@ -192,6 +192,7 @@ struct PipeParams {
     // (ll_epoch << 32 | bits of the value) at ll[k][ll_off + r] (NVLink stores;
     // an aligned 8-byte store arrives whole, so the epoch marks the value
     // valid and no fence is needed).
+    int early;                  // weight copies per warp issued before the dependency wait
     int ll_n, ll_off;
     unsigned ll_epoch;
     unsigned long long *ll[kMaxPeers];
@@ -294,8 +295,8 @@ __device__ __forceinline__ int digit_slot(int p) {
     }
 }
 
-// The ternary register path (below) reads a long x with one load per element
-// and per lane; `after_loads` runs once those loads are issued.
+// `after_loads` runs once this CTA's x loads have been issued (the ternary
+// register path) or have returned (the other paths).
 template <tensor_dtype_t DT, int NW>
 __host__ __device__ constexpr bool tq2_reg_path(int nb) {
     return DT == DTYPE_TQ2_0 && (nb + NW - 1) / NW <= kTq2RegBlocks;
@@ -396,6 +397,7 @@ __device__ void prepare_x(const PipeParams &p, XPrep xp, const float *xs_smem = 
             bad |= !isfinite(v);
             m = fmaxf(m, fabsf(v));
         }
+        after_loads();
         if (bad) *xp.nonfinite = 1;
         for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         if (lane == 0) s_red[warp] = m;
@@ -815,24 +817,26 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_pipe(const PipeParams p) {
         fence_mbar_init();
     }
     __syncwarp();
-    // The weight copies do not depend on earlier kernels: they start before
-    // the wait for the kernel that produced x - except on the ternary
-    // register path, whose x loads (a whole long row per CTA) would queue
-    // behind them: there they follow the x loads.
-    auto issue_first = [&]() {
+    // The weight copies do not depend on earlier kernels: `early` of them
+    // start before the wait for the kernel that produced x, the rest once
+    // the x loads are out, which would otherwise queue behind the copies of
+    // every SM (none early on the ternary register path, whose x loads are a
+    // whole long row per CTA).
+    const int early = tq2_reg_path<DT, NW>(p.nb) ? 0 : min(p.early, NS);
+    if (lane == 0)
+        for (int j = 0; j < early && j < n_items; ++j) issue(j);
+    auto issue_rest = [&]() {
         if (lane == 0)
-            for (int j = 0; j < NS && j < n_items; ++j) issue(j);
+            for (int j = early; j < NS && j < n_items; ++j) issue(j);
     };
-    const bool late_issue = tq2_reg_path<DT, NW>(p.nb);
-    if (!late_issue) issue_first();
     pdl_wait();
     __syncthreads();   // s_nonfinite initialised before x preparation writes it
 
     // x image, built once per CTA while the first copies are in flight.
     if (G::kMma) {
-        if (late_issue) prepare_x<DT, NW>(p, xp, nullptr, issue_first);
-        else prepare_x<DT, NW>(p, xp);
+        prepare_x<DT, NW>(p, xp, nullptr, issue_rest);
     } else {
+        issue_rest();
         const int xpad = dense_xpad(DT, p.kchunks);
         for (int i = threadIdx.x; i < xpad; i += blockDim.x) xs[i] = (i < p.cols) ? p.x[i] : 0.0f;
     }
@@ -931,6 +935,19 @@ PipeCfg pipe_cfg(const DevWeight &w) {
     if (dt == DTYPE_TQ2_0) return kPipeConfigs[2];
     if (dt == DTYPE_Q4_0 && pipe_smem(dt, w.nb, w.kchunks, kPipeConfigs[3]) <= 227 * 1024) return kPipeConfigs[3];
     return kPipeConfigs[0];
+}
+
+// Weight copies per warp issued before the wait for x's producer: two (C2
+// and the Q4_0 LM head measured best with two of 3-4 slots early: the first
+// bytes are in flight across the wait, and the x loads queue behind only two
+// slots of every warp).  SAPPHIRE_PIPE_EARLY overrides it (tuning runs).
+int pipe_early(PipeCfg c) {
+    static const int env = [] {
+        const char *v = getenv("SAPPHIRE_PIPE_EARLY");
+        return v ? atoi(v) : -1;
+    }();
+    if (env >= 0) return env;
+    return std::min(2, c.ns);
 }
 
 int item_nseg(const DevWeight &w) {
@@ -1308,6 +1325,7 @@ int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *
     }
     const PipeCfg c = pipe_cfg(w);
     PipeParams p;
+    p.early = pipe_early(c);
     p.ll_n = ll_n;
     p.ll_off = ll_off;
     p.ll_epoch = ll_epoch;
