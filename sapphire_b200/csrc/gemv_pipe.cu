@@ -675,22 +675,26 @@ __device__ __forceinline__ void tile_rows(const MmaAcc &acc, unsigned long long 
 }
 
 // ---------------------------------------------------------- tile output ---
+// Index of row r's scale among a ternary tile's 32 (slot order g*4+i -> row g+8i).
+__device__ __forceinline__ int tq2_scale_slot(int r) { return (r & 7) * 4 + (r >> 3); }
+
+// rs: ternary row scale of row r, loaded when the tile started.
 template <tensor_dtype_t DT>
-__device__ __forceinline__ float finish_row(const PipeParams &p, const XPrep &xp, int tile, int r, unsigned long long v,
-                                            bool nonfinite) {
+__device__ __forceinline__ float finish_row(const XPrep &xp, unsigned long long v, bool nonfinite, float rs) {
     float out;
     if (DT == DTYPE_TQ2_0) {
-        const float s = __ldg(p.scales + (size_t)tile * 32 + (r & 7) * 4 + (r >> 3));
-        out = (float)((double)s * ((double)(long long)v * (double)xp.pexp[0]));
+        out = (float)((double)rs * ((double)(long long)v * (double)xp.pexp[0]));
     } else {
         out = __uint_as_float((uint32_t)v);
     }
     return nonfinite ? __int_as_float(0x7FC00000) : out;
 }
 
+// Rows are stored one per lane (row tile*32 + lane); rs is that row's ternary
+// scale.
 template <tensor_dtype_t DT>
 __device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int lane, int my_warp, bool whole,
-                           const unsigned long long (&v)[4], bool nonfinite) {
+                           const unsigned long long (&v)[4], bool nonfinite, float rs) {
     constexpr bool kMma = Geo<DT>::kMma;
     const bool owner_lane = kMma ? ((lane & 3) == 0) : true;
     constexpr int kRows = kMma ? 4 : 1;
@@ -706,7 +710,7 @@ __device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int l
                 if ((lane >> 3) == i) mine = t;
             }
         }
-        if (tile * 32 + lane < p.nrows) store_y(p, (size_t)tile * 32 + lane, finish_row<DT>(p, xp, tile, lane, mine, nonfinite));
+        if (tile * 32 + lane < p.nrows) store_y(p, (size_t)tile * 32 + lane, finish_row<DT>(xp, mine, nonfinite, rs));
         return;
     }
     // k = contributors of the tile, slot = this warp's rank among them.
@@ -757,7 +761,7 @@ __device__ void flush_tile(const PipeParams &p, const XPrep &xp, int tile, int l
             for (int j = 0; j < k; ++j) s += __ldcg(base32 + (size_t)j * 32 + r);
             sum = __float_as_uint(s);
         }
-        if (tile * 32 + r < p.nrows) store_y(p, (size_t)tile * 32 + r, finish_row<DT>(p, xp, tile, r, sum, nonfinite));
+        if (tile * 32 + r < p.nrows) store_y(p, (size_t)tile * 32 + r, finish_row<DT>(xp, sum, nonfinite, rs));
         __syncwarp();
         if (lane == 0) p.cnt[tile] = 0;
     }
@@ -845,6 +849,7 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_pipe(const PipeParams p) {
     const float x_scale = (G::kMma && DT != DTYPE_TQ2_0) ? xp.pexp[0] : 1.0f;
 
     int cur_tile = -1, c_tile = tile0, c_seg = seg0;
+    float row_scale = 0.0f;
     bool cur_whole = false;
     MmaAcc acc;
     acc.reset();
@@ -874,18 +879,21 @@ __global__ void __launch_bounds__(NW * 32, 1) gemv_pipe(const PipeParams p) {
             if (cur_tile >= 0) {
                 unsigned long long v[4] = {0, 0, 0, 0};
                 tile_rows<DT>(acc, v, x_scale);
-                flush_tile<DT>(p, xp, cur_tile, lane, gw, cur_whole, v, nonfinite);
+                flush_tile<DT>(p, xp, cur_tile, lane, gw, cur_whole, v, nonfinite, row_scale);
             }
             cur_tile = tile;
             acc.reset();
             cur_whole = (seg == 0) && ((long long)tile * p.nseg + p.nseg <= it1);
+            // The ternary row scale this lane stores with, loaded now so the
+            // flush does not wait for it.
+            if (DT == DTYPE_TQ2_0) row_scale = __ldg(p.scales + (size_t)tile * 32 + tq2_scale_slot(lane));
         }
         compute_item(R, u0, p.nb, lane, xp, xs, acc);
     }
     if (cur_tile >= 0) {
         unsigned long long v[4] = {0, 0, 0, 0};
         tile_rows<DT>(acc, v, x_scale);
-        flush_tile<DT>(p, xp, cur_tile, lane, gw, cur_whole, v, nonfinite);
+        flush_tile<DT>(p, xp, cur_tile, lane, gw, cur_whole, v, nonfinite, row_scale);
     }
 }
 
