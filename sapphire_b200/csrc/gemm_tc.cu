@@ -69,6 +69,8 @@ constexpr uint32_t kIdesc = (1u << 4)            // D format f32
                           | (1u << 10)           // B format bf16
                           | ((uint32_t)(kBN >> 3) << 17)
                           | ((uint32_t)(kBM >> 4) << 24);
+// The same with N = 128, for the half-width tiles of the last wave.
+constexpr uint32_t kIdescHalf = (kIdesc & ~(0x3Fu << 17)) | ((uint32_t)((kBN / 2) >> 3) << 17);
 
 struct GemmParams {
     const uint4 *codes;   // device layout of the Q4_0 weight
@@ -76,7 +78,20 @@ struct GemmParams {
     float *y;
     int *err;
     int nrows, nb, ntiles32, batch, ldy, mtiles, total_tiles, kstages;
+    // Tiles [0, full_tiles) are 128 x 256; the rest are the 128 x 128 halves
+    // of full tiles full_tiles, full_tiles + 1, ... (the last wave, split so
+    // that twice as many SMs share it).
+    int full_tiles;
 };
+
+struct TileGeom {
+    int m, n0, width;   // 128-row group, first token, tokens
+};
+__device__ __forceinline__ TileGeom tile_geom(const GemmParams &p, int tile) {
+    if (tile < p.full_tiles) return {tile % p.mtiles, (tile / p.mtiles) * kBN, kBN};
+    const int h = tile - p.full_tiles, f = p.full_tiles + (h >> 1);
+    return {f % p.mtiles, (f / p.mtiles) * kBN + (h & 1) * (kBN / 2), kBN / 2};
+}
 
 // ------------------------------------------------------------ PTX helpers --
 __device__ __forceinline__ uint32_t saddr(const void *p) {
@@ -147,11 +162,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
     d |= (uint64_t)2 << 61;                 // 128-byte swizzle
     return d;
 }
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
@@ -248,8 +264,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             long long kc = 0;
             for (int tile = blockIdx.x; tile < p.total_tiles && !*abort_flag; tile += gridDim.x) {
-                const int n0 = (tile / p.mtiles) * kBN;
-                const int t32_0 = (tile % p.mtiles) * 4;
+                // A half-width tile still loads the full 256-token box (its
+                // MMAs read the first 128 rows).
+                const TileGeom tg = tile_geom(p, tile);
+                const int n0 = tg.n0;
+                const int t32_0 = tg.m * 4;
                 const int ngroups = min(4, p.ntiles32 - t32_0);
                 for (int ks = 0; ks < p.kstages; ++ks, ++kc) {
                     const int s = (int)(kc % kStages);
@@ -290,6 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(b * kBN);
+                const uint32_t idesc = tile_geom(p, tile).width == kBN ? kIdesc : kIdescHalf;
                 for (int ks = 0; ks < p.kstages; ++ks, ++kc) {
                     const int s = (int)(kc % kStages);
                     const uint32_t ph = (uint32_t)(kc / kStages) & 1u;
@@ -303,8 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk) {
                         const uint64_t bdesc = sw128_desc(xa + kk * 32);
-                        umma_bf16(d_tmem, sw128_desc(ha + kk * 32), bdesc, (ks | kk) != 0);
-                        umma_bf16(d_tmem, sw128_desc(la + kk * 32), bdesc, 1u);
+                        umma_bf16(d_tmem, sw128_desc(ha + kk * 32), bdesc, idesc, (ks | kk) != 0);
+                        umma_bf16(d_tmem, sw128_desc(la + kk * 32), bdesc, idesc, 1u);
                     }
                     umma_commit(empty + s);   // frees the stage once these MMAs have read it
                 }
@@ -321,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int g = lane >> 2, tig = lane & 3;
         long long kc = 0;
         for (int tile = blockIdx.x; tile < p.total_tiles && !*abort_flag; tile += gridDim.x) {
-            const int t32 = (tile % p.mtiles) * 4 + d;
+            const int t32 = tile_geom(p, tile).m * 4 + d;
             const bool tile_ok = t32 < p.ntiles32;
             bool ok = true;
             for (int ks = 0; ks < p.kstages; ++ks, ++kc) {
@@ -375,11 +395,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int row = (tile % p.mtiles) * kBM + 32 * q + lane;
-            const int t0 = (tile / p.mtiles) * kBN;
+            const TileGeom tg = tile_geom(p, tile);
+            const int row = tg.m * kBM + 32 * q + lane;
+            const int t0 = tg.n0;
             const bool row_ok = row < p.nrows;
 #pragma unroll 1
-            for (int c0 = 0; c0 < kBN; c0 += 32) {
+            for (int c0 = 0; c0 < tg.width; c0 += 32) {
                 uint32_t v[32];
                 tmem_ld32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(b * kBN + c0), v);
                 const int tmax = min(32, p.batch - (t0 + c0));
@@ -519,7 +540,15 @@ int launch_gemm_tc_bf16(kernel_context_t *ctx, const DevWeight &w, const void *x
     p.batch = batch;
     p.ldy = ldy;
     p.mtiles = (w.ntiles + 3) / 4;
-    p.total_tiles = p.mtiles * ((batch + kBN - 1) / kBN);
+    const int full = p.mtiles * ((batch + kBN - 1) / kBN);
+    // Several waves whose last is partial: its r tiles run as 2r half-width
+    // tiles when those still fit one wave (C5: 640 tiles on 148 SMs, the last
+    // 48 become 96 halves).
+    const int sms_all = sm_count_of(ctx->device);
+    const int rest = full > sms_all ? full % sms_all : 0;
+    const bool split = rest > 0 && 2 * rest <= sms_all;
+    p.full_tiles = split ? full - rest : full;
+    p.total_tiles = split ? full + rest : full;
     p.kstages = kp / kBK;
     const int grid = std::min(p.total_tiles, sm_count_of(ctx->device));
 

@@ -48,6 +48,7 @@ def padded(X, cols):
     (96, 2560, 40),       # fewer rows than one 128-row tile
     (384, 2560, 300),     # several token tiles with a ragged last one
     (2048, 640, 600),
+    (2048, 64, 2560),     # 160 tiles: more than one wave, the last 12 run as half-width tiles
 ])
 def test_prefill_matches_reference_rows(sp, ctx, oracle, rows, cols, batch):
     packed, X = make_case(oracle, rows, cols, batch, seed=rows + cols + batch)
