@@ -13,7 +13,27 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import DTYPE_Q4_0, DTYPE_Q8_0, DTYPE_TQ2_0
+# tensor_dtype_t values (include/tensor.h).  Defined here rather than imported
+# from the binding so this module loads without libsapphire_cuda.so: the
+# benchmark's CPU reference arm imports it by file path and must not map the
+# GPU library.
+DTYPE_F32, DTYPE_BF16, DTYPE_F16, DTYPE_Q4_0, DTYPE_Q8_0, DTYPE_TQ2_0 = range(6)
+DTYPE_NAMES = {DTYPE_F32: "F32", DTYPE_BF16: "BF16", DTYPE_F16: "F16", DTYPE_Q4_0: "Q4_0",
+               DTYPE_Q8_0: "Q8_0", DTYPE_TQ2_0: "TQ2_0"}
+
+
+def row_bytes(dtype: int, cols: int) -> int:
+    """Bytes of one packed host row: Q4_0 / Q8_0 blocks of 20 / 36 bytes
+    (include/kernels.h block structs), TQ2_0 an fp32 row scale and 8 bytes per
+    32 trits, F32 / BF16 / F16 dense."""
+    nb = (cols + 31) // 32
+    if dtype == DTYPE_Q4_0:
+        return nb * 20
+    if dtype == DTYPE_Q8_0:
+        return nb * 36
+    if dtype == DTYPE_TQ2_0:
+        return 4 + nb * 8
+    return cols * (4 if dtype == DTYPE_F32 else 2)
 
 
 @dataclass(frozen=True)
