@@ -102,6 +102,17 @@ bool weight_shape(const tensor_t *A, int *rows, int *cols) {
     return true;
 }
 
+int sm_count(int dev) {
+    static int cached[64] = {0};
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
 size_t sapphire_row_bytes_internal(tensor_dtype_t dt, int cols) {
     if (cols <= 0) return 0;
     const size_t nb = ((size_t)cols + 31) / 32;
@@ -146,7 +157,7 @@ extern "C" SAPPHIRE_API kernel_context_t *kernel_ctx_create(int num_threads, int
 
 extern "C" SAPPHIRE_API int kernel_ctx_init(kernel_context_t *ctx) {
     if (!ctx) {
-        LOG_ERROR("kernel_ctx_init: context is NULL");
+        LOG_ERROR("kernel_ctx_init: NULL context");
         return -1;
     }
     std::lock_guard<std::recursive_mutex> lk(ctx->exec_mutex);
@@ -165,6 +176,7 @@ extern "C" SAPPHIRE_API int kernel_ctx_init(kernel_context_t *ctx) {
         CUDA_TRY(ctx, cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
         ctx->own_stream = true;
     }
+    if (ensure_err_word(ctx)) return -1;
     if (!ctx->pool) {
         HostPool *p = new HostPool();
         try {
@@ -290,25 +302,32 @@ int ensure_scratch(kernel_context_t *ctx, float **buf, size_t *cap, size_t bytes
 }
 
 // ------------------------------------------------ pipelined GEMV scratch ---
+// The error word lives in mapped pinned host memory: a kernel writes it only
+// on failure and the host reads it after a sync.  Created at kernel_ctx_init
+// (so entry points that must not allocate can still report errors).
+int ensure_err_word(kernel_context_t *ctx) {
+    if (ctx->h_err) return 0;
+    int *h = nullptr;
+    CUDA_TRY(ctx, cudaHostAlloc((void **)&h, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable));
+    *h = 0;
+    int *d = nullptr;
+    if (cudaHostGetDevicePointer((void **)&d, h, 0) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFreeHost(h);
+        ctx_fail(ctx, "ensure_err_word", "no device alias for the mapped error word");
+        return -1;
+    }
+    ctx->h_err = h;
+    ctx->d_err = d;
+    return 0;
+}
+
 // Partial sums and zeroed arrival counters for the pipelined kernel, grown on
 // demand; the counters return to zero at the end of every launch, so only new
-// memory needs clearing.  The error word lives in mapped pinned host memory:
-// a kernel writes it only on failure and the host reads it after a sync.
+// memory needs clearing (check_kernel_error clears them after a launch that
+// gave up, since a warp that bails out leaves its tiles' counts behind).
 int ensure_pipe_scratch(kernel_context_t *ctx, size_t part_floats, size_t cnt_ints) {
-    if (!ctx->h_err) {
-        int *h = nullptr;
-        CUDA_TRY(ctx, cudaHostAlloc((void **)&h, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable));
-        *h = 0;
-        int *d = nullptr;
-        if (cudaHostGetDevicePointer((void **)&d, h, 0) != cudaSuccess) {
-            cudaGetLastError();
-            cudaFreeHost(h);
-            ctx_fail(ctx, "ensure_pipe_scratch", "no device alias for the mapped error word");
-            return -1;
-        }
-        ctx->h_err = h;
-        ctx->d_err = d;
-    }
+    if (ensure_err_word(ctx)) return -1;
     if (ensure_scratch(ctx, &ctx->d_part, &ctx->d_part_cap, part_floats * sizeof(float))) return -1;
     if (ctx->d_cnt_cap < cnt_ints * sizeof(int) || !ctx->d_cnt) {
         float *buf = reinterpret_cast<float *>(ctx->d_cnt);
@@ -323,7 +342,7 @@ int ensure_pipe_scratch(kernel_context_t *ctx, size_t part_floats, size_t cnt_in
 
 int launch_gemv_best(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, cudaStream_t st) {
     if (w.ntiles <= kDirectMaxTiles && direct_supported(w)) return launch_gemv_direct(ctx, w, x, y, st);
-    if (pipe_supported(w)) {
+    if (pipe_supported(ctx, w)) {
         size_t pf = 0, ci = 0;
         pipe_scratch_size(ctx, w, &pf, &ci);
         if (ensure_pipe_scratch(ctx, pf, ci)) return -1;
@@ -350,12 +369,17 @@ int launch_product(kernel_context_t *ctx, const DevWeight &w, const float *x, in
 }
 
 int check_kernel_error(kernel_context_t *ctx, const char *who) {
-    if (ctx->h_err && *reinterpret_cast<volatile int *>(ctx->h_err)) {
-        *ctx->h_err = 0;
+    const int bits = ctx->h_err ? *reinterpret_cast<volatile int *>(ctx->h_err) : 0;
+    if (!bits) return 0;
+    *ctx->h_err = 0;
+    // A GEMV warp that gave up left the arrival counts of the tiles it had
+    // joined behind; later launches sharing the counters would miscount.
+    if (ctx->d_cnt && ctx->d_cnt_cap) cudaMemsetAsync(ctx->d_cnt, 0, ctx->d_cnt_cap, ctx->stream);
+    if (bits & 8)
+        ctx_fail(ctx, who, "a peer-memory gather gave up waiting for another rank's rows (bounded wait expired)");
+    else
         ctx_fail(ctx, who, "a kernel gave up waiting for its asynchronous copies (bounded wait expired)");
-        return -1;
-    }
-    return 0;
+    return -1;
 }
 
 // ------------------------------------------------------- weight upload ----
@@ -529,7 +553,9 @@ extern "C" SAPPHIRE_API int kernel_ctx_synchronize(kernel_context_t *ctx) {
     if (!ctx->stream) return 0;
     DeviceGuard g(ctx->device);
     CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
-    return 0;
+    // Errors of asynchronous calls (kernel_gemv_device and the like) surface
+    // here: a kernel whose bounded wait expired set the error word.
+    return check_kernel_error(ctx, "kernel_ctx_synchronize");
 }
 
 extern "C" SAPPHIRE_API void *kernel_ctx_get_stream(kernel_context_t *ctx) {

@@ -964,17 +964,6 @@ int item_nseg(const DevWeight &w) {
     return (units + bpi - 1) / bpi;
 }
 
-int sm_count(int dev) {
-    static int cached[64] = {0};
-    if (dev < 0 || dev >= 64) return 148;
-    if (!cached[dev]) {
-        int n = 0;
-        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-        cached[dev] = n;
-    }
-    return cached[dev];
-}
-
 // Raises a kernel's dynamic shared-memory opt-in on the context's device only
 // when a launch needs more than was set before, so repeated launches (and
 // launches recorded into a CUDA graph after a first eager one) make no
@@ -1299,16 +1288,21 @@ int pipe_kmax(long long T, long long W, int nseg) {
     return (int)(k < nseg ? k : nseg);
 }
 
-bool pipe_supported(const DevWeight &w) {
-    if (w.dtype != DTYPE_Q8_0 && w.dtype != DTYPE_Q4_0 && w.dtype != DTYPE_TQ2_0 && w.dtype != DTYPE_F32 &&
-        w.dtype != DTYPE_BF16)
-        return false;
+// Quantized formats run gemv_stream (gemv_stream.cu); dense F32 / BF16 rows
+// the pipelined kernel of this file.
+bool pipe_supported(kernel_context_t *ctx, const DevWeight &w) {
+    if (stream_dtype(w.dtype)) return stream_supported(ctx, w);
+    if (w.dtype != DTYPE_F32 && w.dtype != DTYPE_BF16) return false;
     return pipe_smem(w.dtype, w.nb, w.kchunks, pipe_cfg(w)) <= 227 * 1024;
 }
 
 // Scratch in float units: partials [ntiles][kmax][32] (two floats per entry
 // for the int64 ternary sums), counters [ntiles].
 void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints) {
+    if (stream_dtype(w.dtype)) {
+        stream_scratch_size(ctx, w, part_floats, cnt_ints);
+        return;
+    }
     const int nseg = item_nseg(w);
     const long long T = (long long)w.ntiles * nseg;
     const long long W = (long long)sm_count(ctx->device) * pipe_cfg(w).nw;
@@ -1326,6 +1320,7 @@ int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, 
 int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
                         int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
                         cudaStream_t st) {
+    if (stream_dtype(w.dtype)) return launch_gemv_stream(ctx, w, x, y, part, cnt, err, ll, ll_n, ll_off, ll_epoch, st);
     if (w.ntiles == 0) return 0;
     if (ll_n < 0 || ll_n > kMaxPeers) {
         ctx_fail(ctx, "launch_gemv_pipe", "%d gather targets (at most %d)", ll_n, kMaxPeers);
@@ -1360,9 +1355,6 @@ int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *
     p.kmax = pipe_kmax(p.total_items, p.total_warps, p.nseg);
     const size_t smem = pipe_smem(w.dtype, w.nb, w.kchunks, c);
     switch (w.dtype) {
-        case DTYPE_Q8_0: return launch_cfg<DTYPE_Q8_0>(ctx, p, c, grid, smem, st);
-        case DTYPE_Q4_0: return launch_cfg<DTYPE_Q4_0>(ctx, p, c, grid, smem, st);
-        case DTYPE_TQ2_0: return launch_cfg<DTYPE_TQ2_0>(ctx, p, c, grid, smem, st);
         case DTYPE_F32: return launch_cfg<DTYPE_F32>(ctx, p, c, grid, smem, st);
         case DTYPE_BF16: return launch_cfg<DTYPE_BF16>(ctx, p, c, grid, smem, st);
         default:

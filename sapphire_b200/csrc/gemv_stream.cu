@@ -1,0 +1,1009 @@
+// gemv_stream.cu - batch-1 GEMV of the quantized formats (Q8_0, Q4_0, TQ2_0):
+// the decode hot path behind kernel_gemv.
+//
+// Same products as the reference row kernels (src/kernels/q4_0_avx.c:102-148,
+// q8_0_avx.c:16-136, driven per row by src/kernels/pool.c:106-143), plus the
+// ternary format.
+//
+// Work split.  A "unit" is 32 rows x 64 columns (two 32-column blocks) of a
+// 32-row tile; an item is up to UPI consecutive units of one tile (a K
+// segment).  Items are numbered tile-major and every consumer warp of the
+// persistent grid (one CTA per SM) takes a contiguous, equal-size range of
+// them, so every SM streams the same number of bytes whatever the shape.
+//
+// Memory pipeline.  Warp NC of each CTA is the producer: its lane c streams
+// consumer c's items into that consumer's ring of NS shared-memory slots with
+// cp.async.bulk, completing on the slot's "full" mbarrier (expect_tx).  A
+// consumer waits on "full", copies the item into registers, arrives on the
+// slot's "empty" mbarrier (release; the producer's acquire-wait on it orders
+// the refill after the reads, so no proxy fence is needed) and only then
+// computes.  Consumers issue no copies.
+//
+// Dot products run on the integer tensor cores (mma.sync m16n8k32).  x is
+// converted once per CTA to a 22-bit fixed-point image X_j = round(x_j 2^e)
+// (one exponent e for all of x) split into three balanced int8 digits
+// X = d0 + 256 d1 + 65536 d2, stored per 32-column block as the B fragments
+// of digit columns 0..2 plus a zero column.
+//   Q8_0 / Q4_0: a unit's two blocks share one C tile - block 2p in digit
+//     columns 0..2, block 2p+1 in columns 4..6 - so one epilogue (digit join,
+//     conversion, per-block scale FMA, like the reference's per-block
+//     (q - 8) * scale) serves two blocks.  Q4_0 nibbles are fed as unsigned
+//     codes with -8 * (digit sum) as the MMA's start value.
+//   TQ2_0: the codes c = t + 1 of four 16-row x 32-column fragments are
+//     interleaved as the four 2-bit planes of the same bytes, so each MMA
+//     register is one AND with a plane mask (plane m carries 4^m c); the four
+//     planes accumulate exactly in int32 across all of K, are joined by exact
+//     shifts at the end of a tile, and sum_j X_j is subtracted once per row.
+//
+// Split tiles.  A tile whose items span several warps is finished by the last
+// contributor: each stores its per-row partial (fp32, or the exact int64 sum
+// for ternary) in the slot of its rank among the tile's contributors, fences,
+// and bumps the tile's counter; the one that completes the count sums the
+// slots in slot order (deterministic), writes y and resets the counter.
+//
+// Waits are bounded.  A consumer whose slot does not fill sets bit 0 of *err
+// and its abort flag, and leaves the loop; the producer lane serving it stops
+// waiting for it; before the CTA exits every producer lane waits (bounded) for
+// the copies it issued that may still be in flight.
+#include <cfloat>
+
+#include "internal.cuh"
+
+namespace {
+
+constexpr unsigned kWaitLimit = 1u << 26;     // polls of a bounded wait
+constexpr int kImgBlock = 128;                // digit rows d0, d1, d2 and a zero row, 32 bytes each
+constexpr int kMaxConsumers = 16;
+
+// ------------------------------------------------------------ PTX helpers --
+__device__ __forceinline__ uint32_t saddr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(saddr(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+// Bulk global -> shared copy (16-byte aligned, multiple of 16 bytes), into this CTA only.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(saddr(dst)),
+        "l"(src), "r"(bytes), "r"(saddr(bar))
+        : "memory");
+}
+
+// D = A(16x32) * B(32x8) + C, 8-bit operands, int32 accumulate.
+__device__ __forceinline__ void mma_s8(int (&d)[4], uint4 a, uint2 b, const int (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]));
+}
+__device__ __forceinline__ void mma_u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint2 b,
+                                       const int (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]));
+}
+
+template <typename T>
+__device__ __forceinline__ T lds(const uint8_t *p) {
+    return *reinterpret_cast<const T *>(p);
+}
+
+// ------------------------------------------------------------ formats -----
+// Bytes of one unit in the device layout (internal.cuh / repack.cu): codes
+// and (per-block formats) scales; per-block formats store a unit as two
+// consecutive blocks, so the last unit of an odd-block row is one block.
+template <tensor_dtype_t DT>
+struct Fmt;
+template <>
+struct Fmt<DTYPE_Q8_0> {
+    static constexpr int kBlockCode = 1024;
+    static constexpr bool kBlockScales = true;
+};
+template <>
+struct Fmt<DTYPE_Q4_0> {
+    static constexpr int kBlockCode = 512;
+    static constexpr bool kBlockScales = true;
+};
+template <>
+struct Fmt<DTYPE_TQ2_0> {
+    static constexpr int kBlockCode = 256;
+    static constexpr bool kBlockScales = false;    // one fp32 scale per row, read when a tile starts
+};
+template <tensor_dtype_t DT>
+__host__ __device__ constexpr int unit_code() { return 2 * Fmt<DT>::kBlockCode; }
+template <tensor_dtype_t DT>
+__host__ __device__ constexpr int unit_scale() { return Fmt<DT>::kBlockScales ? 256 : 0; }
+template <tensor_dtype_t DT, int UPI>
+__host__ __device__ constexpr int slot_bytes() { return UPI * (unit_code<DT>() + unit_scale<DT>()); }
+
+struct StreamParams {
+    const uint8_t *codes;
+    const float *scales;
+    const float *x;
+    float *y;
+    void *part;                 // [ntiles][kmax][32] partials of split tiles (fp32; int64 for TQ2_0)
+    int *cnt;                   // [ntiles] arrival counters, zero between launches
+    int *err;                   // error word (bit 0: a bounded wait expired)
+    long long total_items;
+    int nrows, cols, nb, nunits, ntiles, nseg, kmax, total_warps;
+    unsigned wait_limit;        // test hook: polls before the unarmed consumer's first wait gives up
+    int test_unarmed;           // test hook: consumer 0 of CTA 0 gets no copy for its first item
+    // Row-sharded products gathered over peer memory: when ll_n > 0 row r is
+    // not stored at y[r] but sent to every rank k as the 8-byte word
+    // (ll_epoch << 32 | bits of the value) at ll[k][ll_off + r] (NVLink stores;
+    // an aligned 8-byte store arrives whole, so the epoch marks the value
+    // valid and no fence is needed).
+    int ll_n, ll_off;
+    unsigned ll_epoch;
+    unsigned long long *ll[kMaxPeers];
+};
+
+__device__ __forceinline__ void store_y(const StreamParams &p, size_t r, float v) {
+    if (p.ll_n) {
+        const unsigned long long word = ((unsigned long long)p.ll_epoch << 32) | __float_as_uint(v);
+        for (int k = 0; k < p.ll_n; ++k)
+            asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p.ll[k] + (size_t)p.ll_off + r), "l"(word) : "memory");
+    } else {
+        p.y[r] = v;
+    }
+}
+
+__device__ __forceinline__ long long range_begin(long long w, long long T, long long W) { return (w * T) / W; }
+__device__ __forceinline__ int item_owner(long long i, long long T, long long W) {
+    long long w = ((i + 1) * W + T - 1) / T - 1;
+    return (int)(w < W - 1 ? w : W - 1);
+}
+
+// Named barrier over the NC consumer warps (the producer warp never joins).
+__device__ __forceinline__ void consumers_sync(int nthreads) {
+    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// ------------------------------------------------------- x preparation ----
+// Shared-memory image of x, built by the consumer warps:
+//   img[nbp][4][4][8]  per block: digit rows d0, d1, d2 (B fragments: per
+//                      lane-in-group tig, K slots 4tig..4tig+3 then
+//                      16+4tig..16+4tig+3) and a zero row; nbp = nb rounded
+//                      up to even, the extra block all zero;
+//   corr[nbp][4]       Q4_0: -8 * (sum of the block's digits d0, d1, d2), 0;
+//   sx                 TQ2_0: sum over all columns of X_j (int64);
+//   pexp               2^-e.
+struct XImage {
+    uint8_t *img;
+    int *corr;
+    long long *sx;
+    float *pexp;
+    int *nonfinite;
+};
+
+__host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+__host__ __device__ inline int nb_even(int nb) { return (nb + 1) & ~1; }
+__host__ __device__ inline size_t ximg_bytes(int nb, bool q4) {
+    size_t b = (size_t)nb_even(nb) * kImgBlock;
+    if (q4) b += (size_t)nb_even(nb) * 16;
+    return align16(b) + 16 + 16;          // + sx (8) + pexp (4), padded
+}
+
+// Exponent e with max|x| * 2^e < 2^22 (0 for all-zero x).
+__device__ __forceinline__ int x_exponent(float m) {
+    if (!(m > 0.0f)) return 0;
+    const int be = (__float_as_int(m) >> 23) & 0xFF;
+    int E;
+    if (be != 0) {
+        E = be - 126;
+    } else {
+        frexpf(m, &E);
+    }
+    return 22 - E;
+}
+
+// Byte offset, inside a 32-byte digit row, of the K slot that carries
+// element p (0..31) of a block.  Q8_0 / TQ2_0: slot = p.  Q4_0: the low nibble
+// of code byte 4t+j (element 8t+2j) is slot 4t+j, the high nibble (element
+// 8t+2j+1) slot 16+4t+j.
+template <tensor_dtype_t DT>
+__device__ __forceinline__ int digit_byte(int p) {
+    if (DT == DTYPE_Q4_0) return (p >> 3) * 8 + (p & 1) * 4 + ((p & 7) >> 1);
+    return ((p & 15) >> 2) * 8 + (p >> 4) * 4 + (p & 3);
+}
+
+constexpr int kXRegBlocks = 16;   // blocks per consumer warp held in registers between the two passes
+
+template <tensor_dtype_t DT, int NC>
+__device__ void prepare_x(const StreamParams &p, const XImage &xi) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ float s_max[kMaxConsumers];
+    __shared__ long long s_sx[kMaxConsumers];
+    const int nbp = nb_even(p.nb);
+    // Pass 1: max |x| (and non-finite values) over all of x.
+    float v[kXRegBlocks];
+    float m = 0.0f;
+    bool bad = false;
+#pragma unroll
+    for (int k = 0; k < kXRegBlocks; ++k) {
+        const int c = (warp + NC * k) * 32 + lane;
+        v[k] = c < p.cols ? __ldg(p.x + c) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < kXRegBlocks; ++k) {
+        bad |= !isfinite(v[k]);
+        m = fmaxf(m, fabsf(v[k]));
+    }
+    for (int b = warp + NC * kXRegBlocks; b < p.nb; b += NC) {
+        const int c = b * 32 + lane;
+        const float t = c < p.cols ? __ldg(p.x + c) : 0.0f;
+        bad |= !isfinite(t);
+        m = fmaxf(m, fabsf(t));
+    }
+    if (bad) *xi.nonfinite = 1;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) s_max[warp] = m;
+    consumers_sync(NC * 32);
+    m = 0.0f;
+    for (int i = 0; i < NC; ++i) m = fmaxf(m, s_max[i]);
+    const int e = x_exponent(isfinite(m) ? m : FLT_MAX);
+    if (threadIdx.x == 0) *xi.pexp = (e >= -126 && e <= 127) ? __int_as_float((127 - e) << 23) : ldexpf(1.0f, -e);
+    // x * 2^e as two exact multiplies by normal powers of two (e <= 170).
+    const int e1 = min(max(e, -126), 127);
+    const float f1 = __int_as_float((e1 + 127) << 23), f2 = __int_as_float((e - e1 + 127) << 23);
+    // Pass 2: digits of every block (blocks b = warp + NC*k), the zero rows,
+    // the Q4_0 corrections and the ternary x sum.
+    long long sx = 0;
+    const int off = digit_byte<DT>(lane);
+    auto convert = [&](int b, float t) {
+        const int X = isfinite(t) ? __float2int_rn(t * f1 * f2) : 0;
+        sx += X;
+        const int d0 = ((X & 0xFF) ^ 0x80) - 0x80;
+        const int X1 = (X - d0) >> 8;
+        const int d1 = ((X1 & 0xFF) ^ 0x80) - 0x80;
+        const int d2 = (X1 - d1) >> 8;
+        uint8_t *blk = xi.img + (size_t)b * kImgBlock;
+        blk[off] = (uint8_t)d0;
+        blk[32 + off] = (uint8_t)d1;
+        blk[64 + off] = (uint8_t)d2;
+        blk[96 + lane] = 0;
+        if (DT == DTYPE_Q4_0) {
+            int s0 = d0, s1 = d1, s2 = d2;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+                s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+                s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+            }
+            if (lane < 4) xi.corr[b * 4 + lane] = lane == 0 ? -8 * s0 : lane == 1 ? -8 * s1 : lane == 2 ? -8 * s2 : 0;
+        }
+    };
+#pragma unroll
+    for (int k = 0; k < kXRegBlocks; ++k) {
+        const int b = warp + NC * k;
+        if (b < p.nb) convert(b, v[k]);
+    }
+    for (int b = warp + NC * kXRegBlocks; b < p.nb; b += NC) {
+        const int c = b * 32 + lane;
+        convert(b, c < p.cols ? __ldg(p.x + c) : 0.0f);
+    }
+    if (nbp > p.nb && warp == NC - 1) {
+        // The padding block of an odd-block row: all digit rows zero.
+        uint32_t *blk = reinterpret_cast<uint32_t *>(xi.img + (size_t)p.nb * kImgBlock);
+        blk[lane] = 0;
+        if (DT == DTYPE_Q4_0 && lane < 4) xi.corr[p.nb * 4 + lane] = 0;
+    }
+    if (DT == DTYPE_TQ2_0) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+        if (lane == 0) s_sx[warp] = sx;
+        consumers_sync(NC * 32);
+        if (threadIdx.x == 0) {
+            long long t = 0;
+            for (int i = 0; i < NC; ++i) t += s_sx[i];
+            *xi.sx = t;
+        }
+    }
+}
+
+// ----------------------------------------------------------- item in regs --
+// The part of a staged item one lane needs (unit u of UPI; units past the
+// item's count are not loaded).
+template <tensor_dtype_t DT, int UPI>
+struct Item;
+template <int UPI>
+struct Item<DTYPE_Q8_0, UPI> {
+    uint4 a[UPI][2][2];   // [unit][block of the unit][16-row half]: the A fragment
+    float4 s[UPI];        // scales of rows g, g+8, g+16, g+24 of block 2p + tig/2
+    __device__ __forceinline__ void load(const uint8_t *st, int nu, int lane, bool last_half) {
+        const int g = lane >> 2, tig = lane & 3;
+#pragma unroll
+        for (int u = 0; u < UPI; ++u) {
+            if (u < nu) {
+#pragma unroll
+                for (int k = 0; k < 2; ++k)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) a[u][k][h] = lds<uint4>(st + (2 * u + k) * 1024 + h * 512 + lane * 16);
+                // Block 2p+1 of an odd-block row's last unit is not copied:
+                // its lanes (tig >= 2) use zero scales, not the slot's stale bytes.
+                const float4 t = lds<float4>(st + UPI * 2048 + u * 256 + (tig >> 1) * 128 + g * 16);
+                const bool z = last_half && u == nu - 1 && tig >= 2;
+                s[u] = make_float4(z ? 0.f : t.x, z ? 0.f : t.y, z ? 0.f : t.z, z ? 0.f : t.w);
+            }
+        }
+    }
+};
+template <int UPI>
+struct Item<DTYPE_Q4_0, UPI> {
+    uint4 a[UPI][2];      // [unit][block]: code word tig of rows g, g+8, g+16, g+24
+    float4 s[UPI];
+    __device__ __forceinline__ void load(const uint8_t *st, int nu, int lane, bool last_half) {
+        const int g = lane >> 2, tig = lane & 3;
+#pragma unroll
+        for (int u = 0; u < UPI; ++u) {
+            if (u < nu) {
+#pragma unroll
+                for (int k = 0; k < 2; ++k) a[u][k] = lds<uint4>(st + (2 * u + k) * 512 + lane * 16);
+                const float4 t = lds<float4>(st + UPI * 1024 + u * 256 + (tig >> 1) * 128 + g * 16);
+                const bool z = last_half && u == nu - 1 && tig >= 2;
+                s[u] = make_float4(z ? 0.f : t.x, z ? 0.f : t.y, z ? 0.f : t.z, z ? 0.f : t.w);
+            }
+        }
+    }
+};
+template <int UPI>
+struct Item<DTYPE_TQ2_0, UPI> {
+    uint4 a[UPI];         // four words: 2-bit planes of four A fragments
+    __device__ __forceinline__ void load(const uint8_t *st, int nu, int lane, bool) {
+#pragma unroll
+        for (int u = 0; u < UPI; ++u)
+            if (u < nu) a[u] = lds<uint4>(st + u * 512 + lane * 16);
+    }
+};
+
+// Accumulators of one 32-row tile for a lane (g = lane/4, tig = lane%4).
+struct Acc {
+    float f[2][2];        // Q8_0 / Q4_0: [half][row g / g+8] scaled sums (digit columns of this lane)
+    int d[4][4];          // TQ2_0: [plane][C register] exact sums
+    __device__ __forceinline__ void reset() {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) f[h][0] = f[h][1] = 0.0f;
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) d[m][i] = 0;
+    }
+};
+
+// Lane constants for the B loads: offsets inside a unit's 256-byte image
+// (blocks 2p, 2p+1).  Q8_0 / Q4_0: block 2p feeds digit columns 0..2 (lanes
+// g < 3, g == 3 reads the zero row), block 2p+1 columns 4..6 (lanes g = 4..6;
+// all other lanes read a zero row).  TQ2_0: both blocks feed columns 0..2.
+struct LaneOff {
+    int b0, b1;
+};
+template <tensor_dtype_t DT>
+__device__ __forceinline__ LaneOff lane_offsets(int lane) {
+    const int g = lane >> 2, tig = lane & 3;
+    LaneOff o;
+    if (DT == DTYPE_TQ2_0) {
+        o.b0 = min(g, 3) * 32 + tig * 8;
+        o.b1 = kImgBlock + o.b0;
+    } else {
+        o.b0 = (g < 4 ? g : 3) * 32 + tig * 8;
+        o.b1 = kImgBlock + (g >= 4 ? min(g - 4, 3) : 3) * 32 + tig * 8;
+    }
+    return o;
+}
+
+// Joins digits 0 and 1 of a C register pair (below 2^28: a block's digit
+// products are below 2^22) and adds scale * value.
+__device__ __forceinline__ void scale2(float (&acc)[2], const int (&D)[4], float s0, float s1) {
+    acc[0] = fmaf(s0, (float)(D[0] + 256 * D[1]), acc[0]);
+    acc[1] = fmaf(s1, (float)(D[2] + 256 * D[3]), acc[1]);
+}
+
+template <int UPI>
+__device__ __forceinline__ void compute(const Item<DTYPE_Q8_0, UPI> &R, int nu, int p0, const XImage &xi,
+                                        LaneOff lo, int, Acc &acc) {
+    const int zero[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int u = 0; u < UPI; ++u) {
+        if (u < nu) {
+            const uint8_t *bi = xi.img + (size_t)(p0 + u) * (2 * kImgBlock);
+            const uint2 B0 = lds<uint2>(bi + lo.b0), B1 = lds<uint2>(bi + lo.b1);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                int D[4];
+                mma_s8(D, R.a[u][0][h], B0, zero);
+                mma_s8(D, R.a[u][1][h], B1, D);
+                scale2(acc.f[h], D, h ? R.s[u].z : R.s[u].x, h ? R.s[u].w : R.s[u].y);
+            }
+        }
+    }
+}
+
+template <int UPI>
+__device__ __forceinline__ void compute(const Item<DTYPE_Q4_0, UPI> &R, int nu, int p0, const XImage &xi,
+                                        LaneOff lo, int tig, Acc &acc) {
+#pragma unroll
+    for (int u = 0; u < UPI; ++u) {
+        if (u < nu) {
+            const uint8_t *bi = xi.img + (size_t)(p0 + u) * (2 * kImgBlock);
+            const uint2 B0 = lds<uint2>(bi + lo.b0), B1 = lds<uint2>(bi + lo.b1);
+            const int2 C = *reinterpret_cast<const int2 *>(xi.corr + (size_t)(p0 + u) * 8 + tig * 2);
+            const int c0[4] = {C.x, C.y, C.x, C.y};
+            const uint4 A0 = R.a[u][0], A1 = R.a[u][1];
+            // Half 0 (rows g, g+8): words x, y; half 1 (rows g+16, g+24): z, w.
+            // Low nibbles are K slots 0..15, high nibbles 16..31.
+            {
+                int D[4];
+                mma_u8(D, A0.x & 0x0F0F0F0Fu, A0.y & 0x0F0F0F0Fu, (A0.x >> 4) & 0x0F0F0F0Fu, (A0.y >> 4) & 0x0F0F0F0Fu,
+                       B0, c0);
+                mma_u8(D, A1.x & 0x0F0F0F0Fu, A1.y & 0x0F0F0F0Fu, (A1.x >> 4) & 0x0F0F0F0Fu, (A1.y >> 4) & 0x0F0F0F0Fu,
+                       B1, D);
+                scale2(acc.f[0], D, R.s[u].x, R.s[u].y);
+            }
+            {
+                int D[4];
+                mma_u8(D, A0.z & 0x0F0F0F0Fu, A0.w & 0x0F0F0F0Fu, (A0.z >> 4) & 0x0F0F0F0Fu, (A0.w >> 4) & 0x0F0F0F0Fu,
+                       B0, c0);
+                mma_u8(D, A1.z & 0x0F0F0F0Fu, A1.w & 0x0F0F0F0Fu, (A1.z >> 4) & 0x0F0F0F0Fu, (A1.w >> 4) & 0x0F0F0F0Fu,
+                       B1, D);
+                scale2(acc.f[1], D, R.s[u].z, R.s[u].w);
+            }
+        }
+    }
+}
+
+template <int UPI>
+__device__ __forceinline__ void compute(const Item<DTYPE_TQ2_0, UPI> &R, int nu, int p0, const XImage &xi,
+                                        LaneOff lo, int, Acc &acc) {
+#pragma unroll
+    for (int u = 0; u < UPI; ++u) {
+        if (u < nu) {
+            const uint8_t *bi = xi.img + (size_t)(p0 + u) * (2 * kImgBlock);
+            const uint2 B0 = lds<uint2>(bi + lo.b0), B1 = lds<uint2>(bi + lo.b1);
+            const uint4 W = R.a[u];
+            // Plane m (bits 2m, 2m+1 of every byte) is the fragment of half
+            // m & 1 and block 2p + (m >> 1), scaled by 4^m.
+            mma_u8(acc.d[0], W.x & 0x03030303u, W.y & 0x03030303u, W.z & 0x03030303u, W.w & 0x03030303u, B0,
+                   acc.d[0]);
+            mma_u8(acc.d[1], W.x & 0x0C0C0C0Cu, W.y & 0x0C0C0C0Cu, W.z & 0x0C0C0C0Cu, W.w & 0x0C0C0C0Cu, B0,
+                   acc.d[1]);
+            mma_u8(acc.d[2], W.x & 0x30303030u, W.y & 0x30303030u, W.z & 0x30303030u, W.w & 0x30303030u, B1,
+                   acc.d[2]);
+            mma_u8(acc.d[3], W.x & 0xC0C0C0C0u, W.y & 0xC0C0C0C0u, W.z & 0xC0C0C0C0u, W.w & 0xC0C0C0C0u, B1,
+                   acc.d[3]);
+        }
+    }
+}
+
+// Per-row results of a tile: lanes with tig == 0 hold rows g + 8i (i = 0..3)
+// as 8-byte values (fp32 bits for Q8_0 / Q4_0, already scaled by 2^-e; the
+// exact int64 sum of c * X for TQ2_0).  All lanes must call (shuffles).
+template <tensor_dtype_t DT>
+__device__ __forceinline__ void tile_rows(const Acc &acc, unsigned long long (&v)[4], float pe) {
+    if (DT == DTYPE_TQ2_0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int D[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                D[i] = h == 0 ? acc.d[0][i] + (acc.d[2][i] >> 4) : (acc.d[1][i] >> 2) + (acc.d[3][i] >> 6);
+            const int up0 = __shfl_down_sync(0xffffffffu, D[0], 1);
+            const int up2 = __shfl_down_sync(0xffffffffu, D[2], 1);
+            v[2 * h] = (unsigned long long)((long long)D[0] + 256LL * D[1] + 65536LL * up0);
+            v[2 * h + 1] = (unsigned long long)((long long)D[2] + 256LL * D[3] + 65536LL * up2);
+        }
+    } else {
+        // Lanes tig 0 / 2: digits 0-1 of blocks 2p / 2p+1; tig 1 / 3: digit 2.
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                float t = fmaf(65536.0f, __shfl_down_sync(0xffffffffu, acc.f[h][i], 1), acc.f[h][i]);
+                t += __shfl_down_sync(0xffffffffu, t, 2);
+                v[2 * h + i] = __float_as_uint(t * pe);
+            }
+    }
+}
+
+// rs: ternary row scale of row tile*32 + lane, loaded when the tile started.
+template <tensor_dtype_t DT>
+__device__ __forceinline__ float finish_row(const XImage &xi, unsigned long long v, bool nonfinite, float rs) {
+    float out;
+    if (DT == DTYPE_TQ2_0) {
+        out = (float)((double)rs * ((double)((long long)v - *xi.sx) * (double)*xi.pexp));
+    } else {
+        out = __uint_as_float((uint32_t)v);
+    }
+    return nonfinite ? __int_as_float(0x7FC00000) : out;
+}
+
+// Stores a finished tile (one row per lane), or its partial for a tile
+// shared with other warps.
+template <tensor_dtype_t DT>
+__device__ void flush_tile(const StreamParams &p, const XImage &xi, int tile, int lane, int my_warp, bool whole,
+                           const unsigned long long (&v)[4], bool nonfinite, float rs) {
+    if (whole) {
+        // Lane l takes row l = g + 8i from the lane holding it, (l % 8) * 4.
+        unsigned long long mine = v[0];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const unsigned long long t = __shfl_sync(0xffffffffu, v[i], (lane & 7) * 4);
+            if ((lane >> 3) == i) mine = t;
+        }
+        if (tile * 32 + lane < p.nrows) store_y(p, (size_t)tile * 32 + lane, finish_row<DT>(xi, mine, nonfinite, rs));
+        return;
+    }
+    // k = contributors of the tile, slot = this warp's rank among them.
+    const long long first = (long long)tile * p.nseg;
+    int k = 0, slot = -1;
+    const int o0 = item_owner(first, p.total_items, p.total_warps);
+    if (p.total_items >= p.total_warps) {
+        // Every warp owns at least one item, so the tile's owners are the
+        // consecutive warps o0..o1.
+        k = item_owner(first + p.nseg - 1, p.total_items, p.total_warps) - o0 + 1;
+        slot = my_warp - o0;
+    } else {
+        int prev = -1;
+        for (int s = 0; s < p.nseg; ++s) {
+            const int o = s == 0 ? o0 : item_owner(first + s, p.total_items, p.total_warps);
+            if (o != prev) {
+                if (o == my_warp) slot = k;
+                ++k;
+                prev = o;
+            }
+        }
+    }
+    long long *base64 = reinterpret_cast<long long *>(p.part) + (size_t)tile * p.kmax * 32;
+    float *base32 = reinterpret_cast<float *>(p.part) + (size_t)tile * p.kmax * 32;
+    if ((lane & 3) == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = (lane >> 2) + 8 * i;
+            if (DT == DTYPE_TQ2_0) base64[(size_t)slot * 32 + r] = (long long)v[i];
+            else base32[(size_t)slot * 32 + r] = __uint_as_float((uint32_t)v[i]);
+        }
+    }
+    __threadfence();
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atomicAdd(p.cnt + tile, 1);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == k - 1) {
+        __threadfence();
+        // The last contributor sums the slots in slot order, one row per lane.
+        const int r = lane;
+        unsigned long long sum;
+        if (DT == DTYPE_TQ2_0) {
+            long long s = 0;
+            for (int j = 0; j < k; ++j) s += __ldcg(base64 + (size_t)j * 32 + r);
+            sum = (unsigned long long)s;
+        } else {
+            float s = 0.0f;
+            for (int j = 0; j < k; ++j) s += __ldcg(base32 + (size_t)j * 32 + r);
+            sum = __float_as_uint(s);
+        }
+        if (tile * 32 + r < p.nrows) store_y(p, (size_t)tile * 32 + r, finish_row<DT>(xi, sum, nonfinite, rs));
+        __syncwarp();
+        if (lane == 0) p.cnt[tile] = 0;
+    }
+}
+
+// --------------------------------------------------------------- kernel ---
+template <tensor_dtype_t DT, int NC, int NS, int UPI>
+__global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_stream(const StreamParams p) {
+    constexpr int kSlot = slot_bytes<DT, UPI>();
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int s_nonfinite;
+    __shared__ int s_abort[kMaxConsumers];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // Shared memory: [rings][x image], barriers in static shared memory.
+    __shared__ __align__(8) uint64_t full[kMaxConsumers][NS];
+    __shared__ __align__(8) uint64_t empty[kMaxConsumers][NS];
+    uint8_t *rings = smem;
+    uint8_t *ximg = smem + (size_t)NC * NS * kSlot;
+    XImage xi;
+    xi.img = ximg;
+    const size_t img_b = (size_t)nb_even(p.nb) * kImgBlock;
+    xi.corr = reinterpret_cast<int *>(ximg + img_b);
+    const size_t tail = align16(img_b + (DT == DTYPE_Q4_0 ? (size_t)nb_even(p.nb) * 16 : 0));
+    xi.sx = reinterpret_cast<long long *>(ximg + tail);
+    xi.pexp = reinterpret_cast<float *>(ximg + tail + 16);
+    xi.nonfinite = &s_nonfinite;
+
+    const long long T = p.total_items, W = p.total_warps;
+    pdl_trigger();
+    if (threadIdx.x < NC * NS) {
+        mbar_init(&full[0][0] + threadIdx.x, 1);
+        mbar_init(&empty[0][0] + threadIdx.x, 32);
+    }
+    if (threadIdx.x < kMaxConsumers) s_abort[threadIdx.x] = 0;
+    if (threadIdx.x == 0) {
+        s_nonfinite = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == NC) {
+        // ------------------------------------------------------ producer --
+        // Lane c streams consumer c's items; the weight does not depend on
+        // earlier kernels, so it starts before the programmatic-launch wait.
+        const int c = lane;
+        if (c < NC) {
+            const int gw = blockIdx.x * NC + c;
+            const long long it0 = range_begin(gw, T, W), it1 = range_begin(gw + 1, T, W);
+            const int n = (int)(it1 - it0);
+            int tile = (int)(it0 / p.nseg), seg = (int)(it0 % p.nseg);
+            uint8_t *ring = rings + (size_t)c * NS * kSlot;
+            int issued = 0;
+            for (int j = 0; j < n; ++j) {
+                const int s = j % NS;
+                if (j >= NS) {
+                    const uint32_t ph = (uint32_t)((j / NS) - 1) & 1u;
+                    bool ok = false;
+                    for (unsigned i = 0; i < kWaitLimit; ++i) {
+                        if (mbar_try_wait(&empty[c][s], ph)) {
+                            ok = true;
+                            break;
+                        }
+                        if (*reinterpret_cast<volatile int *>(&s_abort[c])) break;
+                    }
+                    if (!ok) break;     // the consumer gave up (it reports the error)
+                }
+                const int u0 = seg * UPI;
+                const int nu = min(UPI, p.nunits - u0);
+                uint8_t *dst = ring + (size_t)s * kSlot;
+                if (!(p.test_unarmed && blockIdx.x == 0 && c == 0 && j == 0)) {
+                    if (Fmt<DT>::kBlockScales) {
+                        const int b0 = 2 * u0, nblk = min(2 * nu, p.nb - b0);
+                        const uint32_t cb = (uint32_t)nblk * Fmt<DT>::kBlockCode, sb = (uint32_t)nblk * 128u;
+                        mbar_expect_tx(&full[c][s], cb + sb);
+                        bulk_g2s(dst, p.codes + ((size_t)tile * p.nb + b0) * Fmt<DT>::kBlockCode, cb, &full[c][s]);
+                        bulk_g2s(dst + UPI * unit_code<DT>(), p.scales + ((size_t)tile * p.nb + b0) * 32, sb,
+                                 &full[c][s]);
+                    } else {
+                        const uint32_t cb = (uint32_t)nu * unit_code<DT>();
+                        mbar_expect_tx(&full[c][s], cb);
+                        bulk_g2s(dst, p.codes + ((size_t)tile * p.nunits + u0) * unit_code<DT>(), cb, &full[c][s]);
+                    }
+                    issued = j + 1;
+                }
+                if (++seg == p.nseg) {
+                    seg = 0;
+                    ++tile;
+                }
+            }
+            // Copies still in flight land before the CTA exits: wait for the
+            // last NS issued items' slots (their consumer may have left).
+            for (int q = max(0, issued - NS); q < issued; ++q) {
+                if (p.test_unarmed && blockIdx.x == 0 && c == 0 && q == 0) continue;
+                for (unsigned i = 0; i < kWaitLimit; ++i)
+                    if (mbar_try_wait(&full[c][q % NS], (uint32_t)(q / NS) & 1u)) break;
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------ consumers --
+        const int gw = blockIdx.x * NC + warp;
+        const long long it0 = range_begin(gw, T, W), it1 = range_begin(gw + 1, T, W);
+        const int n = (int)(it1 - it0);
+        const int tig = lane & 3;
+        pdl_wait();
+        prepare_x<DT, NC>(p, xi);
+        consumers_sync(NC * 32);
+        const bool nonfinite = s_nonfinite != 0;
+        const float pe = *xi.pexp;
+        const LaneOff lo = lane_offsets<DT>(lane);
+        const bool odd_nb = (p.nb & 1) != 0;
+
+        int cur_tile = -1, tile = (int)(it0 / p.nseg), seg = (int)(it0 % p.nseg);
+        float row_scale = 0.0f;
+        bool cur_whole = false;
+        Acc acc;
+        acc.reset();
+        for (int j = 0; j < n; ++j) {
+            const int s = j % NS;
+            const uint32_t ph = (uint32_t)(j / NS) & 1u;
+            const unsigned limit = (j == 0 && p.test_unarmed && blockIdx.x == 0 && warp == 0) ? p.wait_limit
+                                                                                              : kWaitLimit;
+            bool ok = false;
+            for (unsigned i = 0; i < limit; ++i)
+                if (mbar_try_wait(&full[warp][s], ph)) {
+                    ok = true;
+                    break;
+                }
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) {
+                if (lane == 0) {
+                    atomicOr(p.err, 1);
+                    s_abort[warp] = 1;
+                }
+                __syncwarp();
+                cur_tile = -1;     // nothing is stored for an unfinished tile
+                break;
+            }
+            const int u0 = seg * UPI;
+            const int nu = min(UPI, p.nunits - u0);
+            Item<DT, UPI> R;
+            R.load(rings + ((size_t)warp * NS + s) * kSlot, nu, lane, odd_nb && u0 + nu == p.nunits);
+            mbar_arrive(&empty[warp][s]);
+
+            if (tile != cur_tile) {
+                if (cur_tile >= 0) {
+                    unsigned long long v[4] = {0, 0, 0, 0};
+                    tile_rows<DT>(acc, v, pe);
+                    flush_tile<DT>(p, xi, cur_tile, lane, gw, cur_whole, v, nonfinite, row_scale);
+                }
+                cur_tile = tile;
+                acc.reset();
+                cur_whole = (seg == 0) && ((long long)tile * p.nseg + p.nseg <= it1);
+                if (DT == DTYPE_TQ2_0) row_scale = __ldg(p.scales + (size_t)tile * 32 + lane);
+            }
+            compute<UPI>(R, nu, u0, xi, lo, tig, acc);
+            if (++seg == p.nseg) {
+                seg = 0;
+                ++tile;
+            }
+        }
+        if (cur_tile >= 0) {
+            unsigned long long v[4] = {0, 0, 0, 0};
+            tile_rows<DT>(acc, v, pe);
+            flush_tile<DT>(p, xi, cur_tile, lane, gw, cur_whole, v, nonfinite, row_scale);
+        }
+    }
+    __syncthreads();
+}
+
+// ----------------------------------------------------------------- host ---
+struct StreamCfg {
+    int nc, ns, upi;
+};
+
+size_t stream_smem(tensor_dtype_t dt, int nb, StreamCfg c) {
+    int slot = 0;
+    switch (dt) {
+        case DTYPE_Q8_0: slot = c.upi * (unit_code<DTYPE_Q8_0>() + unit_scale<DTYPE_Q8_0>()); break;
+        case DTYPE_Q4_0: slot = c.upi * (unit_code<DTYPE_Q4_0>() + unit_scale<DTYPE_Q4_0>()); break;
+        case DTYPE_TQ2_0: slot = c.upi * unit_code<DTYPE_TQ2_0>(); break;
+        default: return 0;
+    }
+    return (size_t)c.nc * c.ns * slot + ximg_bytes(nb, dt == DTYPE_Q4_0);
+}
+
+// Configurations instantiated per format: (consumer warps, slots, units per
+// item).  SAPPHIRE_STREAM_CFG = an index selects one (tuning runs);
+// otherwise the first that fits shared memory with at least six items per
+// consumer warp on average, else the one with the most items per warp.
+// Consumer counts of 7, 11 and 15 make 8, 12 and 16 warps with the producer:
+// a whole number of warps per SM sub-partition, so no sub-partition's
+// register file caps the others' registers per thread.
+constexpr StreamCfg kQ8Cfgs[] = {{11, 3, 2}, {15, 2, 2}, {11, 2, 3}, {7, 4, 2}};
+constexpr StreamCfg kQ4Cfgs[] = {{11, 2, 5}, {11, 3, 4}, {15, 2, 4}, {11, 4, 2}, {15, 3, 2}};
+constexpr StreamCfg kTq2Cfgs[] = {{15, 4, 5}, {15, 2, 8}, {15, 3, 4}, {11, 4, 5}, {15, 4, 4}};
+
+// Dynamic shared memory a configuration may use (the static barriers and
+// reduction arrays take the rest of the 227 KB per block).
+constexpr size_t kStreamSmemMax = 225 * 1024;
+
+// {0, 0, 0} when no configuration fits (rows too long for the x image).
+template <size_t N>
+StreamCfg pick(const StreamCfg (&cfgs)[N], const DevWeight &w, int sms, int env) {
+    if (env >= 0 && env < (int)N && stream_smem(w.dtype, w.nb, cfgs[env]) <= kStreamSmemMax) return cfgs[env];
+    const int nunits = (w.nb + 1) / 2;
+    StreamCfg best = {0, 0, 0};
+    double best_ipw = -1.0;
+    for (size_t i = 0; i < N; ++i) {
+        const StreamCfg c = cfgs[i];
+        if (stream_smem(w.dtype, w.nb, c) > kStreamSmemMax) continue;
+        const long long items = (long long)w.ntiles * ((nunits + c.upi - 1) / c.upi);
+        const double ipw = (double)items / ((double)sms * c.nc);
+        if (ipw >= 6.0) return c;
+        if (ipw > best_ipw) {
+            best_ipw = ipw;
+            best = c;
+        }
+    }
+    return best;
+}
+
+StreamCfg stream_cfg(const DevWeight &w, int sms) {
+    static const int env = [] {
+        const char *v = getenv("SAPPHIRE_STREAM_CFG");
+        return v ? atoi(v) : -1;
+    }();
+    switch (w.dtype) {
+        case DTYPE_Q8_0: return pick(kQ8Cfgs, w, sms, env);
+        case DTYPE_Q4_0: return pick(kQ4Cfgs, w, sms, env);
+        default: return pick(kTq2Cfgs, w, sms, env);
+    }
+}
+
+template <typename K>
+cudaError_t smem_optin(K kernel, int device, size_t smem) {
+    static std::mutex mu;
+    static std::unordered_map<const void *, size_t> set[64];
+    if (device < 0 || device >= 64)
+        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    std::lock_guard<std::mutex> lk(mu);
+    size_t &cur = set[device][reinterpret_cast<const void *>(kernel)];
+    if (smem <= cur) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) cur = smem;
+    return e;
+}
+
+template <tensor_dtype_t DT, int NC, int NS, int UPI>
+int run_cfg(kernel_context_t *ctx, const StreamParams &p, int grid, size_t smem, cudaStream_t st) {
+    auto kernel = gemv_stream<DT, NC, NS, UPI>;
+    cudaError_t e = smem_optin(kernel, ctx->device, smem);
+    if (e != cudaSuccess) {
+        ctx_fail(ctx, "launch_gemv_stream", "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    e = launch_pdl(kernel, dim3(grid), dim3((NC + 1) * 32), smem, st, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        ctx_fail(ctx, "launch_gemv_stream", "launch failed: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+#define SAPPHIRE_STREAM_TRY(DT, NC, NS, UPI) \
+    if (c.nc == NC && c.ns == NS && c.upi == UPI) return run_cfg<DT, NC, NS, UPI>(ctx, p, grid, smem, st);
+
+int dispatch(kernel_context_t *ctx, tensor_dtype_t dt, StreamCfg c, const StreamParams &p, int grid, size_t smem,
+             cudaStream_t st) {
+    if (dt == DTYPE_Q8_0) {
+        SAPPHIRE_STREAM_TRY(DTYPE_Q8_0, 11, 3, 2)
+        SAPPHIRE_STREAM_TRY(DTYPE_Q8_0, 15, 2, 2)
+        SAPPHIRE_STREAM_TRY(DTYPE_Q8_0, 11, 2, 3)
+        SAPPHIRE_STREAM_TRY(DTYPE_Q8_0, 7, 4, 2)
+    } else if (dt == DTYPE_Q4_0) {
+        SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 11, 2, 5)
+        SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 11, 3, 4)
+        SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 15, 2, 4)
+        SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 11, 4, 2)
+        SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 15, 3, 2)
+    } else if (dt == DTYPE_TQ2_0) {
+        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 15, 4, 5)
+        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 15, 2, 8)
+        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 15, 3, 4)
+        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 11, 4, 5)
+        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 15, 4, 4)
+    }
+    ctx_fail(ctx, "launch_gemv_stream", "no kernel instantiated for this configuration");
+    return -1;
+}
+#undef SAPPHIRE_STREAM_TRY
+
+// Largest number of warps that can share one tile: ranges hold at least
+// floor(T/W) items each, so nseg consecutive items meet at most
+// ceil((nseg-1)/L) + 1 of them; with fewer items than warps every range holds
+// at most one item.
+int stream_kmax(long long T, long long W, int nseg) {
+    if (T <= 0) return 1;
+    if (T < W) return nseg;
+    const long long L = T / W;
+    const long long k = (nseg - 1 + L - 1) / L + 1;
+    return (int)(k < nseg ? k : nseg);
+}
+
+struct Geometry {
+    StreamCfg c;
+    int nunits, nseg, grid;
+    long long items;
+};
+
+Geometry geometry(kernel_context_t *ctx, const DevWeight &w) {
+    Geometry g;
+    const int sms = sm_count(ctx->device);
+    g.c = stream_cfg(w, sms);
+    g.nunits = (w.nb + 1) / 2;
+    if (g.c.nc == 0) {
+        g.nseg = 0;
+        g.items = 0;
+        g.grid = 0;
+        return g;
+    }
+    g.nseg = (g.nunits + g.c.upi - 1) / g.c.upi;
+    g.items = (long long)w.ntiles * g.nseg;
+    // One CTA per SM, or fewer when the weight has fewer items than a full
+    // grid has consumer warps: every warp gets work.
+    const long long want = (g.items + g.c.nc - 1) / g.c.nc;
+    g.grid = (int)std::min<long long>(sms, std::max<long long>(1, want));
+    return g;
+}
+
+// Test hook (sapphire_test_stream_unarmed): 1 = the next launches leave consumer
+// 0 of CTA 0 without its first copy, with a short wait limit.
+std::atomic<int> g_test_unarmed{0};
+
+}  // namespace
+
+bool stream_dtype(tensor_dtype_t dt) { return dt == DTYPE_Q8_0 || dt == DTYPE_Q4_0 || dt == DTYPE_TQ2_0; }
+
+bool stream_supported(kernel_context_t *ctx, const DevWeight &w) {
+    if (!stream_dtype(w.dtype) || w.nb <= 0) return false;
+    // TQ2_0 plane sums: 64 * 2 * 128 per element over half the blocks of a
+    // row stay below 2^31 for up to 8192 blocks.
+    if (w.dtype == DTYPE_TQ2_0 && w.nb > 8192) return false;
+    return geometry(ctx, w).c.nc > 0;
+}
+
+void stream_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints) {
+    const Geometry g = geometry(ctx, w);
+    const long long W = (long long)g.grid * g.c.nc;
+    *part_floats = (size_t)w.ntiles * stream_kmax(g.items, W, g.nseg) * 32 * (w.dtype == DTYPE_TQ2_0 ? 2 : 1);
+    *cnt_ints = (size_t)w.ntiles;
+}
+
+int launch_gemv_stream(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
+                       int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
+                       cudaStream_t st) {
+    if (w.ntiles == 0) return 0;
+    if (ll_n < 0 || ll_n > kMaxPeers) {
+        ctx_fail(ctx, "launch_gemv_stream", "%d gather targets (at most %d)", ll_n, kMaxPeers);
+        return -1;
+    }
+    const Geometry g = geometry(ctx, w);
+    if (g.c.nc == 0) {
+        ctx_fail(ctx, "launch_gemv_stream", "%s weight with %d columns exceeds the kernel's shared-memory budget",
+                 dtype_name(w.dtype), w.cols);
+        return -1;
+    }
+    StreamParams p{};
+    p.codes = reinterpret_cast<const uint8_t *>(w.codes);
+    p.scales = w.scales;
+    p.x = x;
+    p.y = y;
+    p.part = part;
+    p.cnt = cnt;
+    p.err = err;
+    p.nrows = w.nrows;
+    p.cols = w.cols;
+    p.nb = w.nb;
+    p.nunits = g.nunits;
+    p.ntiles = w.ntiles;
+    p.nseg = g.nseg;
+    p.total_items = g.items;
+    p.total_warps = g.grid * g.c.nc;
+    p.kmax = stream_kmax(g.items, p.total_warps, g.nseg);
+    p.test_unarmed = g_test_unarmed.load() ? 1 : 0;
+    p.wait_limit = p.test_unarmed ? (1u << 12) : kWaitLimit;
+    p.ll_n = ll_n;
+    p.ll_off = ll_off;
+    p.ll_epoch = ll_epoch;
+    for (int k = 0; k < kMaxPeers; ++k) p.ll[k] = k < ll_n ? ll[k] : nullptr;
+    const size_t smem = stream_smem(w.dtype, w.nb, g.c);
+    return dispatch(ctx, w.dtype, g.c, p, g.grid, smem, st);
+}
+
+// Test-only: makes the following quantized batch-1 GEMV launches leave one
+// consumer warp without its first copy (an mbarrier nothing arms) and give it
+// a short wait limit, so the bounded wait runs out and the error path runs.
+// No GPU fault is involved.  on = 0 restores normal launches.
+extern "C" SAPPHIRE_API int sapphire_test_stream_unarmed(int on) {
+    g_test_unarmed.store(on ? 1 : 0);
+    return 0;
+}

@@ -42,7 +42,8 @@ struct PeerGather {
 // Chunk contents per dtype (weights in column order):
 //     Q8_0 : 16 int8 codes, two chunks per block, nscale = nb
 //     Q4_0 : the block's 16 code bytes (32 weights, interleaved nibbles), nscale = nb
-//     TQ2_0: two 8-byte trit blocks (64 weights), nscale = 1 (row scale)
+//     TQ2_0: 64 columns (two trit blocks) of 32 rows per 512-byte chunk group,
+//            interleaved as 2-bit planes (repack.cu), nscale = 1 (row scale)
 //     F32  : 4 floats;  BF16: 8 bf16 values; nscale = 0
 // Padding rows (past the tensor's last row) hold zero codes and zero scales.
 struct DevWeight {
@@ -204,12 +205,18 @@ int launch_row_dot(kernel_context_t *ctx, tensor_dtype_t dt, const void *row, co
 int launch_axpy(kernel_context_t *ctx, float *y, const float *t, float alpha, size_t n,
                 cudaStream_t stream);
 
+// The context's error word (mapped host memory; created at kernel_ctx_init).
+int ensure_err_word(kernel_context_t *ctx);
 // Error word (mapped host memory) plus split-tile scratch of the pipelined
 // GEMV, grown to at least the given sizes.
 int ensure_pipe_scratch(kernel_context_t *ctx, size_t part_floats, size_t cnt_ints);
 
-// Pipelined batch-1 GEMV (gemv_pipe.cu).
-bool pipe_supported(const DevWeight &w);
+// SMs of a device (cached; 148 when the query fails).
+int sm_count(int dev);
+
+// Pipelined batch-1 GEMV (gemv_pipe.cu): quantized formats are served by
+// gemv_stream (gemv_stream.cu), dense F32 / BF16 by gemv_pipe.
+bool pipe_supported(kernel_context_t *ctx, const DevWeight &w);
 void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints);
 int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part,
                      int *cnt, int *err, cudaStream_t stream);
@@ -219,6 +226,13 @@ int pipe_kmax(long long T, long long W, int nseg);
 int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
                         int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
                         cudaStream_t stream);
+// Streaming batch-1 GEMV of the quantized formats (gemv_stream.cu).
+bool stream_dtype(tensor_dtype_t dt);
+bool stream_supported(kernel_context_t *ctx, const DevWeight &w);
+void stream_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints);
+int launch_gemv_stream(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
+                       int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
+                       cudaStream_t stream);
 // Latency-bound GEMV of a small Q8_0 / Q4_0 weight (gemv_pipe.cu): one CTA per
 // 32-row tile, no scratch.
 bool direct_supported(const DevWeight &w);
@@ -240,7 +254,8 @@ int launch_gemv_best(kernel_context_t *ctx, const DevWeight &w, const float *x, 
 int launch_product(kernel_context_t *ctx, const DevWeight &w, const float *x, int x_stride, float *y, int y_stride,
                    int batch, cudaStream_t stream);
 // Reads and clears the error word after a synchronisation; -1 if a kernel
-// reported a failed wait.
+// reported a failed wait (the split-tile counters are then cleared too).
+// Bits: 1 GEMV copy wait, 2/4 prefill-product waits, 8 peer-gather wait.
 int check_kernel_error(kernel_context_t *ctx, const char *who);
 
 // Tensor-core batched product of a Q4_0 weight (gemm_tc.cu), used for

@@ -14,11 +14,12 @@
 //          1024 bytes per (tile, block), half-major then lane.
 //   Q4_0 : a uint4 of code word tig (bytes 4tig..4tig+3, i.e. elements
 //          8tig..8tig+7) of rows g, g+8, g+16, g+24; 512 bytes per (tile, block).
-//   TQ2_0: a uint2 of four 16-bit values, rows g, g+8, g+16, g+24, each
-//          (block byte tig) | (block byte 4+tig) << 8; 256 bytes per (tile, block).
-// Scales: per (tile, block) (Q8_0 / Q4_0) or per tile (TQ2_0), 32 floats in
-// the order g*4 + i -> row g + 8i.  Rows past the tensor are zero codes
-// (TQ2_0: code 1, trit 0) with zero scales.
+//   TQ2_0: per pair of blocks (a "unit", 64 columns) a uint4 per lane whose
+//          2-bit planes are four A fragments (repack_tq2_0 below); 512 bytes
+//          per (tile, unit).
+// Scales: per (tile, block) (Q8_0 / Q4_0), 32 floats in the order
+// g*4 + i -> row g + 8i; per tile (TQ2_0), 32 floats in row order.  Rows past
+// the tensor are zero codes (TQ2_0: code 1, trit 0) with zero scales.
 #include "internal.cuh"
 
 namespace {
@@ -89,33 +90,43 @@ __global__ void repack_q4_0(const uint8_t *__restrict__ src, int nrows, int nb, 
     }
 }
 
-// TQ2_0 row: 4-byte scale then nb 8-byte blocks.  One thread per (tile, block, lane).
-__global__ void repack_tq2_0(const uint8_t *__restrict__ src, int nrows, int nb, int kchunks, int tile0,
-                             int ntile_in, uint2 *__restrict__ codes, float *__restrict__ scales, bool aligned) {
+// TQ2_0 row: 4-byte scale then nb 8-byte blocks.  One thread per (tile,
+// unit, lane); unit p holds blocks 2p and 2p+1 as four words per lane whose
+// 2-bit planes are four mma A fragments: word i, byte j, bits 2m..2m+1 hold
+// the code of row 16*(m&1) + g + 8*(i&1), column
+// 32*(2p + (m>>1)) + 16*(i>>1) + 4*tig + j.  Codes of blocks past the row and
+// of rows past the tensor are 1 (trit 0).  Scales: 32 floats per tile in row
+// order (0 for rows past the tensor).
+__global__ void repack_tq2_0(const uint8_t *__restrict__ src, int nrows, int nb, int nunits, int tile0,
+                             int ntile_in, uint4 *__restrict__ codes, float *__restrict__ scales, bool aligned) {
     const size_t row_bytes = 4 + (size_t)8 * nb;
-    const size_t n = (size_t)ntile_in * nb * 32;
+    const size_t n = (size_t)ntile_in * nunits * 32;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const int lane = (int)(i & 31);
-        const size_t tb = i >> 5;
-        const int b = (int)(tb % nb);
-        const int tl = (int)(tb / nb);
+        const size_t tu = i >> 5;
+        const int p = (int)(tu % nunits);
+        const int tl = (int)(tu / nunits);
         const int g = lane >> 2, tig = lane & 3;
-        uint32_t u[4];
+        uint32_t wd[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int r = tl * 32 + g + 8 * k;
-            if (r < nrows) {
-                const uint8_t *blk = src + (size_t)r * row_bytes + 4 + (size_t)8 * b;
-                u[k] = (uint32_t)blk[tig] | ((uint32_t)blk[4 + tig] << 8);
-            } else {
-                u[k] = 0x5555u;                    // trits 0
+        for (int ii = 0; ii < 4; ++ii) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int r = tl * 32 + 16 * (m & 1) + g + 8 * (ii & 1);
+                const int b = 2 * p + (m >> 1);
+                // Byte 4*(ii/2) + tig of the block holds columns 16*(ii/2) + 4*tig + j at bits 2j.
+                uint32_t byte = 0x55u;
+                if (r < nrows && b < nb) byte = src[(size_t)r * row_bytes + 4 + (size_t)8 * b + 4 * (ii >> 1) + tig];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) word |= ((byte >> (2 * j)) & 3u) << (8 * j + 2 * m);
             }
+            wd[ii] = word;
         }
         const size_t tile = (size_t)tile0 + tl;
-        // A tile spans kchunks * 512 bytes = kchunks * 64 uint2.
-        codes[tile * (size_t)kchunks * 64 + (size_t)b * 32 + lane] = make_uint2(u[0] | (u[1] << 16), u[2] | (u[3] << 16));
-        if (b == 0) {
-            const int r = tl * 32 + scale_row(lane);
+        codes[(tile * nunits + p) * 32 + lane] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        if (p == 0) {
+            const int r = tl * 32 + lane;
             scales[tile * 32 + lane] = r < nrows ? __uint_as_float(ld_u32(src + (size_t)r * row_bytes, aligned)) : 0.0f;
         }
     }
@@ -180,9 +191,9 @@ int launch_repack(kernel_context_t *ctx, const DevWeight &w, const void *src, in
             break;
         }
         case DTYPE_TQ2_0: {
-            size_t n = (size_t)ntile_in * w.nb * 32;
-            repack_tq2_0<<<grid_for(n), 256, 0, st>>>(s, nrows, w.nb, w.kchunks, tile0, ntile_in,
-                                                      reinterpret_cast<uint2 *>(w.codes), w.scales, aligned);
+            size_t n = (size_t)ntile_in * w.kchunks * 32;
+            repack_tq2_0<<<grid_for(n), 256, 0, st>>>(s, nrows, w.nb, w.kchunks, tile0, ntile_in, w.codes, w.scales,
+                                                      aligned);
             break;
         }
         case DTYPE_F32:

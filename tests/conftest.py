@@ -25,6 +25,16 @@ def normwise_rel(y, ref) -> float:
     return float(np.max(np.abs(y - ref)) / (den if den > 0 else 1.0))
 
 
+def elem_rel_floor(y, ref, floor_frac: float = 1e-3) -> float:
+    """max_i |y_i - ref_i| / max(|ref_i|, floor_frac * max|ref|): per-element
+    relative error with a floor (rows that cancel to near zero would make the
+    plain per-element ratio meaningless)."""
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    den = np.maximum(np.abs(ref), floor_frac * max(float(np.max(np.abs(ref))), 1e-300))
+    return float(np.max(np.abs(y - ref) / den))
+
+
 # Parity bar of the GEMV path: normwise relative error against the fp32
 # reference result (the north-star tolerance).
 GEMV_RTOL = 1e-4

@@ -359,3 +359,80 @@ def test_ternary_full_size(sp, ctx, oracle):
     ref = oracle.gemv(TQ2_0, packed, cfg.rows, cfg.cols, X)[0]
     assert normwise_rel(y, ref) < GEMV_RTOL
     sp.lib.kernel_tensor_evict(ctx.handle, A.handle)
+
+
+# ----------------------------------------- streaming kernel, odd geometry --
+# Q8_0 / Q4_0 weights of more than 512 tiles or more than 64 blocks per row
+# run the streaming kernel (smaller ones the latency-bound direct kernel);
+# TQ2_0 always does.  Odd block counts leave the last 64-column unit with one
+# block; ragged rows leave a partial last tile.
+STREAM_SHAPES = [(Q8_0, 20000, 96), (Q8_0, 1000, 2080), (Q4_0, 16421, 96), (Q4_0, 777, 2080),
+                 (Q4_0, 17000, 640), (TQ2_0, 100, 80), (TQ2_0, 3001, 2080), (TQ2_0, 33, 16384)]
+
+
+@pytest.mark.parametrize("dtype,rows,cols", STREAM_SHAPES)
+def test_stream_kernel_shapes(sp, ctx, oracle, dtype, rows, cols):
+    packed = rand_packed(oracle, dtype, rows, cols, seed=rows + 3 * cols)
+    x = np.random.default_rng(rows).standard_normal(cols, dtype=np.float32)
+    A = sp.Tensor(dtype, (rows, cols), packed)
+    y = sp.gemv(ctx, A, x)
+    assert normwise_rel(y, oracle_y(oracle, dtype, packed, rows, cols, x)[0]) < GEMV_RTOL
+    assert np.array_equal(y, sp.gemv(ctx, A, x))          # repeatable bit for bit
+
+
+# ------------------------------------------- high-dynamic-range activations --
+# x is converted to a 22-bit fixed-point image with one exponent for all of x
+# (the streaming kernel and the Q8_0 direct kernel; the Q4_0 direct kernel
+# uses fp32 x).  These cases stress that conversion: outliers 1e3 / 1e4 above
+# the bulk, magnitudes spread over eight decades, an all-zero block beside a
+# block of tiny values.  Bar: normwise error <= 1e-4 against the oracle in f64
+# (the GEMV parity bar); the per-element relative error with a floor of
+# 1e-3 * max|y| is printed and checked against a looser 5e-2 (a 1e4 outlier
+# over 16384 N(0,1) columns puts the fixed-point step at 2^-8, about 1e-1 of
+# accumulated error on a row, the size of an fp32 sum's own rounding there).
+def hdr_x(kind: str, cols: int, seed: int) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    if kind == "outliers":
+        x = rng.standard_normal(cols).astype(np.float32)
+        i = rng.choice(cols, size=2, replace=False)
+        x[i[0]] = np.float32(1e3) * rng.choice([-1, 1])
+        x[i[1]] = np.float32(1e4) * rng.choice([-1, 1])
+    elif kind == "decades":
+        x = (10.0 ** rng.uniform(-6, 2, cols) * rng.choice([-1.0, 1.0], cols)).astype(np.float32)
+    else:                                            # zero block and tiny block
+        x = rng.standard_normal(cols).astype(np.float32)
+        nb = cols // 32
+        x[32 * (nb // 3): 32 * (nb // 3) + 32] = 0.0
+        x[32 * (2 * nb // 3): 32 * (2 * nb // 3) + 32] *= np.float32(1e-7)
+    return x
+
+
+HDR_SHAPES = [(Q8_0, 20000, 640), (Q4_0, 20000, 640), (TQ2_0, 20000, 640), (Q8_0, 2048, 640),
+              (Q4_0, 2048, 640), (Q8_0, 1024, 16384), (Q4_0, 1024, 16384), (TQ2_0, 1024, 16384)]
+
+
+@pytest.mark.parametrize("kind", ["outliers", "decades", "zero_tiny"])
+@pytest.mark.parametrize("dtype,rows,cols", HDR_SHAPES)
+def test_high_dynamic_range_x(sp, ctx, oracle, dtype, rows, cols, kind):
+    from conftest import elem_rel_floor
+    packed = rand_packed(oracle, dtype, rows, cols, seed=rows + cols + dtype)
+    x = hdr_x(kind, cols, seed=cols + dtype)
+    y = sp.gemv(ctx, sp.Tensor(dtype, (rows, cols), packed), x)
+    ref = oracle_y(oracle, dtype, packed, rows, cols, x)[0]
+    nw, el = normwise_rel(y, ref), elem_rel_floor(y, ref)
+    print(f"HDR {kind} dtype={dtype} {rows}x{cols}: normwise {nw:.3e} per-element(floor 1e-3) {el:.3e}")
+    assert nw < GEMV_RTOL
+    assert el < 5e-2
+
+
+# --------------------------------------------- LM-head shape, all formats --
+@pytest.mark.parametrize("cfg", [workloads.C2_Q4, workloads.C2_TQ2], ids=lambda c: c.name)
+def test_lm_head_shape_q4_0_and_ternary(sp, ctx, oracle, cfg):
+    src, X = workloads.make_inputs(cfg, seed=0)
+    packed = sp.pack_tq2(ctx, *src) if cfg.dtype == TQ2_0 else sp.quantize(ctx, cfg.dtype, src)
+    del src
+    A = sp.Tensor(cfg.dtype, (cfg.rows, cfg.cols), packed)
+    y = sp.gemv(ctx, A, X[0])
+    ref = oracle.gemv(cfg.dtype, packed, cfg.rows, cfg.cols, X, f64=True)[0]
+    assert normwise_rel(y, ref) < GEMV_RTOL
+    sp.lib.kernel_tensor_evict(ctx.handle, A.handle)
