@@ -98,10 +98,14 @@ typedef void (*parallel_for_fn_t)(void* arg, int idx);
 SAPPHIRE_API int kernel_parallel_for(kernel_context_t *ctx, parallel_for_fn_t fn, void* arg, int n);
 
 /* One-row dot products.  W_row and x are host pointers; the row is computed
- * on the GPU of a process-wide default context (one launch per call), so these
- * are correct but slow: they exist for ABI compatibility with callers of the
- * reference row kernels (its tests and benches).  block_size must be 32 for the
- * quantized forms (the reference returns 0.0f otherwise, and so do these). */
+ * on the GPU of a process-wide default context: every call copies the row
+ * and x to the device, launches one kernel and synchronises with the GPU
+ * before it returns (tens of microseconds per call, against well under a
+ * microsecond for the reference's AVX2 row on the host).  They are correct
+ * but slow: they exist for ABI compatibility with callers of the reference
+ * row kernels (its tests and benches); whole products belong in kernel_gemv.
+ * block_size must be 32 for the quantized forms (the reference returns 0.0f
+ * otherwise, and so do these). */
 SAPPHIRE_API float quantized_gemv_q4_0_aligned(const void *W_row, const float *x, int block_count, int block_size);
 SAPPHIRE_API float quantized_gemv_q4_0_unaligned(const void *W_row, const float *x, int block_count, int block_size);
 SAPPHIRE_API float quantized_gemv_q8_0_aligned(const void *W_row, const float *x, int block_count, int block_size);

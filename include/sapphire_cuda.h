@@ -89,14 +89,19 @@ SAPPHIRE_API int kernel_gemm_device_bf16(kernel_context_t *ctx, float *Y, const 
  *  pointers on the context's GPU; the work is enqueued on the context stream.
  *  Scratch is a fixed 4 MiB device array inside the library, held by every
  *  GPU that loads it until exit.  The scratch grows with the row count (about
- *  260 bytes per 32 rows at 640 columns: the 262144-row LM head needs 2.1 MB);
- *  a weight that needs more than 4 MiB is rejected with -1 and an error
- *  message.  The first call on a device looks up the
- *  array's device address, so make that call before any stream capture.  All
- *  calls share the array and it keeps the last call's contents (each call
- *  clears what must start at zero): calls that overlap on the GPU, from any
- *  context or stream, race.  Not for sharded contexts. */
+ *  260 bytes per 32 rows for Q8_0 / Q4_0 and twice that for TQ2_0 at 640
+ *  columns: the 262144-row Q8_0 LM head needs 2.1 MB); a weight that needs
+ *  more than 4 MiB is rejected with -1 and an error message.  The first call
+ *  on a device looks up the array's device address, so make that call before
+ *  any stream capture.  All calls share the array and it keeps the last
+ *  call's contents (each call clears what must start at zero): calls that
+ *  overlap on the GPU, from any context or stream, race.  A kernel error (an
+ *  expired bounded wait) is recorded in the context's error word and returned
+ *  as -1 by the next kernel_ctx_synchronize.  Not for sharded contexts. */
 SAPPHIRE_API int kernel_gemv_device_noalloc(kernel_context_t *ctx, float *y, const tensor_t *A, const float *x);
+/** Waits for the context stream; -1 if it failed or if a kernel enqueued by
+ *  an asynchronous call since the last check reported an expired bounded
+ *  wait (details via kernel_ctx_last_error). */
 SAPPHIRE_API int kernel_ctx_synchronize(kernel_context_t *ctx);
 /** The context's cudaStream_t (as void*). */
 SAPPHIRE_API void* kernel_ctx_get_stream(kernel_context_t *ctx);
@@ -152,6 +157,25 @@ SAPPHIRE_API int kernel_ctx_shard_info(kernel_context_t *ctx, int *rank, int *wo
  *  `world_size` (the rule above; *nrows may be 0 for trailing ranks).
  *  Pure arithmetic, no GPU.  0 on success, -1 on bad arguments. */
 SAPPHIRE_API int sapphire_shard_rows(int rows, int rank, int world_size, int *row0, int *nrows);
+
+/* ------------------------------------------------------------------------- *
+ * Test hooks for the bounded-wait error paths.  No reference counterpart
+ * (the reference has no device waits).  They make a wait run out without any
+ * GPU fault - a barrier or a flag that nothing sets - so tests can check that
+ * the error is reported and the context stays usable.
+ * ------------------------------------------------------------------------- */
+/** on != 0: the following quantized batch-1 GEMV launches (kernel_gemv,
+ *  kernel_gemv_device, kernel_gemv_device_noalloc) give one consumer warp a
+ *  shared-memory slot that no copy fills and a short wait limit; the call (or
+ *  the next kernel_ctx_synchronize) returns -1.  on = 0 restores normal
+ *  launches.  Process-wide. */
+SAPPHIRE_API int sapphire_test_stream_unarmed(int on);
+/** Runs the peer-gather pull of a sharded product over a local buffer of
+ *  `rows` words that nothing writes, with a wait limit of wait_ns
+ *  nanoseconds: y (device, `rows` floats) receives NaN and the call returns -1
+ *  with the expiry recorded in kernel_ctx_last_error. */
+SAPPHIRE_API int sapphire_test_pull_expiry(kernel_context_t *ctx, float *y, long long rows,
+                                           unsigned long long wait_ns);
 
 #ifdef __cplusplus
 }

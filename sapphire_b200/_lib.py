@@ -101,6 +101,8 @@ _SIGNATURES = {
     "kernel_shard_unique_id": (i32, [vp]),
     "kernel_ctx_init_sharded": (i32, [vp, i32, i32, vp]),
     "kernel_ctx_shard_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32)]),
+    "sapphire_test_stream_unarmed": (i32, [i32]),
+    "sapphire_test_pull_expiry": (i32, [vp, vp, C.c_longlong, C.c_ulonglong]),
     # include/sapphire_decode.h
     "sapphire_decoder_create": (vp, [vp, vp, vp]),
     "sapphire_decoder_generate": (i32, [vp, vp, i32, i32, vp, vp]),

@@ -126,24 +126,24 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
 // Common validation of kernel_gemv (src/kernels/dispatch.c:101-156).
 int check_gemv_args(const char *who, float *y, const tensor_t *A, const float *x) {
     if (!y || !A || !x) {
-        LOG_ERROR("%s null pointer", who);
+        LOG_ERROR("%s: NULL y, A or x", who);
         return -1;
     }
     if (tensor_ndim(A) != 2) {
-        LOG_ERROR("%s weight must be 2D", who);
+        LOG_ERROR("%s: A has to be two-dimensional", who);
         return -1;
     }
     const int *shape = tensor_shape(A);
     if (!shape) {
-        LOG_ERROR("%s invalid shape", who);
+        LOG_ERROR("%s: A has no shape", who);
         return -1;
     }
     if (shape[0] <= 0 || shape[1] <= 0) {
-        LOG_ERROR("%s invalid shape [%d, %d]", who, shape[0], shape[1]);
+        LOG_ERROR("%s: A has a non-positive dimension (%d x %d)", who, shape[0], shape[1]);
         return -1;
     }
     if (!gemv_dtype(tensor_dtype(A))) {
-        LOG_ERROR("%s unsupported dtype %d", who, (int)tensor_dtype(A));
+        LOG_ERROR("%s: no product for dtype %d", who, (int)tensor_dtype(A));
         return -1;
     }
     return 0;
@@ -155,7 +155,7 @@ extern "C" SAPPHIRE_API int kernel_gemv(kernel_context_t *ctx, float *y, const t
     if (check_gemv_args("kernel_gemv", y, A, x)) return -1;
     if (!ctx) {
         if (quantized(tensor_dtype(A))) {
-            LOG_ERROR("kernel_gemv requires non-NULL context for quantized weights");
+            LOG_ERROR("kernel_gemv: a quantized weight needs a context (got NULL)");
             return -1;
         }
         ctx = default_context();
@@ -170,11 +170,11 @@ extern "C" SAPPHIRE_API int kernel_gemv(kernel_context_t *ctx, float *y, const t
 extern "C" SAPPHIRE_API int kernel_gemm(kernel_context_t *ctx, float *Y, const tensor_t *A, const float *X,
                                         int batch_size, int out_stride) {
     if (!Y || !A || !X || batch_size <= 0) {
-        LOG_ERROR("kernel_gemm invalid arguments");
+        LOG_ERROR("kernel_gemm: NULL buffer or batch_size <= 0");
         return -1;
     }
     if (!ctx) {
-        LOG_ERROR("kernel_gemm requires non-NULL context");
+        LOG_ERROR("kernel_gemm: a context is required (got NULL)");
         return -1;
     }
     if (check_gemv_args("kernel_gemm", Y, A, X)) return -1;
@@ -185,28 +185,28 @@ extern "C" SAPPHIRE_API int kernel_gemm(kernel_context_t *ctx, float *Y, const t
 extern "C" SAPPHIRE_API int kernel_gemv_tensor(kernel_context_t *ctx, const tensor_t *y, const tensor_t *A,
                                                const tensor_t *x) {
     if (!y || !A || !x) {
-        LOG_ERROR("kernel_gemv_tensor null pointer");
+        LOG_ERROR("kernel_gemv_tensor: NULL tensor argument");
         return -1;
     }
     if (tensor_ndim(y) != 1 || tensor_dtype(y) != DTYPE_F32) {
-        LOG_ERROR("kernel_gemv_tensor output must be 1D F32 tensor");
+        LOG_ERROR("kernel_gemv_tensor: y has to be a one-dimensional F32 tensor");
         return -1;
     }
     if (tensor_ndim(x) != 1 || tensor_dtype(x) != DTYPE_F32) {
-        LOG_ERROR("kernel_gemv_tensor input must be 1D F32 tensor");
+        LOG_ERROR("kernel_gemv_tensor: x has to be a one-dimensional F32 tensor");
         return -1;
     }
     const int *sa = tensor_shape(A), *sx = tensor_shape(x), *sy = tensor_shape(y);
     if (!sa || !sx || !sy) {
-        LOG_ERROR("kernel_gemv_tensor shapes invalid");
+        LOG_ERROR("kernel_gemv_tensor: a tensor has no shape");
         return -1;
     }
     if (sa[1] != sx[0]) {
-        LOG_ERROR("kernel_gemv_tensor shape mismatch: A[*,%d] vs x[%d]", sa[1], sx[0]);
+        LOG_ERROR("kernel_gemv_tensor: A has %d columns but x has %d elements", sa[1], sx[0]);
         return -1;
     }
     if (sy[0] != sa[0]) {
-        LOG_ERROR("kernel_gemv_tensor output size mismatch: y[%d] vs A[%d,*]", sy[0], sa[0]);
+        LOG_ERROR("kernel_gemv_tensor: y has %d elements but A has %d rows", sy[0], sa[0]);
         return -1;
     }
     return kernel_gemv(ctx, tensor_data_f32(y), A, (const float *)tensor_data(x));
@@ -215,11 +215,11 @@ extern "C" SAPPHIRE_API int kernel_gemv_tensor(kernel_context_t *ctx, const tens
 extern "C" SAPPHIRE_API int kernel_gemv_add(kernel_context_t *ctx, float *y, const tensor_t *A, const float *x,
                                             float alpha) {
     if (!y || !A || !x) {
-        LOG_ERROR("kernel_gemv_add null pointer");
+        LOG_ERROR("kernel_gemv_add: NULL buffer or tensor");
         return -1;
     }
     if (tensor_ndim(A) != 2) {
-        LOG_ERROR("kernel_gemv_add weight must be 2D");
+        LOG_ERROR("kernel_gemv_add: A has to be two-dimensional");
         return -1;
     }
     if (check_gemv_args("kernel_gemv_add", y, A, x)) return -1;
@@ -264,11 +264,11 @@ extern "C" SAPPHIRE_API int kernel_gemv_add(kernel_context_t *ctx, float *y, con
 extern "C" SAPPHIRE_API int kernel_gemv_batch(kernel_context_t *ctx, float *Y, const tensor_t *A, const float *X,
                                               int batch_size) {
     if (!Y || !A || !X || batch_size <= 0) {
-        LOG_ERROR("kernel_gemv_batch invalid arguments");
+        LOG_ERROR("kernel_gemv_batch: NULL buffer or batch size <= 0");
         return -1;
     }
     if (tensor_ndim(A) != 2) {
-        LOG_ERROR("kernel_gemv_batch weight must be 2D");
+        LOG_ERROR("kernel_gemv_batch: A has to be two-dimensional");
         return -1;
     }
     if (batch_size > 1 && ctx) {

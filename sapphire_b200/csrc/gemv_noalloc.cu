@@ -10,11 +10,16 @@
 // (kernel_tensor_upload at model load) and afterwards multiplies with this
 // entry point, which allocates nothing.
 //
-// The scratch (split-tile partial sums, per-tile arrival counters and an
-// error word) lives in g_noalloc_scratch below, kNoallocScratchBytes (4 MiB)
-// per GPU, held by every GPU that loads this library until the process exits.
-// Host code cannot use the array's name as a device address; the device
-// address is fetched once per device with cudaGetSymbolAddress.
+// The scratch (split-tile partial sums and per-tile arrival counters) lives
+// in g_noalloc_scratch below, kNoallocScratchBytes (4 MiB) per GPU, held by
+// every GPU that loads this library until the process exits.  Host code
+// cannot use the array's name as a device address; the device address is
+// fetched once per device with cudaGetSymbolAddress.
+//
+// Errors: the kernel reports an expired bounded wait in the context's error
+// word, a 4-byte mapped host word created by kernel_ctx_init (not here), so
+// such an error surfaces as -1 from the next kernel_ctx_synchronize (or the
+// next synchronous call) on the context.
 #include "internal.cuh"
 
 namespace {
@@ -72,7 +77,7 @@ extern "C" SAPPHIRE_API int kernel_gemv_device_noalloc(kernel_context_t *ctx, fl
         return -1;
     }
     const DevWeight &w = it->second;
-    if (!pipe_supported(w)) {
+    if (!pipe_supported(ctx, w)) {
         ctx_fail(ctx, "kernel_gemv_device_noalloc", "dtype %s / %d columns not supported by the pipelined kernel",
                  dtype_name(w.dtype), w.cols);
         return -1;
@@ -86,11 +91,15 @@ extern "C" SAPPHIRE_API int kernel_gemv_device_noalloc(kernel_context_t *ctx, fl
         ctx_fail(ctx, "kernel_gemv_device_noalloc", "x and y must be device memory of the context's GPU");
         rc = -1;
     }
-    // Scratch layout: [error word | pad to 256 B | counters (ntiles ints) |
-    // pad to 256 B | partial sums (ntiles * kmax * 32 floats)].
+    if (rc == 0 && !ctx->d_err) {
+        ctx_fail(ctx, "kernel_gemv_device_noalloc", "context has no error word (kernel_ctx_init creates it)");
+        rc = -1;
+    }
+    // Scratch layout: [counters (ntiles ints) | pad to 256 B | partial sums
+    // (ntiles * kmax * 32 floats)].
     size_t part_floats = 0, cnt_ints = 0;
     if (rc == 0) pipe_scratch_size(ctx, w, &part_floats, &cnt_ints);
-    const size_t cnt_off = 256;
+    const size_t cnt_off = 0;
     const size_t part_off = cnt_off + ((cnt_ints * sizeof(int) + 255) & ~(size_t)255);
     const size_t need = part_off + part_floats * sizeof(float);
     if (rc == 0 && need > kNoallocScratchBytes) {
@@ -105,8 +114,8 @@ extern "C" SAPPHIRE_API int kernel_gemv_device_noalloc(kernel_context_t *ctx, fl
         if (!base) rc = -1;
     }
     if (rc == 0) {
-        // The array keeps the last call's contents: the error word and the
-        // arrival counters must start at zero.
+        // The array keeps the last call's contents: the arrival counters
+        // must start at zero.
         cudaError_t e = cudaMemsetAsync(base, 0, part_off, ctx->stream);
         if (e != cudaSuccess) {
             ctx_fail(ctx, "kernel_gemv_device_noalloc", "clearing scratch failed: %s", cudaGetErrorString(e));
@@ -115,7 +124,7 @@ extern "C" SAPPHIRE_API int kernel_gemv_device_noalloc(kernel_context_t *ctx, fl
     }
     if (rc == 0)
         rc = launch_gemv_pipe(ctx, w, x, y, reinterpret_cast<float *>(base + part_off),
-                              reinterpret_cast<int *>(base + cnt_off), reinterpret_cast<int *>(base), ctx->stream);
+                              reinterpret_cast<int *>(base + cnt_off), ctx->d_err, ctx->stream);
     if (prev >= 0 && prev != ctx->device) cudaSetDevice(prev);
     return rc;
 }

@@ -160,8 +160,16 @@ namespace {
 constexpr unsigned long long kPeerWaitNs = 2000000000ull;
 constexpr int kPullThreads = 256;
 
+// Waits are bounded by time (wait_ns per word, restarted while words keep
+// arriving); the first expiry in a block sets bit 3 of *err and a block-wide
+// flag, after which the block's threads stop waiting and store NaN for every
+// word that is still stale.
 __global__ void __launch_bounds__(kPullThreads) ll_pull_kernel(const unsigned long long *ll, long long rows,
-                                                               unsigned epoch, float *y, int *err) {
+                                                               unsigned epoch, float *y, int *err,
+                                                               unsigned long long wait_ns) {
+    __shared__ int s_expired;
+    if (threadIdx.x == 0) s_expired = 0;
+    __syncthreads();
     pdl_trigger();
     pdl_wait();
     const long long stride = (long long)gridDim.x * blockDim.x;
@@ -172,13 +180,18 @@ __global__ void __launch_bounds__(kPullThreads) ll_pull_kernel(const unsigned lo
             uint64_t t0;
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
             for (;;) {
+                if (*reinterpret_cast<volatile int *>(&s_expired)) {
+                    w = 0x7FC00000ull;   // NaN
+                    break;
+                }
                 __nanosleep(64);
                 asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(ll + i) : "memory");
                 if ((unsigned)(w >> 32) == epoch) break;
                 uint64_t t;
                 asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-                if (t - t0 > kPeerWaitNs) {
+                if (t - t0 > wait_ns) {
                     atomicOr(err, 8);
+                    s_expired = 1;
                     w = 0x7FC00000ull;   // NaN
                     break;
                 }
@@ -249,7 +262,7 @@ bool shard_peer_product(kernel_context_t *ctx, const DevWeight &w, const float *
     *rc = 0;
     // The decision depends only on arguments every rank shares (the pipelined
     // kernel is used on every rank, whatever its local row count).
-    if (ctx->world > kMaxPeers || (size_t)per * ctx->world > ((size_t)4 << 20) || !pipe_supported(w)) return false;
+    if (ctx->world > kMaxPeers || (size_t)per * ctx->world > ((size_t)4 << 20) || !pipe_supported(ctx, w)) return false;
     if (!ctx->pg) peer_gather_setup(ctx);
     PeerGather &g = *ctx->pg;
     if (!g.ready || (size_t)per * ctx->world > g.cap_rows) return false;
@@ -272,7 +285,8 @@ bool shard_peer_product(kernel_context_t *ctx, const DevWeight &w, const float *
     }
     const int grid = (int)std::max<long long>(1, std::min<long long>(4 * 148, ((long long)rows + kPullThreads - 1) / kPullThreads));
     cudaError_t e = launch_pdl(ll_pull_kernel, dim3(grid), dim3(kPullThreads), 0, st,
-                               (const unsigned long long *)(g.local + buf), (long long)rows, epoch, yd, ctx->d_err);
+                               (const unsigned long long *)(g.local + buf), (long long)rows, epoch, yd, ctx->d_err,
+                               kPeerWaitNs);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         ctx_fail(ctx, "kernel_gemv", "gather launch failed: %s", cudaGetErrorString(e));
@@ -305,4 +319,37 @@ void shard_destroy(kernel_context_t *ctx) {
     }
     ctx->rank = 0;
     ctx->world = 1;
+}
+
+// Test-only: runs the peer-gather pull on a local buffer of `rows` words that
+// no rank writes (epoch 0, the pull waits for epoch 1), with a wait limit of
+// wait_ns, on the context's GPU.  The bounded wait runs out: y (device,
+// `rows` floats) receives NaN, bit 3 of the error word is set and the call
+// returns -1 after its synchronisation.  No GPU fault is involved.
+extern "C" SAPPHIRE_API int sapphire_test_pull_expiry(kernel_context_t *ctx, float *y, long long rows,
+                                                      unsigned long long wait_ns) {
+    if (!ctx || !y || rows <= 0) return -1;
+    std::lock_guard<std::recursive_mutex> lk(ctx->exec_mutex);
+    if (!ctx->initialized || ensure_err_word(ctx)) return -1;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(ctx->device);
+    unsigned long long *buf = nullptr;
+    int rc = -1;
+    if (cudaMalloc(&buf, (size_t)rows * sizeof(unsigned long long)) == cudaSuccess &&
+        cudaMemsetAsync(buf, 0, (size_t)rows * sizeof(unsigned long long), ctx->stream) == cudaSuccess) {
+        const int grid = (int)std::max<long long>(1, std::min<long long>(4 * 148, (rows + kPullThreads - 1) / kPullThreads));
+        cudaError_t e = launch_pdl(ll_pull_kernel, dim3(grid), dim3(kPullThreads), 0, ctx->stream,
+                                   (const unsigned long long *)buf, rows, 1u, y, ctx->d_err, wait_ns);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) {
+            ctx_fail(ctx, "sapphire_test_pull_expiry", "%s", cudaGetErrorString(e));
+        } else {
+            rc = check_kernel_error(ctx, "sapphire_test_pull_expiry");
+        }
+    }
+    if (buf) cudaFree(buf);
+    cudaGetLastError();
+    if (prev >= 0) cudaSetDevice(prev);
+    return rc;
 }
