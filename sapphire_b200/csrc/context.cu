@@ -298,6 +298,10 @@ int ensure_scratch(kernel_context_t *ctx, float **buf, size_t *cap, size_t bytes
     }
     CUDA_TRY(ctx, cudaMalloc((void **)buf, want));
     *cap = want;
+    // New scratch starts zeroed: the split-tile partial words of the
+    // streaming GEMV are valid only when tagged with the current launch's
+    // epoch, and zero is never an epoch.
+    CUDA_TRY(ctx, cudaMemsetAsync(*buf, 0, want, ctx->stream));
     return 0;
 }
 

@@ -6,10 +6,11 @@
 // ternary format.
 //
 // Work split.  A "unit" is 32 rows x 64 columns (two 32-column blocks) of a
-// 32-row tile; an item is up to UPI consecutive units of one tile (a K
-// segment).  Items are numbered tile-major and every consumer warp of the
-// persistent grid (one CTA per SM) takes a contiguous, equal-size range of
-// them, so every SM streams the same number of bytes whatever the shape.
+// 32-row tile.  Units are numbered tile-major and every consumer warp of the
+// persistent grid (one CTA per SM) takes a contiguous range of them whose
+// length differs from the others' by at most one unit, so every SM streams
+// the same number of bytes whatever the shape.  A warp walks its range in
+// items of up to UPI units, cut at tile boundaries and at the range's end.
 //
 // Memory pipeline.  Warp NC of each CTA is the producer: its lane c streams
 // consumer c's items into that consumer's ring of NS shared-memory slots with
@@ -35,11 +36,15 @@
 //     planes accumulate exactly in int32 across all of K, are joined by exact
 //     shifts at the end of a tile, and sum_j X_j is subtracted once per row.
 //
-// Split tiles.  A tile whose items span several warps is finished by the last
-// contributor: each stores its per-row partial (fp32, or the exact int64 sum
-// for ternary) in the slot of its rank among the tile's contributors, fences,
-// and bumps the tile's counter; the one that completes the count sums the
-// slots in slot order (deterministic), writes y and resets the counter.
+// Split tiles.  A tile whose items span several warps is finished by the
+// warp that owns its first segment - for that warp it is the last tile of its
+// range, while the other owners meet it first, so their parts are long done
+// when it gets there.  The others store their per-row partials (fp32, or the
+// exact int64 sum for ternary) as 8-byte words tagged with the launch's epoch
+// in the slot of their rank among the tile's owners; the finisher waits
+// (bounded) for each word to carry the epoch and sums in slot order
+// (deterministic).  An aligned 8-byte store arrives whole, so the tag marks
+// the value valid: no fence, atomic or counter is needed.
 //
 // Waits are bounded.  A consumer whose slot does not fill sets bit 0 of *err
 // and its abort flag, and leaves the loop; the producer lane serving it stops
@@ -73,6 +78,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
     uint32_t ok;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(saddr(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
         : "=r"(ok)
         : "r"(saddr(bar)), "r"(phase)
         : "memory");
@@ -141,11 +155,13 @@ struct StreamParams {
     const float *scales;
     const float *x;
     float *y;
-    void *part;                 // [ntiles][kmax][32] partials of split tiles (fp32; int64 for TQ2_0)
-    int *cnt;                   // [ntiles] arrival counters, zero between launches
+    unsigned long long *part;   // [ntiles][kmax][32][words] epoch-tagged partials of split tiles
+                                // (one word of fp32 bits; two of int64 halves for TQ2_0)
     int *err;                   // error word (bit 0: a bounded wait expired)
-    long long total_items;
-    int nrows, cols, nb, nunits, ntiles, nseg, kmax, total_warps;
+    unsigned epoch;             // tag of this launch's partial words (never 0)
+    long long total_units;      // ntiles * nunits
+    int nrows, cols, nb, nunits, ntiles, kmax, total_warps;
+    int early;                  // items per consumer the producer issues before the x loads are out
     unsigned wait_limit;        // test hook: polls before the unarmed consumer's first wait gives up
     int test_unarmed;           // test hook: consumer 0 of CTA 0 gets no copy for its first item
     // Row-sharded products gathered over peer memory: when ll_n > 0 row r is
@@ -168,11 +184,39 @@ __device__ __forceinline__ void store_y(const StreamParams &p, size_t r, float v
     }
 }
 
-__device__ __forceinline__ long long range_begin(long long w, long long T, long long W) { return (w * T) / W; }
-__device__ __forceinline__ int item_owner(long long i, long long T, long long W) {
-    long long w = ((i + 1) * W + T - 1) / T - 1;
+// Warp w of W owns units [w*U/W, (w+1)*U/W); unit_owner(i) is the warp whose
+// range holds unit i.
+__device__ __forceinline__ long long range_begin(long long w, long long U, long long W) { return (w * U) / W; }
+__device__ __forceinline__ int unit_owner(long long i, long long U, long long W) {
+    long long w = ((i + 1) * W + U - 1) / U - 1;
     return (int)(w < W - 1 ? w : W - 1);
 }
+
+// Walks a warp's unit range item by item (producer lanes and consumers walk
+// the same sequence).
+struct Cursor {
+    long long u, ub;      // next unit, end of the range
+    int tile, pu;         // tile of unit u and its position in the tile
+    __device__ __forceinline__ void start(long long ua, long long ub_, int nunits) {
+        u = ua;
+        ub = ub_;
+        tile = (int)(ua / nunits);
+        pu = (int)(ua - (long long)tile * nunits);
+    }
+    __device__ __forceinline__ bool more() const { return u < ub; }
+    // Units in the next item (at most upi, not past the tile or the range).
+    __device__ __forceinline__ int count(int upi, int nunits) const {
+        return (int)min((long long)min(upi, nunits - pu), ub - u);
+    }
+    __device__ __forceinline__ void advance(int nu, int nunits) {
+        u += nu;
+        pu += nu;
+        if (pu == nunits) {
+            pu = 0;
+            ++tile;
+        }
+    }
+};
 
 // Named barrier over the NC consumer warps (the producer warp never joins).
 __device__ __forceinline__ void consumers_sync(int nthreads) {
@@ -227,93 +271,118 @@ __device__ __forceinline__ int digit_byte(int p) {
     return ((p & 15) >> 2) * 8 + (p >> 4) * 4 + (p & 3);
 }
 
-constexpr int kXRegBlocks = 16;   // blocks per consumer warp held in registers between the two passes
+// Loads of x in flight per consumer thread in the staging pass.
+constexpr int kXLoads = 16;
 
+// Builds the x image.  Pass 1 stages x as fp32 in the image region itself
+// (block b's 128 bytes hold x[32b .. 32b+32) as floats; columns past `cols`
+// are zero) with every load of a thread issued at once, and reduces max|x|.
+// Pass 2 converts block b in place: the warp that owns it reads the block's
+// 32 floats, then overwrites the same 128 bytes with the digit rows.
 template <tensor_dtype_t DT, int NC>
 __device__ void prepare_x(const StreamParams &p, const XImage &xi) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __shared__ float s_max[kMaxConsumers];
+    constexpr int kThreads = NC * 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    __shared__ unsigned s_max[kMaxConsumers];
     __shared__ long long s_sx[kMaxConsumers];
     const int nbp = nb_even(p.nb);
-    // Pass 1: max |x| (and non-finite values) over all of x.
-    float v[kXRegBlocks];
-    float m = 0.0f;
+    float *stage = reinterpret_cast<float *>(xi.img);
+    // Pass 1.  The bits of a non-negative float order like the float, so an
+    // unsigned maximum gives max|x| (NaN bits sort above every finite value).
+    unsigned m = 0;
     bool bad = false;
-#pragma unroll
-    for (int k = 0; k < kXRegBlocks; ++k) {
-        const int c = (warp + NC * k) * 32 + lane;
-        v[k] = c < p.cols ? __ldg(p.x + c) : 0.0f;
-    }
-#pragma unroll
-    for (int k = 0; k < kXRegBlocks; ++k) {
-        bad |= !isfinite(v[k]);
-        m = fmaxf(m, fabsf(v[k]));
-    }
-    for (int b = warp + NC * kXRegBlocks; b < p.nb; b += NC) {
-        const int c = b * 32 + lane;
-        const float t = c < p.cols ? __ldg(p.x + c) : 0.0f;
+    auto take = [&](float t) {
         bad |= !isfinite(t);
-        m = fmaxf(m, fabsf(t));
-    }
-    if (bad) *xi.nonfinite = 1;
+        m = max(m, __float_as_uint(fabsf(t)));
+    };
+    // Every thread issues a first batch of loads, then all consumer threads
+    // arrive on barrier 2 together (the x loads are out: the producer may
+    // issue the rest of the rings); later batches, for long rows, follow.
+    if (((uintptr_t)p.x & 15) == 0 && (p.cols & 3) == 0) {
+        const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+        const int n4 = p.cols >> 2;
+        for (int i0 = tid, first = 1; first || i0 < n4; i0 += kXLoads * kThreads, first = 0) {
+            float4 t[kXLoads];
 #pragma unroll
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            for (int q = 0; q < kXLoads; ++q) {
+                const int i = i0 + q * kThreads;
+                t[q] = i < n4 ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (first) asm volatile("bar.arrive 2, %0;" ::"r"(kThreads + 32) : "memory");
+#pragma unroll
+            for (int q = 0; q < kXLoads; ++q) {
+                const int i = i0 + q * kThreads;
+                if (i < n4) {
+                    reinterpret_cast<float4 *>(stage)[i] = t[q];
+                    take(t[q].x);
+                    take(t[q].y);
+                    take(t[q].z);
+                    take(t[q].w);
+                }
+            }
+        }
+    } else {
+        for (int i0 = tid, first = 1; first || i0 < p.cols; i0 += kXLoads * kThreads, first = 0) {
+            float t[kXLoads];
+#pragma unroll
+            for (int q = 0; q < kXLoads; ++q) {
+                const int i = i0 + q * kThreads;
+                t[q] = i < p.cols ? __ldg(p.x + i) : 0.0f;
+            }
+            if (first) asm volatile("bar.arrive 2, %0;" ::"r"(kThreads + 32) : "memory");
+#pragma unroll
+            for (int q = 0; q < kXLoads; ++q) {
+                const int i = i0 + q * kThreads;
+                if (i < p.cols) {
+                    stage[i] = t[q];
+                    take(t[q]);
+                }
+            }
+        }
+    }
+    for (int i = p.cols + tid; i < nbp * 32; i += kThreads) stage[i] = 0.0f;
+    if (bad) *xi.nonfinite = 1;
+    m = __reduce_max_sync(0xffffffffu, m);
     if (lane == 0) s_max[warp] = m;
-    consumers_sync(NC * 32);
-    m = 0.0f;
-    for (int i = 0; i < NC; ++i) m = fmaxf(m, s_max[i]);
-    const int e = x_exponent(isfinite(m) ? m : FLT_MAX);
+    consumers_sync(kThreads);
+    m = 0;
+    for (int i = 0; i < NC; ++i) m = max(m, s_max[i]);
+    const float mf = __uint_as_float(m);
+    const int e = x_exponent(isfinite(mf) ? mf : FLT_MAX);
     if (threadIdx.x == 0) *xi.pexp = (e >= -126 && e <= 127) ? __int_as_float((127 - e) << 23) : ldexpf(1.0f, -e);
     // x * 2^e as two exact multiplies by normal powers of two (e <= 170).
     const int e1 = min(max(e, -126), 127);
     const float f1 = __int_as_float((e1 + 127) << 23), f2 = __int_as_float((e - e1 + 127) << 23);
-    // Pass 2: digits of every block (blocks b = warp + NC*k), the zero rows,
+    // Pass 2: digits of blocks b = warp + NC*k (the padding block of an
+    // odd-block row is staged as zeros, so its digits and correction are 0),
     // the Q4_0 corrections and the ternary x sum.
     long long sx = 0;
     const int off = digit_byte<DT>(lane);
-    auto convert = [&](int b, float t) {
+#pragma unroll 2
+    for (int b = warp; b < nbp; b += NC) {
+        uint8_t *blk = xi.img + (size_t)b * kImgBlock;
+        const float t = stage[b * 32 + lane];
+        __syncwarp();
         const int X = isfinite(t) ? __float2int_rn(t * f1 * f2) : 0;
-        sx += X;
         const int d0 = ((X & 0xFF) ^ 0x80) - 0x80;
         const int X1 = (X - d0) >> 8;
         const int d1 = ((X1 & 0xFF) ^ 0x80) - 0x80;
         const int d2 = (X1 - d1) >> 8;
-        uint8_t *blk = xi.img + (size_t)b * kImgBlock;
         blk[off] = (uint8_t)d0;
         blk[32 + off] = (uint8_t)d1;
         blk[64 + off] = (uint8_t)d2;
         blk[96 + lane] = 0;
         if (DT == DTYPE_Q4_0) {
-            int s0 = d0, s1 = d1, s2 = d2;
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-                s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-                s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-            }
+            const int s0 = __reduce_add_sync(0xffffffffu, d0);
+            const int s1 = __reduce_add_sync(0xffffffffu, d1);
+            const int s2 = __reduce_add_sync(0xffffffffu, d2);
             if (lane < 4) xi.corr[b * 4 + lane] = lane == 0 ? -8 * s0 : lane == 1 ? -8 * s1 : lane == 2 ? -8 * s2 : 0;
         }
-    };
-#pragma unroll
-    for (int k = 0; k < kXRegBlocks; ++k) {
-        const int b = warp + NC * k;
-        if (b < p.nb) convert(b, v[k]);
-    }
-    for (int b = warp + NC * kXRegBlocks; b < p.nb; b += NC) {
-        const int c = b * 32 + lane;
-        convert(b, c < p.cols ? __ldg(p.x + c) : 0.0f);
-    }
-    if (nbp > p.nb && warp == NC - 1) {
-        // The padding block of an odd-block row: all digit rows zero.
-        uint32_t *blk = reinterpret_cast<uint32_t *>(xi.img + (size_t)p.nb * kImgBlock);
-        blk[lane] = 0;
-        if (DT == DTYPE_Q4_0 && lane < 4) xi.corr[p.nb * 4 + lane] = 0;
+        if (DT == DTYPE_TQ2_0) sx += __reduce_add_sync(0xffffffffu, X);   // |X| < 2^22: a block sum fits int32
     }
     if (DT == DTYPE_TQ2_0) {
-#pragma unroll
-        for (int o = 16; o; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
         if (lane == 0) s_sx[warp] = sx;
-        consumers_sync(NC * 32);
+        consumers_sync(kThreads);
         if (threadIdx.x == 0) {
             long long t = 0;
             for (int i = 0; i < NC; ++i) t += s_sx[i];
@@ -331,11 +400,12 @@ template <int UPI>
 struct Item<DTYPE_Q8_0, UPI> {
     uint4 a[UPI][2][2];   // [unit][block of the unit][16-row half]: the A fragment
     float4 s[UPI];        // scales of rows g, g+8, g+16, g+24 of block 2p + tig/2
+    template <bool FULL>
     __device__ __forceinline__ void load(const uint8_t *st, int nu, int lane, bool last_half) {
         const int g = lane >> 2, tig = lane & 3;
 #pragma unroll
         for (int u = 0; u < UPI; ++u) {
-            if (u < nu) {
+            if (FULL || u < nu) {
 #pragma unroll
                 for (int k = 0; k < 2; ++k)
 #pragma unroll
@@ -353,11 +423,12 @@ template <int UPI>
 struct Item<DTYPE_Q4_0, UPI> {
     uint4 a[UPI][2];      // [unit][block]: code word tig of rows g, g+8, g+16, g+24
     float4 s[UPI];
+    template <bool FULL>
     __device__ __forceinline__ void load(const uint8_t *st, int nu, int lane, bool last_half) {
         const int g = lane >> 2, tig = lane & 3;
 #pragma unroll
         for (int u = 0; u < UPI; ++u) {
-            if (u < nu) {
+            if (FULL || u < nu) {
 #pragma unroll
                 for (int k = 0; k < 2; ++k) a[u][k] = lds<uint4>(st + (2 * u + k) * 512 + lane * 16);
                 const float4 t = lds<float4>(st + UPI * 1024 + u * 256 + (tig >> 1) * 128 + g * 16);
@@ -370,24 +441,28 @@ struct Item<DTYPE_Q4_0, UPI> {
 template <int UPI>
 struct Item<DTYPE_TQ2_0, UPI> {
     uint4 a[UPI];         // four words: 2-bit planes of four A fragments
+    template <bool FULL>
     __device__ __forceinline__ void load(const uint8_t *st, int nu, int lane, bool) {
 #pragma unroll
         for (int u = 0; u < UPI; ++u)
-            if (u < nu) a[u] = lds<uint4>(st + u * 512 + lane * 16);
+            if (FULL || u < nu) a[u] = lds<uint4>(st + u * 512 + lane * 16);
     }
 };
 
 // Accumulators of one 32-row tile for a lane (g = lane/4, tig = lane%4).
 struct Acc {
     float f[2][2];        // Q8_0 / Q4_0: [half][row g / g+8] scaled sums (digit columns of this lane)
-    int d[4][4];          // TQ2_0: [plane][C register] exact sums
+    int d[2][4][4];       // TQ2_0: [set: unit parity][plane][C register] exact sums (two independent
+                          // MMA chains)
     __device__ __forceinline__ void reset() {
 #pragma unroll
         for (int h = 0; h < 2; ++h) f[h][0] = f[h][1] = 0.0f;
 #pragma unroll
-        for (int m = 0; m < 4; ++m)
+        for (int q = 0; q < 2; ++q)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) d[m][i] = 0;
+            for (int m = 0; m < 4; ++m)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) d[q][m][i] = 0;
     }
 };
 
@@ -419,13 +494,13 @@ __device__ __forceinline__ void scale2(float (&acc)[2], const int (&D)[4], float
     acc[1] = fmaf(s1, (float)(D[2] + 256 * D[3]), acc[1]);
 }
 
-template <int UPI>
+template <bool FULL, int UPI>
 __device__ __forceinline__ void compute(const Item<DTYPE_Q8_0, UPI> &R, int nu, int p0, const XImage &xi,
                                         LaneOff lo, int, Acc &acc) {
     const int zero[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int u = 0; u < UPI; ++u) {
-        if (u < nu) {
+        if (FULL || u < nu) {
             const uint8_t *bi = xi.img + (size_t)(p0 + u) * (2 * kImgBlock);
             const uint2 B0 = lds<uint2>(bi + lo.b0), B1 = lds<uint2>(bi + lo.b1);
 #pragma unroll
@@ -439,12 +514,12 @@ __device__ __forceinline__ void compute(const Item<DTYPE_Q8_0, UPI> &R, int nu, 
     }
 }
 
-template <int UPI>
+template <bool FULL, int UPI>
 __device__ __forceinline__ void compute(const Item<DTYPE_Q4_0, UPI> &R, int nu, int p0, const XImage &xi,
                                         LaneOff lo, int tig, Acc &acc) {
 #pragma unroll
     for (int u = 0; u < UPI; ++u) {
-        if (u < nu) {
+        if (FULL || u < nu) {
             const uint8_t *bi = xi.img + (size_t)(p0 + u) * (2 * kImgBlock);
             const uint2 B0 = lds<uint2>(bi + lo.b0), B1 = lds<uint2>(bi + lo.b1);
             const int2 C = *reinterpret_cast<const int2 *>(xi.corr + (size_t)(p0 + u) * 8 + tig * 2);
@@ -472,25 +547,23 @@ __device__ __forceinline__ void compute(const Item<DTYPE_Q4_0, UPI> &R, int nu, 
     }
 }
 
-template <int UPI>
+template <bool FULL, int UPI>
 __device__ __forceinline__ void compute(const Item<DTYPE_TQ2_0, UPI> &R, int nu, int p0, const XImage &xi,
                                         LaneOff lo, int, Acc &acc) {
 #pragma unroll
     for (int u = 0; u < UPI; ++u) {
-        if (u < nu) {
+        if (FULL || u < nu) {
             const uint8_t *bi = xi.img + (size_t)(p0 + u) * (2 * kImgBlock);
             const uint2 B0 = lds<uint2>(bi + lo.b0), B1 = lds<uint2>(bi + lo.b1);
             const uint4 W = R.a[u];
             // Plane m (bits 2m, 2m+1 of every byte) is the fragment of half
-            // m & 1 and block 2p + (m >> 1), scaled by 4^m.
-            mma_u8(acc.d[0], W.x & 0x03030303u, W.y & 0x03030303u, W.z & 0x03030303u, W.w & 0x03030303u, B0,
-                   acc.d[0]);
-            mma_u8(acc.d[1], W.x & 0x0C0C0C0Cu, W.y & 0x0C0C0C0Cu, W.z & 0x0C0C0C0Cu, W.w & 0x0C0C0C0Cu, B0,
-                   acc.d[1]);
-            mma_u8(acc.d[2], W.x & 0x30303030u, W.y & 0x30303030u, W.z & 0x30303030u, W.w & 0x30303030u, B1,
-                   acc.d[2]);
-            mma_u8(acc.d[3], W.x & 0xC0C0C0C0u, W.y & 0xC0C0C0C0u, W.z & 0xC0C0C0C0u, W.w & 0xC0C0C0C0u, B1,
-                   acc.d[3]);
+            // m & 1 and block 2p + (m >> 1), scaled by 4^m.  Even and odd
+            // units accumulate into separate sets (independent MMA chains).
+            int(&a)[4][4] = acc.d[u & 1];
+            mma_u8(a[0], W.x & 0x03030303u, W.y & 0x03030303u, W.z & 0x03030303u, W.w & 0x03030303u, B0, a[0]);
+            mma_u8(a[1], W.x & 0x0C0C0C0Cu, W.y & 0x0C0C0C0Cu, W.z & 0x0C0C0C0Cu, W.w & 0x0C0C0C0Cu, B0, a[1]);
+            mma_u8(a[2], W.x & 0x30303030u, W.y & 0x30303030u, W.z & 0x30303030u, W.w & 0x30303030u, B1, a[2]);
+            mma_u8(a[3], W.x & 0xC0C0C0C0u, W.y & 0xC0C0C0C0u, W.z & 0xC0C0C0C0u, W.w & 0xC0C0C0C0u, B1, a[3]);
         }
     }
 }
@@ -505,8 +578,10 @@ __device__ __forceinline__ void tile_rows(const Acc &acc, unsigned long long (&v
         for (int h = 0; h < 2; ++h) {
             int D[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                D[i] = h == 0 ? acc.d[0][i] + (acc.d[2][i] >> 4) : (acc.d[1][i] >> 2) + (acc.d[3][i] >> 6);
+            for (int i = 0; i < 4; ++i) {
+                const int p0 = acc.d[0][h][i] + acc.d[1][h][i], p2 = acc.d[0][h + 2][i] + acc.d[1][h + 2][i];
+                D[i] = h == 0 ? p0 + (p2 >> 4) : (p0 >> 2) + (p2 >> 6);
+            }
             const int up0 = __shfl_down_sync(0xffffffffu, D[0], 1);
             const int up2 = __shfl_down_sync(0xffffffffu, D[2], 1);
             v[2 * h] = (unsigned long long)((long long)D[0] + 256LL * D[1] + 65536LL * up0);
@@ -537,35 +612,55 @@ __device__ __forceinline__ float finish_row(const XImage &xi, unsigned long long
     return nonfinite ? __int_as_float(0x7FC00000) : out;
 }
 
-// Stores a finished tile (one row per lane), or its partial for a tile
-// shared with other warps.
+// Epoch-tagged 8-byte words of the split-tile partials: (epoch << 32) | bits.
+__device__ __forceinline__ void put_word(unsigned long long *p, unsigned epoch, uint32_t bits) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(((unsigned long long)epoch << 32) | bits)
+                 : "memory");
+}
+// Polls a word until it carries `epoch` (bounded); false if the wait ran out.
+__device__ __forceinline__ bool get_word(const unsigned long long *p, unsigned epoch, uint32_t &bits) {
+    for (unsigned i = 0; i < kWaitLimit; ++i) {
+        unsigned long long w;
+        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+        if ((unsigned)(w >> 32) == epoch) {
+            bits = (uint32_t)w;
+            return true;
+        }
+        __nanosleep(64);
+    }
+    return false;
+}
+
+// Stores a finished tile (one row per lane), or its part of a tile shared
+// with other warps (see "Split tiles" above).
 template <tensor_dtype_t DT>
 __device__ void flush_tile(const StreamParams &p, const XImage &xi, int tile, int lane, int my_warp, bool whole,
                            const unsigned long long (&v)[4], bool nonfinite, float rs) {
-    if (whole) {
-        // Lane l takes row l = g + 8i from the lane holding it, (l % 8) * 4.
-        unsigned long long mine = v[0];
+    // Lane l takes row l = g + 8i from the lane holding it, (l % 8) * 4.
+    unsigned long long mine = v[0];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const unsigned long long t = __shfl_sync(0xffffffffu, v[i], (lane & 7) * 4);
-            if ((lane >> 3) == i) mine = t;
-        }
-        if (tile * 32 + lane < p.nrows) store_y(p, (size_t)tile * 32 + lane, finish_row<DT>(xi, mine, nonfinite, rs));
+    for (int i = 0; i < 4; ++i) {
+        const unsigned long long t = __shfl_sync(0xffffffffu, v[i], (lane & 7) * 4);
+        if ((lane >> 3) == i) mine = t;
+    }
+    const bool row_ok = tile * 32 + lane < p.nrows;
+    if (whole) {
+        if (row_ok) store_y(p, (size_t)tile * 32 + lane, finish_row<DT>(xi, mine, nonfinite, rs));
         return;
     }
-    // k = contributors of the tile, slot = this warp's rank among them.
-    const long long first = (long long)tile * p.nseg;
+    // k = owners of the tile's units, slot = this warp's rank among them.
+    const long long first = (long long)tile * p.nunits;
     int k = 0, slot = -1;
-    const int o0 = item_owner(first, p.total_items, p.total_warps);
-    if (p.total_items >= p.total_warps) {
-        // Every warp owns at least one item, so the tile's owners are the
+    const int o0 = unit_owner(first, p.total_units, p.total_warps);
+    if (p.total_units >= p.total_warps) {
+        // Every warp owns at least one unit, so the tile's owners are the
         // consecutive warps o0..o1.
-        k = item_owner(first + p.nseg - 1, p.total_items, p.total_warps) - o0 + 1;
+        k = unit_owner(first + p.nunits - 1, p.total_units, p.total_warps) - o0 + 1;
         slot = my_warp - o0;
     } else {
         int prev = -1;
-        for (int s = 0; s < p.nseg; ++s) {
-            const int o = s == 0 ? o0 : item_owner(first + s, p.total_items, p.total_warps);
+        for (int s = 0; s < p.nunits; ++s) {
+            const int o = s == 0 ? o0 : unit_owner(first + s, p.total_units, p.total_warps);
             if (o != prev) {
                 if (o == my_warp) slot = k;
                 ++k;
@@ -573,39 +668,37 @@ __device__ void flush_tile(const StreamParams &p, const XImage &xi, int tile, in
             }
         }
     }
-    long long *base64 = reinterpret_cast<long long *>(p.part) + (size_t)tile * p.kmax * 32;
-    float *base32 = reinterpret_cast<float *>(p.part) + (size_t)tile * p.kmax * 32;
-    if ((lane & 3) == 0) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = (lane >> 2) + 8 * i;
-            if (DT == DTYPE_TQ2_0) base64[(size_t)slot * 32 + r] = (long long)v[i];
-            else base32[(size_t)slot * 32 + r] = __uint_as_float((uint32_t)v[i]);
-        }
+    constexpr int kWords = DT == DTYPE_TQ2_0 ? 2 : 1;
+    unsigned long long *base = p.part + (size_t)tile * p.kmax * 32 * kWords;
+    if (slot > 0) {
+        unsigned long long *w = base + ((size_t)slot * 32 + lane) * kWords;
+        put_word(w, p.epoch, (uint32_t)mine);
+        if (kWords == 2) put_word(w + 1, p.epoch, (uint32_t)(mine >> 32));
+        return;
     }
-    __threadfence();
-    __syncwarp();
-    int old = 0;
-    if (lane == 0) old = atomicAdd(p.cnt + tile, 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == k - 1) {
-        __threadfence();
-        // The last contributor sums the slots in slot order, one row per lane.
-        const int r = lane;
-        unsigned long long sum;
-        if (DT == DTYPE_TQ2_0) {
-            long long s = 0;
-            for (int j = 0; j < k; ++j) s += __ldcg(base64 + (size_t)j * 32 + r);
-            sum = (unsigned long long)s;
-        } else {
-            float s = 0.0f;
-            for (int j = 0; j < k; ++j) s += __ldcg(base32 + (size_t)j * 32 + r);
-            sum = __float_as_uint(s);
+    // The finisher: sum the parts in slot order.
+    bool ok = true;
+    unsigned long long sum;
+    if (DT == DTYPE_TQ2_0) {
+        long long t = (long long)mine;
+        for (int j = 1; j < k; ++j) {
+            const unsigned long long *w = base + ((size_t)j * 32 + lane) * kWords;
+            uint32_t lo = 0, hi = 0;
+            ok = ok && get_word(w, p.epoch, lo) && get_word(w + 1, p.epoch, hi);
+            t += (long long)(((unsigned long long)hi << 32) | lo);
         }
-        if (tile * 32 + r < p.nrows) store_y(p, (size_t)tile * 32 + r, finish_row<DT>(xi, sum, nonfinite, rs));
-        __syncwarp();
-        if (lane == 0) p.cnt[tile] = 0;
+        sum = (unsigned long long)t;
+    } else {
+        float t = __uint_as_float((uint32_t)mine);
+        for (int j = 1; j < k; ++j) {
+            uint32_t bits = 0;
+            ok = ok && get_word(base + (size_t)j * 32 + lane, p.epoch, bits);
+            t += __uint_as_float(bits);
+        }
+        sum = __float_as_uint(t);
     }
+    if (!ok) atomicOr(p.err, 1);
+    if (row_ok) store_y(p, (size_t)tile * 32 + lane, ok ? finish_row<DT>(xi, sum, nonfinite, rs) : __int_as_float(0x7FC00000));
 }
 
 // --------------------------------------------------------------- kernel ---
@@ -631,7 +724,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_stream(const StreamPara
     xi.pexp = reinterpret_cast<float *>(ximg + tail + 16);
     xi.nonfinite = &s_nonfinite;
 
-    const long long T = p.total_items, W = p.total_warps;
+    const long long U = p.total_units, W = p.total_warps;
     pdl_trigger();
     if (threadIdx.x < NC * NS) {
         mbar_init(&full[0][0] + threadIdx.x, 1);
@@ -646,67 +739,82 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_stream(const StreamPara
 
     if (warp == NC) {
         // ------------------------------------------------------ producer --
-        // Lane c streams consumer c's items; the weight does not depend on
-        // earlier kernels, so it starts before the programmatic-launch wait.
+        // Lane c streams consumer c's items.  The lanes poll their consumers'
+        // "empty" barriers with the non-blocking test_wait in lockstep, so a
+        // lane whose consumer is still computing never holds up the others
+        // (a blocking wait would suspend the whole warp).  The weight does
+        // not depend on earlier kernels, so `early` items per consumer go
+        // out before the programmatic-launch wait; the rest wait until the
+        // consumers have issued their x loads (named barrier 2), which would
+        // otherwise queue behind every ring's copies.
         const int c = lane;
+        Cursor cur;
+        cur.start(0, 0, p.nunits);
         if (c < NC) {
             const int gw = blockIdx.x * NC + c;
-            const long long it0 = range_begin(gw, T, W), it1 = range_begin(gw + 1, T, W);
-            const int n = (int)(it1 - it0);
-            int tile = (int)(it0 / p.nseg), seg = (int)(it0 % p.nseg);
-            uint8_t *ring = rings + (size_t)c * NS * kSlot;
-            int issued = 0;
-            for (int j = 0; j < n; ++j) {
+            cur.start(range_begin(gw, U, W), range_begin(gw + 1, U, W), p.nunits);
+        }
+        uint8_t *ring = rings + (size_t)min(c, NC - 1) * NS * kSlot;
+        int j = 0, issued = 0;
+        unsigned idle = 0;
+        bool live = c < NC && cur.more();
+        bool gate = true;                  // the x-load barrier is still ahead
+        const int early = min(p.early, NS);
+        for (;;) {
+            if (gate && !__any_sync(0xffffffffu, live && j < early)) {
+                asm volatile("bar.sync 2, %0;" ::"r"((NC + 1) * 32) : "memory");
+                gate = false;
+            }
+            if (!__any_sync(0xffffffffu, live)) break;
+            bool ready = false;
+            if (live && !(gate && j >= early)) {
+                ready = j < NS || mbar_test_wait(&empty[c][j % NS], (uint32_t)((j / NS) - 1) & 1u);
+                // A consumer that gave up reports the error; stop serving it.
+                if (!ready && (*reinterpret_cast<volatile int *>(&s_abort[c]) || ++idle > kWaitLimit)) live = false;
+            }
+            if (ready) {
+                idle = 0;
                 const int s = j % NS;
-                if (j >= NS) {
-                    const uint32_t ph = (uint32_t)((j / NS) - 1) & 1u;
-                    bool ok = false;
-                    for (unsigned i = 0; i < kWaitLimit; ++i) {
-                        if (mbar_try_wait(&empty[c][s], ph)) {
-                            ok = true;
-                            break;
-                        }
-                        if (*reinterpret_cast<volatile int *>(&s_abort[c])) break;
-                    }
-                    if (!ok) break;     // the consumer gave up (it reports the error)
-                }
-                const int u0 = seg * UPI;
-                const int nu = min(UPI, p.nunits - u0);
+                const int nu = cur.count(UPI, p.nunits);
+                const int u0 = cur.pu;
                 uint8_t *dst = ring + (size_t)s * kSlot;
                 if (!(p.test_unarmed && blockIdx.x == 0 && c == 0 && j == 0)) {
                     if (Fmt<DT>::kBlockScales) {
                         const int b0 = 2 * u0, nblk = min(2 * nu, p.nb - b0);
                         const uint32_t cb = (uint32_t)nblk * Fmt<DT>::kBlockCode, sb = (uint32_t)nblk * 128u;
                         mbar_expect_tx(&full[c][s], cb + sb);
-                        bulk_g2s(dst, p.codes + ((size_t)tile * p.nb + b0) * Fmt<DT>::kBlockCode, cb, &full[c][s]);
-                        bulk_g2s(dst + UPI * unit_code<DT>(), p.scales + ((size_t)tile * p.nb + b0) * 32, sb,
+                        bulk_g2s(dst, p.codes + ((size_t)cur.tile * p.nb + b0) * Fmt<DT>::kBlockCode, cb,
+                                 &full[c][s]);
+                        bulk_g2s(dst + UPI * unit_code<DT>(), p.scales + ((size_t)cur.tile * p.nb + b0) * 32, sb,
                                  &full[c][s]);
                     } else {
                         const uint32_t cb = (uint32_t)nu * unit_code<DT>();
                         mbar_expect_tx(&full[c][s], cb);
-                        bulk_g2s(dst, p.codes + ((size_t)tile * p.nunits + u0) * unit_code<DT>(), cb, &full[c][s]);
+                        bulk_g2s(dst, p.codes + ((size_t)cur.tile * p.nunits + u0) * unit_code<DT>(), cb,
+                                 &full[c][s]);
                     }
                     issued = j + 1;
                 }
-                if (++seg == p.nseg) {
-                    seg = 0;
-                    ++tile;
-                }
+                cur.advance(nu, p.nunits);
+                ++j;
+                if (!cur.more()) live = false;
             }
-            // Copies still in flight land before the CTA exits: wait for the
-            // last NS issued items' slots (their consumer may have left).
+            if (!__any_sync(0xffffffffu, ready)) __nanosleep(32);
+        }
+        if (gate) asm volatile("bar.sync 2, %0;" ::"r"((NC + 1) * 32) : "memory");
+        // Copies still in flight land before the CTA exits: wait for the
+        // last NS issued items' slots (their consumer may have left).
+        if (c < NC) {
             for (int q = max(0, issued - NS); q < issued; ++q) {
                 if (p.test_unarmed && blockIdx.x == 0 && c == 0 && q == 0) continue;
                 for (unsigned i = 0; i < kWaitLimit; ++i)
                     if (mbar_try_wait(&full[c][q % NS], (uint32_t)(q / NS) & 1u)) break;
             }
         }
-        __syncwarp();
     } else {
         // ------------------------------------------------------ consumers --
         const int gw = blockIdx.x * NC + warp;
-        const long long it0 = range_begin(gw, T, W), it1 = range_begin(gw + 1, T, W);
-        const int n = (int)(it1 - it0);
+        const long long ua = range_begin(gw, U, W), ub = range_begin(gw + 1, U, W);
         const int tig = lane & 3;
         pdl_wait();
         prepare_x<DT, NC>(p, xi);
@@ -716,12 +824,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_stream(const StreamPara
         const LaneOff lo = lane_offsets<DT>(lane);
         const bool odd_nb = (p.nb & 1) != 0;
 
-        int cur_tile = -1, tile = (int)(it0 / p.nseg), seg = (int)(it0 % p.nseg);
+        Cursor cur;
+        cur.start(ua, ub, p.nunits);
+        int cur_tile = -1;
         float row_scale = 0.0f;
         bool cur_whole = false;
         Acc acc;
         acc.reset();
-        for (int j = 0; j < n; ++j) {
+        for (int j = 0; cur.more(); ++j) {
             const int s = j % NS;
             const uint32_t ph = (uint32_t)(j / NS) & 1u;
             const unsigned limit = (j == 0 && p.test_unarmed && blockIdx.x == 0 && warp == 0) ? p.wait_limit
@@ -742,10 +852,15 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_stream(const StreamPara
                 cur_tile = -1;     // nothing is stored for an unfinished tile
                 break;
             }
-            const int u0 = seg * UPI;
-            const int nu = min(UPI, p.nunits - u0);
+            const int u0 = cur.pu;
+            const int nu = cur.count(UPI, p.nunits);
+            const int tile = cur.tile;
+            const bool full_item = nu == UPI;
             Item<DT, UPI> R;
-            R.load(rings + ((size_t)warp * NS + s) * kSlot, nu, lane, odd_nb && u0 + nu == p.nunits);
+            const uint8_t *slot = rings + ((size_t)warp * NS + s) * kSlot;
+            const bool last_half = odd_nb && u0 + nu == p.nunits;
+            if (full_item) R.template load<true>(slot, nu, lane, last_half);
+            else R.template load<false>(slot, nu, lane, last_half);
             mbar_arrive(&empty[warp][s]);
 
             if (tile != cur_tile) {
@@ -756,14 +871,12 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_stream(const StreamPara
                 }
                 cur_tile = tile;
                 acc.reset();
-                cur_whole = (seg == 0) && ((long long)tile * p.nseg + p.nseg <= it1);
+                cur_whole = u0 == 0 && (long long)tile * p.nunits + p.nunits <= ub;
                 if (DT == DTYPE_TQ2_0) row_scale = __ldg(p.scales + (size_t)tile * 32 + lane);
             }
-            compute<UPI>(R, nu, u0, xi, lo, tig, acc);
-            if (++seg == p.nseg) {
-                seg = 0;
-                ++tile;
-            }
+            if (full_item) compute<true, UPI>(R, nu, u0, xi, lo, tig, acc);
+            else compute<false, UPI>(R, nu, u0, xi, lo, tig, acc);
+            cur.advance(nu, p.nunits);
         }
         if (cur_tile >= 0) {
             unsigned long long v[4] = {0, 0, 0, 0};
@@ -789,17 +902,16 @@ size_t stream_smem(tensor_dtype_t dt, int nb, StreamCfg c) {
     }
     return (size_t)c.nc * c.ns * slot + ximg_bytes(nb, dt == DTYPE_Q4_0);
 }
-
 // Configurations instantiated per format: (consumer warps, slots, units per
 // item).  SAPPHIRE_STREAM_CFG = an index selects one (tuning runs);
-// otherwise the first that fits shared memory with at least six items per
-// consumer warp on average, else the one with the most items per warp.
-// Consumer counts of 7, 11 and 15 make 8, 12 and 16 warps with the producer:
-// a whole number of warps per SM sub-partition, so no sub-partition's
-// register file caps the others' registers per thread.
-constexpr StreamCfg kQ8Cfgs[] = {{11, 3, 2}, {15, 2, 2}, {11, 2, 3}, {7, 4, 2}};
-constexpr StreamCfg kQ4Cfgs[] = {{11, 2, 5}, {11, 3, 4}, {15, 2, 4}, {11, 4, 2}, {15, 3, 2}};
-constexpr StreamCfg kTq2Cfgs[] = {{15, 4, 5}, {15, 2, 8}, {15, 3, 4}, {11, 4, 5}, {15, 4, 4}};
+// otherwise the first whose rings and x image fit shared memory.  Work is
+// balanced to a unit whatever the item size, so the order is by measured
+// speed.  Consumer counts of 7, 11 and 15 make 8, 12 and 16 warps with the
+// producer: a whole number of warps per SM sub-partition, so no
+// sub-partition's register file caps the others' registers per thread.
+constexpr StreamCfg kQ8Cfgs[] = {{11, 3, 2}, {15, 2, 2}, {11, 2, 3}, {7, 4, 2}, {11, 2, 4}};
+constexpr StreamCfg kQ4Cfgs[] = {{11, 2, 5}, {15, 2, 5}, {11, 3, 4}, {15, 2, 4}, {11, 2, 8}};
+constexpr StreamCfg kTq2Cfgs[] = {{15, 2, 10}, {11, 3, 10}, {15, 3, 6}, {15, 4, 5}, {15, 2, 8}};
 
 // Dynamic shared memory a configuration may use (the static barriers and
 // reduction arrays take the rest of the 227 KB per block).
@@ -807,34 +919,22 @@ constexpr size_t kStreamSmemMax = 225 * 1024;
 
 // {0, 0, 0} when no configuration fits (rows too long for the x image).
 template <size_t N>
-StreamCfg pick(const StreamCfg (&cfgs)[N], const DevWeight &w, int sms, int env) {
+StreamCfg pick(const StreamCfg (&cfgs)[N], const DevWeight &w, int env) {
     if (env >= 0 && env < (int)N && stream_smem(w.dtype, w.nb, cfgs[env]) <= kStreamSmemMax) return cfgs[env];
-    const int nunits = (w.nb + 1) / 2;
-    StreamCfg best = {0, 0, 0};
-    double best_ipw = -1.0;
-    for (size_t i = 0; i < N; ++i) {
-        const StreamCfg c = cfgs[i];
-        if (stream_smem(w.dtype, w.nb, c) > kStreamSmemMax) continue;
-        const long long items = (long long)w.ntiles * ((nunits + c.upi - 1) / c.upi);
-        const double ipw = (double)items / ((double)sms * c.nc);
-        if (ipw >= 6.0) return c;
-        if (ipw > best_ipw) {
-            best_ipw = ipw;
-            best = c;
-        }
-    }
-    return best;
+    for (size_t i = 0; i < N; ++i)
+        if (stream_smem(w.dtype, w.nb, cfgs[i]) <= kStreamSmemMax) return cfgs[i];
+    return StreamCfg{0, 0, 0};
 }
 
-StreamCfg stream_cfg(const DevWeight &w, int sms) {
+StreamCfg stream_cfg(const DevWeight &w) {
     static const int env = [] {
         const char *v = getenv("SAPPHIRE_STREAM_CFG");
         return v ? atoi(v) : -1;
     }();
     switch (w.dtype) {
-        case DTYPE_Q8_0: return pick(kQ8Cfgs, w, sms, env);
-        case DTYPE_Q4_0: return pick(kQ4Cfgs, w, sms, env);
-        default: return pick(kTq2Cfgs, w, sms, env);
+        case DTYPE_Q8_0: return pick(kQ8Cfgs, w, env);
+        case DTYPE_Q4_0: return pick(kQ4Cfgs, w, env);
+        default: return pick(kTq2Cfgs, w, env);
     }
 }
 
@@ -879,18 +979,19 @@ int dispatch(kernel_context_t *ctx, tensor_dtype_t dt, StreamCfg c, const Stream
         SAPPHIRE_STREAM_TRY(DTYPE_Q8_0, 15, 2, 2)
         SAPPHIRE_STREAM_TRY(DTYPE_Q8_0, 11, 2, 3)
         SAPPHIRE_STREAM_TRY(DTYPE_Q8_0, 7, 4, 2)
+        SAPPHIRE_STREAM_TRY(DTYPE_Q8_0, 11, 2, 4)
     } else if (dt == DTYPE_Q4_0) {
         SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 11, 2, 5)
+        SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 15, 2, 5)
         SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 11, 3, 4)
         SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 15, 2, 4)
-        SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 11, 4, 2)
-        SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 15, 3, 2)
+        SAPPHIRE_STREAM_TRY(DTYPE_Q4_0, 11, 2, 8)
     } else if (dt == DTYPE_TQ2_0) {
+        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 15, 2, 10)
+        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 11, 3, 10)
+        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 15, 3, 6)
         SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 15, 4, 5)
         SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 15, 2, 8)
-        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 15, 3, 4)
-        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 11, 4, 5)
-        SAPPHIRE_STREAM_TRY(DTYPE_TQ2_0, 15, 4, 4)
     }
     ctx_fail(ctx, "launch_gemv_stream", "no kernel instantiated for this configuration");
     return -1;
@@ -898,41 +999,61 @@ int dispatch(kernel_context_t *ctx, tensor_dtype_t dt, StreamCfg c, const Stream
 #undef SAPPHIRE_STREAM_TRY
 
 // Largest number of warps that can share one tile: ranges hold at least
-// floor(T/W) items each, so nseg consecutive items meet at most
-// ceil((nseg-1)/L) + 1 of them; with fewer items than warps every range holds
-// at most one item.
-int stream_kmax(long long T, long long W, int nseg) {
-    if (T <= 0) return 1;
-    if (T < W) return nseg;
-    const long long L = T / W;
-    const long long k = (nseg - 1 + L - 1) / L + 1;
-    return (int)(k < nseg ? k : nseg);
+// floor(U/W) units each, so a tile's n consecutive units meet at most
+// ceil((n-1)/L) + 1 of them; with fewer units than warps every range holds
+// at most one unit.
+int stream_kmax(long long U, long long W, int n) {
+    if (U <= 0) return 1;
+    if (U < W) return n;
+    const long long L = U / W;
+    const long long k = (n - 1 + L - 1) / L + 1;
+    return (int)(k < n ? k : n);
+}
+
+// Items per consumer issued before the consumers' x loads (SAPPHIRE_STREAM_EARLY
+// overrides the default of 1 for tuning runs).
+int stream_early() {
+    static const int v = [] {
+        const char *e = getenv("SAPPHIRE_STREAM_EARLY");
+        return e ? atoi(e) : 1;
+    }();
+    return v;
 }
 
 struct Geometry {
     StreamCfg c;
-    int nunits, nseg, grid;
-    long long items;
+    int nunits, grid;
+    long long units;
 };
 
 Geometry geometry(kernel_context_t *ctx, const DevWeight &w) {
     Geometry g;
     const int sms = sm_count(ctx->device);
-    g.c = stream_cfg(w, sms);
+    g.c = stream_cfg(w);
     g.nunits = (w.nb + 1) / 2;
+    g.units = (long long)w.ntiles * g.nunits;
     if (g.c.nc == 0) {
-        g.nseg = 0;
-        g.items = 0;
         g.grid = 0;
         return g;
     }
-    g.nseg = (g.nunits + g.c.upi - 1) / g.c.upi;
-    g.items = (long long)w.ntiles * g.nseg;
-    // One CTA per SM, or fewer when the weight has fewer items than a full
-    // grid has consumer warps: every warp gets work.
-    const long long want = (g.items + g.c.nc - 1) / g.c.nc;
+    // One CTA per SM, or fewer when the weight has fewer items of UPI units
+    // than a full grid has consumer warps: every warp gets work.
+    const long long items = (long long)w.ntiles * ((g.nunits + g.c.upi - 1) / g.c.upi);
+    const long long want = (items + g.c.nc - 1) / g.c.nc;
     g.grid = (int)std::min<long long>(sms, std::max<long long>(1, want));
     return g;
+}
+
+// Tags of the split-tile partial words: one per launch, process-wide (a
+// partial buffer may be shared by contexts), never 0 so zeroed memory never
+// reads as valid.
+std::atomic<unsigned> g_epoch{0};
+unsigned next_epoch() {
+    unsigned e;
+    do {
+        e = g_epoch.fetch_add(1) + 1;
+    } while (e == 0);
+    return e;
 }
 
 // Test hook (sapphire_test_stream_unarmed): 1 = the next launches leave consumer
@@ -951,14 +1072,16 @@ bool stream_supported(kernel_context_t *ctx, const DevWeight &w) {
     return geometry(ctx, w).c.nc > 0;
 }
 
+// Scratch in float units: epoch-tagged partial words [ntiles][kmax][32] (two
+// floats per word; two words per row for TQ2_0).  No counters.
 void stream_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints) {
     const Geometry g = geometry(ctx, w);
     const long long W = (long long)g.grid * g.c.nc;
-    *part_floats = (size_t)w.ntiles * stream_kmax(g.items, W, g.nseg) * 32 * (w.dtype == DTYPE_TQ2_0 ? 2 : 1);
-    *cnt_ints = (size_t)w.ntiles;
+    *part_floats = (size_t)w.ntiles * stream_kmax(g.units, W, g.nunits) * 32 * (w.dtype == DTYPE_TQ2_0 ? 4 : 2);
+    *cnt_ints = 0;
 }
 
-int launch_gemv_stream(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
+int launch_gemv_stream(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *,
                        int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
                        cudaStream_t st) {
     if (w.ntiles == 0) return 0;
@@ -977,18 +1100,18 @@ int launch_gemv_stream(kernel_context_t *ctx, const DevWeight &w, const float *x
     p.scales = w.scales;
     p.x = x;
     p.y = y;
-    p.part = part;
-    p.cnt = cnt;
+    p.part = reinterpret_cast<unsigned long long *>(part);
     p.err = err;
+    p.epoch = next_epoch();
     p.nrows = w.nrows;
     p.cols = w.cols;
     p.nb = w.nb;
     p.nunits = g.nunits;
     p.ntiles = w.ntiles;
-    p.nseg = g.nseg;
-    p.total_items = g.items;
+    p.total_units = g.units;
     p.total_warps = g.grid * g.c.nc;
-    p.kmax = stream_kmax(g.items, p.total_warps, g.nseg);
+    p.kmax = stream_kmax(g.units, p.total_warps, g.nunits);
+    p.early = stream_early();
     p.test_unarmed = g_test_unarmed.load() ? 1 : 0;
     p.wait_limit = p.test_unarmed ? (1u << 12) : kWaitLimit;
     p.ll_n = ll_n;
