@@ -502,12 +502,49 @@ def measure_gemv(args, env, cfg, with_cpu: bool) -> dict:
     ctx.synchronize()
     parity = gemv_parity(env, cfg, y_dev.cpu().numpy()[0], packed0, X)
 
+    # ---- sharded: the rank's local slice as an unsharded GEMV on its own
+    # context, timed the same way, so the gather's share of a step shows.
+    breakdown = None
+    if world > 1:
+        row0, nloc = sp.shard_rows(cfg.rows, rank, world)
+        rb = WL.row_bytes(cfg.dtype, cfg.cols)
+        lctx = sp.Context(num_threads=1, device=env.local)
+        AL = [sp.Tensor(cfg.dtype, (nloc, cfg.cols), pk[row0 * rb:(row0 + nloc) * rb]) for pk in (packed0, packed1)]
+        for a in AL:
+            lctx.check(sp.lib.kernel_tensor_upload(lctx.handle, a.handle), "upload slice")
+        yl = torch.zeros(nloc, device="cuda")
+        lstream = torch.cuda.ExternalStream(lctx.stream)
+
+        def lstep(i):
+            return sp.lib.kernel_gemv_device(lctx.handle, yl.data_ptr(), AL[i & 1].handle, x_dev.data_ptr())
+        for i in range(args.warmup):
+            lctx.check(lstep(i), "local warm-up")
+        lctx.synchronize()
+        l0 = torch.cuda.Event(enable_timing=True)
+        l1 = torch.cuda.Event(enable_timing=True)
+        l0.record(lstream)
+        for i in range(args.steps):
+            lctx.check(lstep(i), "local step")
+        l1.record(lstream)
+        lctx.synchronize()
+        (local_ms,) = env.max_over_ranks([l0.elapsed_time(l1) / args.steps])
+        for a in AL:
+            a.release()
+        lctx.close()
+        breakdown = {"sharded_product_ms_per_step": round(ms_per_step, 5),
+                     "local_gemv_ms_per_step": round(local_ms, 5),
+                     "gather_and_sync_ms_per_step": round(ms_per_step - local_ms, 5),
+                     "local_rows": nloc,
+                     "how": "the rank's row slice timed as an unsharded GEMV (steps back to back, max over ranks); "
+                            "the difference is the peer-memory gather and the wait for the slowest rank"}
+
     peaks = measured_peaks()
     per_rank_rows = (cfg.rows + world - 1) // world if world > 1 else cfg.rows
     kern_bytes = algorithmic_bytes(cfg.dtype, per_rank_rows, cfg.cols, 1)
     achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
     tag = f"gemv_{WL.DTYPE_NAMES[cfg.dtype].lower()}_{cfg.name}"
-    gather = "peer-memory gather: GEMV epilogue stores 8-byte (epoch | value) words to every rank over NVLink"
+    gather = ("peer-memory gather fused into the GEMV: its epilogue stores 8-byte (epoch | value) words to every "
+              "rank over NVLink and its warps then collect their slice of y")
     entry = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
@@ -522,14 +559,16 @@ def measure_gemv(args, env, cfg, with_cpu: bool) -> dict:
                      "frac_sustained": round(kern_bytes / (ms_per_step * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                      "kernel_ms": round(kern_ms, 5), "traffic": ncu_traffic(tag), "kernel": tag,
                      "kernel_ms_covers": "one GEMV launch alone (events around it)" if world == 1
-                     else "one sharded product alone: local GEMV + peer-memory gather",
+                     else "one sharded product alone: the GEMV with its fused peer-memory gather",
                      "frac_sustained_covers": "the same bytes over ms_per_step (steps back to back)"},
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": 4 * cfg.cols,
                 "d2h_bytes_per_step": 4 * cfg.rows, "ms_per_step": round(e2e_ms, 5),
                 "path": "kernel_gemv with pinned host x/y (weights resident after upload)"},
-        "gpu_launches": args.steps * (1 if world == 1 else 2),
+        "gpu_launches": args.steps,
         "parity": parity,
     }
+    if breakdown:
+        entry["breakdown"] = breakdown
     if rank == 0:
         entry["clocks"] = sampler.summary()
     if with_cpu and rank == 0:

@@ -1314,14 +1314,18 @@ void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_f
 // err: scratch sized by pipe_scratch_size (counters zero), error word.
 int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
                      int *err, cudaStream_t st) {
-    return launch_gemv_pipe_ll(ctx, w, x, y, part, cnt, err, nullptr, 0, 0, 0u, st);
+    return launch_gemv_pipe_ll(ctx, w, x, y, part, cnt, err, nullptr, nullptr, st);
 }
 
 int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
-                        int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
-                        cudaStream_t st) {
-    if (stream_dtype(w.dtype)) return launch_gemv_stream(ctx, w, x, y, part, cnt, err, ll, ll_n, ll_off, ll_epoch, st);
+                        int *err, const GatherArgs *g, bool *gathered, cudaStream_t st) {
+    if (gathered) *gathered = false;
+    if (stream_dtype(w.dtype)) {
+        if (gathered && g) *gathered = w.ntiles > 0;
+        return launch_gemv_stream(ctx, w, x, y, part, cnt, err, g, st);
+    }
     if (w.ntiles == 0) return 0;
+    const int ll_n = g ? g->n : 0;
     if (ll_n < 0 || ll_n > kMaxPeers) {
         ctx_fail(ctx, "launch_gemv_pipe", "%d gather targets (at most %d)", ll_n, kMaxPeers);
         return -1;
@@ -1330,9 +1334,9 @@ int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *
     PipeParams p;
     p.early = pipe_early(c);
     p.ll_n = ll_n;
-    p.ll_off = ll_off;
-    p.ll_epoch = ll_epoch;
-    for (int k = 0; k < kMaxPeers; ++k) p.ll[k] = k < ll_n ? ll[k] : nullptr;
+    p.ll_off = g ? g->row_off : 0;
+    p.ll_epoch = g ? g->epoch : 0u;
+    for (int k = 0; k < kMaxPeers; ++k) p.ll[k] = k < ll_n ? g->targets[k] : nullptr;
     p.codes = reinterpret_cast<const uint8_t *>(w.codes);
     p.scales = w.scales;
     p.x = x;

@@ -172,6 +172,13 @@ struct StreamParams {
     int ll_n, ll_off;
     unsigned ll_epoch;
     unsigned long long *ll[kMaxPeers];
+    // The gather itself: once a consumer warp has finished its items it
+    // waits for rows [gw*R/W, (gw+1)*R/W) of its own buffer `ll_self` to
+    // carry the epoch (bounded by ll_wait_ns) and writes them to y_full.
+    const unsigned long long *ll_self;
+    float *y_full;
+    long long rows_full;
+    unsigned long long ll_wait_ns;
 };
 
 __device__ __forceinline__ void store_y(const StreamParams &p, size_t r, float v) {
@@ -701,6 +708,58 @@ __device__ void flush_tile(const StreamParams &p, const XImage &xi, int tile, in
     if (row_ok) store_y(p, (size_t)tile * 32 + lane, ok ? finish_row<DT>(xi, sum, nonfinite, rs) : __int_as_float(0x7FC00000));
 }
 
+// The gather step of a row-sharded product: rows [r0, r1) of this rank's
+// buffer.  Each lane loads up to kGatherBatch words at once (one round trip
+// for the whole slice), then waits only for words that do not carry the
+// epoch yet.  A word that does not arrive within wait_ns sets bit 3 of *err
+// and the CTA-wide flag `expired`, after which the CTA's warps stop waiting
+// and store NaN for stale words.
+constexpr int kGatherBatch = 8;
+
+__device__ __forceinline__ unsigned long long ld_sys(const unsigned long long *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+__device__ void gather_rows(const StreamParams &p, long long r0, long long r1, int lane, int *expired) {
+    for (long long rb = r0 + lane; rb < r1; rb += 32 * kGatherBatch) {
+        unsigned long long w[kGatherBatch];
+#pragma unroll
+        for (int q = 0; q < kGatherBatch; ++q) {
+            const long long r = rb + 32 * q;
+            w[q] = r < r1 ? ld_sys(p.ll_self + r) : 0ull;
+        }
+#pragma unroll
+        for (int q = 0; q < kGatherBatch; ++q) {
+            const long long r = rb + 32 * q;
+            if (r >= r1) break;
+            if ((unsigned)(w[q] >> 32) != p.ll_epoch) {
+                uint64_t t0;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+                for (;;) {
+                    if (*reinterpret_cast<volatile int *>(expired)) {
+                        w[q] = 0x7FC00000ull;
+                        break;
+                    }
+                    __nanosleep(64);
+                    w[q] = ld_sys(p.ll_self + r);
+                    if ((unsigned)(w[q] >> 32) == p.ll_epoch) break;
+                    uint64_t t;
+                    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                    if (t - t0 > p.ll_wait_ns) {
+                        atomicOr(p.err, 8);
+                        *reinterpret_cast<volatile int *>(expired) = 1;
+                        w[q] = 0x7FC00000ull;
+                        break;
+                    }
+                }
+            }
+            p.y_full[r] = __uint_as_float((unsigned)(w[q] & 0xFFFFFFFFull));
+        }
+    }
+}
+
 // --------------------------------------------------------------- kernel ---
 template <tensor_dtype_t DT, int NC, int NS, int UPI>
 __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_stream(const StreamParams p) {
@@ -708,6 +767,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_stream(const StreamPara
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int s_nonfinite;
     __shared__ int s_abort[kMaxConsumers];
+    __shared__ int s_expired;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // Shared memory: [rings][x image], barriers in static shared memory.
@@ -733,6 +793,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_stream(const StreamPara
     if (threadIdx.x < kMaxConsumers) s_abort[threadIdx.x] = 0;
     if (threadIdx.x == 0) {
         s_nonfinite = 0;
+        s_expired = 0;
         fence_mbar_init();
     }
     __syncthreads();
@@ -883,6 +944,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_stream(const StreamPara
             tile_rows<DT>(acc, v, pe);
             flush_tile<DT>(p, xi, cur_tile, lane, gw, cur_whole, v, nonfinite, row_scale);
         }
+        if (p.ll_n && p.ll_self)
+            gather_rows(p, range_begin(gw, p.rows_full, W), range_begin(gw + 1, p.rows_full, W), lane, &s_expired);
     }
     __syncthreads();
 }
@@ -1082,9 +1145,9 @@ void stream_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part
 }
 
 int launch_gemv_stream(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *,
-                       int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
-                       cudaStream_t st) {
+                       int *err, const GatherArgs *ga, cudaStream_t st) {
     if (w.ntiles == 0) return 0;
+    const int ll_n = ga ? ga->n : 0;
     if (ll_n < 0 || ll_n > kMaxPeers) {
         ctx_fail(ctx, "launch_gemv_stream", "%d gather targets (at most %d)", ll_n, kMaxPeers);
         return -1;
@@ -1115,9 +1178,13 @@ int launch_gemv_stream(kernel_context_t *ctx, const DevWeight &w, const float *x
     p.test_unarmed = g_test_unarmed.load() ? 1 : 0;
     p.wait_limit = p.test_unarmed ? (1u << 12) : kWaitLimit;
     p.ll_n = ll_n;
-    p.ll_off = ll_off;
-    p.ll_epoch = ll_epoch;
-    for (int k = 0; k < kMaxPeers; ++k) p.ll[k] = k < ll_n ? ll[k] : nullptr;
+    p.ll_off = ga ? ga->row_off : 0;
+    p.ll_epoch = ga ? ga->epoch : 0u;
+    for (int k = 0; k < kMaxPeers; ++k) p.ll[k] = k < ll_n ? ga->targets[k] : nullptr;
+    p.ll_self = ga ? ga->self : nullptr;
+    p.y_full = ga ? ga->y_full : nullptr;
+    p.rows_full = ga ? ga->rows_full : 0;
+    p.ll_wait_ns = ga ? ga->wait_ns : 0;
     const size_t smem = stream_smem(w.dtype, w.nb, g.c);
     return dispatch(ctx, w.dtype, g.c, p, g.grid, smem, st);
 }

@@ -221,18 +221,30 @@ void pipe_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_f
 int launch_gemv_pipe(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part,
                      int *cnt, int *err, cudaStream_t stream);
 int pipe_kmax(long long T, long long W, int nseg);
-// The pipelined GEMV sending each row r as (epoch << 32 | value bits) to
-// ll[k][ll_off + r] for the ll_n ranks of a peer-memory gather (ll_n == 0: y[r]).
+// Peer-memory gather of a row-sharded batch-1 product (shard.cu): each row r
+// goes to every rank k as the 8-byte word (epoch << 32 | value bits) at
+// targets[k][row_off + r]; `self` is this rank's own buffer of the epoch,
+// from which y_full[0, rows_full) is gathered.
+struct GatherArgs {
+    unsigned long long *targets[kMaxPeers];
+    int n, row_off;
+    unsigned epoch;
+    const unsigned long long *self;
+    float *y_full;
+    long long rows_full;
+    unsigned long long wait_ns;
+};
+// The pipelined GEMV with its rows sent to a peer-memory gather (g != nullptr)
+// instead of y.  *gathered = true when the kernel also gathered y_full (the
+// streaming kernel does; the dense kernel leaves it to a pull kernel).
 int launch_gemv_pipe_ll(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
-                        int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
-                        cudaStream_t stream);
+                        int *err, const GatherArgs *g, bool *gathered, cudaStream_t stream);
 // Streaming batch-1 GEMV of the quantized formats (gemv_stream.cu).
 bool stream_dtype(tensor_dtype_t dt);
 bool stream_supported(kernel_context_t *ctx, const DevWeight &w);
 void stream_scratch_size(kernel_context_t *ctx, const DevWeight &w, size_t *part_floats, size_t *cnt_ints);
 int launch_gemv_stream(kernel_context_t *ctx, const DevWeight &w, const float *x, float *y, float *part, int *cnt,
-                       int *err, unsigned long long *const *ll, int ll_n, int ll_off, unsigned ll_epoch,
-                       cudaStream_t stream);
+                       int *err, const GatherArgs *g, cudaStream_t stream);
 // Latency-bound GEMV of a small Q8_0 / Q4_0 weight (gemv_pipe.cu): one CTA per
 // 32-row tile, no scratch.
 bool direct_supported(const DevWeight &w);

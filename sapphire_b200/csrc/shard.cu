@@ -270,28 +270,42 @@ bool shard_peer_product(kernel_context_t *ctx, const DevWeight &w, const float *
     cudaStream_t st = ctx->stream;
     const unsigned epoch = ++g.epoch;
     const size_t buf = (size_t)(epoch & 1u) * g.cap_rows;
-    unsigned long long *targets[kMaxPeers];
-    for (int k = 0; k < ctx->world; ++k) targets[k] = g.peer[k] + buf;
-    size_t pf = 0, ci = 0;
-    pipe_scratch_size(ctx, w, &pf, &ci);
-    if (ensure_pipe_scratch(ctx, pf, ci)) return true;
-    if (w.ntiles > 0 && launch_gemv_pipe_ll(ctx, w, x, nullptr, ctx->d_part, ctx->d_cnt, ctx->d_err, targets,
-                                            ctx->world, w.row0, epoch, st))
-        return true;
     float *yd = Y;
     if (!y_on_dev) {
         if (ensure_scratch(ctx, &ctx->d_y, &ctx->d_y_cap, (size_t)rows * sizeof(float))) return true;
         yd = ctx->d_y;
     }
-    const int grid = (int)std::max<long long>(1, std::min<long long>(4 * 148, ((long long)rows + kPullThreads - 1) / kPullThreads));
-    cudaError_t e = launch_pdl(ll_pull_kernel, dim3(grid), dim3(kPullThreads), 0, st,
-                               (const unsigned long long *)(g.local + buf), (long long)rows, epoch, yd, ctx->d_err,
-                               kPeerWaitNs);
-    if (e == cudaSuccess) e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        ctx_fail(ctx, "kernel_gemv", "gather launch failed: %s", cudaGetErrorString(e));
+    GatherArgs ga{};
+    for (int k = 0; k < ctx->world; ++k) ga.targets[k] = g.peer[k] + buf;
+    ga.n = ctx->world;
+    ga.row_off = w.row0;
+    ga.epoch = epoch;
+    ga.self = g.local + buf;
+    ga.y_full = yd;
+    ga.rows_full = rows;
+    ga.wait_ns = kPeerWaitNs;
+    size_t pf = 0, ci = 0;
+    pipe_scratch_size(ctx, w, &pf, &ci);
+    if (ensure_pipe_scratch(ctx, pf, ci)) return true;
+    // The streaming kernel gathers y itself once its warps are done; a rank
+    // with no rows, or the dense kernel, leaves the gather to a pull kernel.
+    bool gathered = false;
+    if (w.ntiles > 0 && launch_gemv_pipe_ll(ctx, w, x, nullptr, ctx->d_part, ctx->d_cnt, ctx->d_err, &ga, &gathered,
+                                            st))
         return true;
+    if (!gathered) {
+        const int grid =
+            (int)std::max<long long>(1, std::min<long long>(4 * 148, ((long long)rows + kPullThreads - 1) / kPullThreads));
+        cudaError_t e = launch_pdl(ll_pull_kernel, dim3(grid), dim3(kPullThreads), 0, st,
+                                   (const unsigned long long *)(g.local + buf), (long long)rows, epoch, yd, ctx->d_err,
+                                   kPeerWaitNs);
+        if (e == cudaSuccess) e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            ctx_fail(ctx, "kernel_gemv", "gather launch failed: %s", cudaGetErrorString(e));
+            return true;
+        }
     }
+    cudaError_t e = cudaSuccess;
     if (!y_on_dev) {
         e = cudaMemcpyAsync(Y, yd, (size_t)rows * sizeof(float), cudaMemcpyDeviceToHost, st);
         if (e != cudaSuccess) {
