@@ -155,12 +155,12 @@ extern "C" SAPPHIRE_API int kernel_gemv(kernel_context_t *ctx, float *y, const t
     if (check_gemv_args("kernel_gemv", y, A, x)) return -1;
     if (!ctx) {
         if (quantized(tensor_dtype(A))) {
-            LOG_ERROR("kernel_gemv: a quantized weight needs a context (got NULL)");
+            LOG_ERROR("a quantized weight needs a context (got NULL)");
             return -1;
         }
         ctx = default_context();
         if (!ctx) {
-            LOG_ERROR("kernel_gemv: no GPU context available");
+            LOG_ERROR("no GPU context available");
             return -1;
         }
     }
@@ -170,11 +170,11 @@ extern "C" SAPPHIRE_API int kernel_gemv(kernel_context_t *ctx, float *y, const t
 extern "C" SAPPHIRE_API int kernel_gemm(kernel_context_t *ctx, float *Y, const tensor_t *A, const float *X,
                                         int batch_size, int out_stride) {
     if (!Y || !A || !X || batch_size <= 0) {
-        LOG_ERROR("kernel_gemm: NULL buffer or batch_size <= 0");
+        LOG_ERROR("NULL buffer or batch_size <= 0");
         return -1;
     }
     if (!ctx) {
-        LOG_ERROR("kernel_gemm: a context is required (got NULL)");
+        LOG_ERROR("a context is required (got NULL)");
         return -1;
     }
     if (check_gemv_args("kernel_gemm", Y, A, X)) return -1;
@@ -185,28 +185,28 @@ extern "C" SAPPHIRE_API int kernel_gemm(kernel_context_t *ctx, float *Y, const t
 extern "C" SAPPHIRE_API int kernel_gemv_tensor(kernel_context_t *ctx, const tensor_t *y, const tensor_t *A,
                                                const tensor_t *x) {
     if (!y || !A || !x) {
-        LOG_ERROR("kernel_gemv_tensor: NULL tensor argument");
+        LOG_ERROR("NULL tensor argument");
         return -1;
     }
     if (tensor_ndim(y) != 1 || tensor_dtype(y) != DTYPE_F32) {
-        LOG_ERROR("kernel_gemv_tensor: y has to be a one-dimensional F32 tensor");
+        LOG_ERROR("y has to be a one-dimensional F32 tensor");
         return -1;
     }
     if (tensor_ndim(x) != 1 || tensor_dtype(x) != DTYPE_F32) {
-        LOG_ERROR("kernel_gemv_tensor: x has to be a one-dimensional F32 tensor");
+        LOG_ERROR("x has to be a one-dimensional F32 tensor");
         return -1;
     }
     const int *sa = tensor_shape(A), *sx = tensor_shape(x), *sy = tensor_shape(y);
     if (!sa || !sx || !sy) {
-        LOG_ERROR("kernel_gemv_tensor: a tensor has no shape");
+        LOG_ERROR("a tensor has no shape");
         return -1;
     }
     if (sa[1] != sx[0]) {
-        LOG_ERROR("kernel_gemv_tensor: A has %d columns but x has %d elements", sa[1], sx[0]);
+        LOG_ERROR("A has %d columns but x has %d elements", sa[1], sx[0]);
         return -1;
     }
     if (sy[0] != sa[0]) {
-        LOG_ERROR("kernel_gemv_tensor: y has %d elements but A has %d rows", sy[0], sa[0]);
+        LOG_ERROR("y has %d elements but A has %d rows", sy[0], sa[0]);
         return -1;
     }
     return kernel_gemv(ctx, tensor_data_f32(y), A, (const float *)tensor_data(x));
@@ -215,17 +215,17 @@ extern "C" SAPPHIRE_API int kernel_gemv_tensor(kernel_context_t *ctx, const tens
 extern "C" SAPPHIRE_API int kernel_gemv_add(kernel_context_t *ctx, float *y, const tensor_t *A, const float *x,
                                             float alpha) {
     if (!y || !A || !x) {
-        LOG_ERROR("kernel_gemv_add: NULL buffer or tensor");
+        LOG_ERROR("NULL buffer or tensor");
         return -1;
     }
     if (tensor_ndim(A) != 2) {
-        LOG_ERROR("kernel_gemv_add: A has to be two-dimensional");
+        LOG_ERROR("A has to be two-dimensional");
         return -1;
     }
     if (check_gemv_args("kernel_gemv_add", y, A, x)) return -1;
     if (!ctx) {
         if (quantized(tensor_dtype(A))) {
-            LOG_ERROR("kernel_gemv_add requires non-NULL context for quantized weights");
+            LOG_ERROR("a quantized weight needs a context (got NULL)");
             return -1;
         }
         ctx = default_context();
@@ -264,11 +264,11 @@ extern "C" SAPPHIRE_API int kernel_gemv_add(kernel_context_t *ctx, float *y, con
 extern "C" SAPPHIRE_API int kernel_gemv_batch(kernel_context_t *ctx, float *Y, const tensor_t *A, const float *X,
                                               int batch_size) {
     if (!Y || !A || !X || batch_size <= 0) {
-        LOG_ERROR("kernel_gemv_batch: NULL buffer or batch size <= 0");
+        LOG_ERROR("NULL buffer or batch size <= 0");
         return -1;
     }
     if (tensor_ndim(A) != 2) {
-        LOG_ERROR("kernel_gemv_batch: A has to be two-dimensional");
+        LOG_ERROR("A has to be two-dimensional");
         return -1;
     }
     if (batch_size > 1 && ctx) {

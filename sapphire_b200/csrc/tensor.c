@@ -63,12 +63,12 @@ static size_t numel_of(int ndim, const int *shape) {
 
 tensor_t* tensor_create(int ndim, const int *shape, tensor_dtype_t dtype) {
     if (ndim < 1 || ndim > 8 || !shape) {
-        LOG_ERROR("tensor_create: ndim %d out of range or shape missing", ndim);
+        LOG_ERROR("ndim %d out of range or shape missing", ndim);
         return NULL;
     }
     tensor_t *t = (tensor_t *)calloc(1, sizeof *t);
     if (!t) {
-        LOG_ERROR("tensor_create: out of memory for the handle");
+        LOG_ERROR("out of memory for the handle");
         return NULL;
     }
     t->ndim = ndim;
@@ -79,7 +79,7 @@ tensor_t* tensor_create(int ndim, const int *shape, tensor_dtype_t dtype) {
     t->nbytes = (dtype == DTYPE_Q4_0) ? (numel + 1) / 2 : numel * dtype_element_size(dtype);
     t->data = calloc(t->nbytes ? t->nbytes : 1, 1);
     if (!t->data) {
-        LOG_ERROR("tensor_create: out of memory for %zu bytes", t->nbytes);
+        LOG_ERROR("out of memory for %zu bytes", t->nbytes);
         free(t);
         return NULL;
     }
@@ -91,7 +91,7 @@ tensor_t* tensor_create(int ndim, const int *shape, tensor_dtype_t dtype) {
 
 tensor_t* tensor_create_view(tensor_dtype_t dtype, int ndim, const int *shape, void *data) {
     if (ndim < 1 || ndim > 8 || !shape) {
-        LOG_ERROR("tensor_create_view: ndim %d out of range or shape missing", ndim);
+        LOG_ERROR("ndim %d out of range or shape missing", ndim);
         return NULL;
     }
     tensor_t *t = (tensor_t *)calloc(1, sizeof *t);
@@ -135,7 +135,7 @@ size_t tensor_numel(const tensor_t *t) { return t ? numel_of(t->ndim, t->shape) 
 
 float tensor_get_f32(const tensor_t *t, size_t idx) {
     if (!t || idx >= tensor_numel(t)) {
-        LOG_ERROR("tensor_get_f32: index %zu out of range", idx);
+        LOG_ERROR("index %zu out of range", idx);
         return 0.0f;
     }
     if (t->dtype == DTYPE_F32) return ((const float *)t->data)[idx];
@@ -147,11 +147,11 @@ float tensor_get_f32(const tensor_t *t, size_t idx) {
 
 int tensor_set_f32(tensor_t *t, size_t idx, float val) {
     if (!t || idx >= tensor_numel(t)) {
-        LOG_ERROR("tensor_set_f32: index %zu out of range", idx);
+        LOG_ERROR("index %zu out of range", idx);
         return -1;
     }
     if (t->dtype != DTYPE_F32) {
-        LOG_ERROR("tensor_set_f32: the tensor is not F32");
+        LOG_ERROR("the tensor is not F32");
         return -1;
     }
     ((float *)t->data)[idx] = val;
@@ -172,7 +172,7 @@ void tensor_release(tensor_t *t) {
 
 void tensor_print_info(const tensor_t *t) {
     if (!t) {
-        LOG_INFO("tensor_print_info: (null tensor)");
+        LOG_INFO("(null tensor)");
         return;
     }
     char shape[8 * 12 + 3];
@@ -180,7 +180,7 @@ void tensor_print_info(const tensor_t *t) {
     for (int i = 0; i < t->ndim && pos < (int)sizeof shape; ++i)
         pos += snprintf(shape + pos, sizeof shape - (size_t)pos, i ? ",%d" : "%d", t->shape[i]);
     if (pos < (int)sizeof shape) snprintf(shape + pos, sizeof shape - (size_t)pos, "]");
-    LOG_INFO("tensor_print_info: shape %s, %s, %s layout, %zu bytes, %d references", shape,
+    LOG_INFO("shape %s, %s, %s layout, %zu bytes, %d references", shape,
              dtype_name(t->dtype), t->layout == LAYOUT_ROW_MAJOR ? "row-major" : "col-major",
              t->nbytes, t->ref_count);
 }
@@ -192,7 +192,7 @@ const void* tensor_data(const tensor_t *t) { return t ? t->data : NULL; }
 float* tensor_data_f32(const tensor_t *t) {
     if (!t) return NULL;
     if (t->dtype != DTYPE_F32) {
-        LOG_WARN("tensor_data_f32: dtype %d is not F32", (int)t->dtype);
+        LOG_WARN("dtype %d is not F32", (int)t->dtype);
         return NULL;
     }
     return (float *)t->data;
