@@ -53,7 +53,13 @@ typedef struct {
 } sapphire_gemma3_weights_t;
 
 /** Upload a model and allocate the KV cache on the context's GPU.  NULL on error
- *  (message in kernel_ctx_last_error). */
+ *  (message in kernel_ctx_last_error).  On a sharded context
+ *  (kernel_ctx_init_sharded) every rank holds the whole model except the LM
+ *  head, whose rows are sharded: each rank computes its slice of the logits
+ *  and the ranks agree on the greedy token by exchanging 8-byte (value,
+ *  index) words over peer memory instead of gathering the logits.  Then
+ *  create, generate and last_logits are collective: every rank calls them in
+ *  the same order with the same arguments. */
 SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_context_t *ctx, const sapphire_gemma3_config_t *cfg,
                                                          const sapphire_gemma3_weights_t *w);
 /** Greedy generation as the reference's perform_inference orders it
@@ -64,7 +70,8 @@ SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_context_t *ctx, 
  *  first.  n_prompt + n_gen must not exceed the context.  0 / -1. */
 SAPPHIRE_API int sapphire_decoder_generate(sapphire_decoder_t *d, const int *prompt, int n_prompt, int n_gen,
                                            int *out_ids, float *out_margins);
-/** Logits of the last generated step ([vocab] floats, host or device pointer). */
+/** Logits of the last generated step ([vocab] floats, host or device pointer);
+ *  on a sharded decoder the ranks' slices are all-gathered (NCCL) first. */
 SAPPHIRE_API int sapphire_decoder_last_logits(sapphire_decoder_t *d, float *out);
 /** Device time in milliseconds of the prompt and generation phases of the last
  *  sapphire_decoder_generate (CUDA events on the context stream). */

@@ -403,7 +403,7 @@ static int fill_layout(kernel_context_t *ctx, DevWeight &w) {
     return 0;
 }
 
-static int upload(kernel_context_t *ctx, const tensor_t *A, DevWeight &w) {
+static int upload(kernel_context_t *ctx, const tensor_t *A, DevWeight &w, bool whole) {
     const void *data = tensor_data(A);
     if (!data) {
         ctx_fail(ctx, "kernel_tensor_upload", "tensor has no data");
@@ -416,7 +416,12 @@ static int upload(kernel_context_t *ctx, const tensor_t *A, DevWeight &w) {
         ctx_fail(ctx, "kernel_tensor_upload", "weight must be 2-D with positive shape");
         return -1;
     }
-    shard_rows(w.rows, ctx->rank, ctx->world, &w.row0, &w.nrows);
+    if (whole) {
+        w.row0 = 0;
+        w.nrows = w.rows;
+    } else {
+        shard_rows(w.rows, ctx->rank, ctx->world, &w.row0, &w.nrows);
+    }
     if (fill_layout(ctx, w)) return -1;
     const size_t code_bytes = (size_t)w.ntiles * w.kchunks * 32 * 16;
     const size_t scale_bytes = (size_t)w.ntiles * w.nscale * 32 * sizeof(float);
@@ -485,21 +490,21 @@ static int upload(kernel_context_t *ctx, const tensor_t *A, DevWeight &w) {
     return rc;
 }
 
-const DevWeight *ctx_weight(kernel_context_t *ctx, const tensor_t *A) {
+const DevWeight *ctx_weight(kernel_context_t *ctx, const tensor_t *A, bool whole) {
     const uint64_t uid = sapphire_tensor_uid(A);
     auto it = ctx->weights.find(uid);
     if (it != ctx->weights.end()) {
         const DevWeight &w = it->second;
         int r = 0, c = 0;
         if (w.src == tensor_data(A) && w.dtype == tensor_dtype(A) && weight_shape(A, &r, &c) && r == w.rows &&
-            c == w.cols)
+            c == w.cols && (whole ? w.nrows == w.rows : true))
             return &w;
         cudaStreamSynchronize(ctx->stream);
         free_weight(it->second);
         ctx->weights.erase(it);
     }
     DevWeight w;
-    if (upload(ctx, A, w)) return nullptr;
+    if (upload(ctx, A, w, whole)) return nullptr;
     auto res = ctx->weights.emplace(uid, w);
     return &res.first->second;
 }

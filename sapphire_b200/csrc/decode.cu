@@ -62,7 +62,16 @@ struct DecState {
     int prompt_index;   // index of cur_token in the prompt during the prompt phase
     int n_prompt;
     int gen_index;      // next output slot
+    unsigned epoch;     // sharded LM head: generated steps so far (tag of the exchange words)
 };
+
+// Sharded LM head: every rank's mapped exchange buffer, [2 parities][kMaxPeers
+// ranks][4 words] of (epoch << 32 | 32 bits).
+struct PeerSlots {
+    unsigned long long *p[kMaxPeers];
+};
+constexpr int kExchWords = 4;
+constexpr unsigned long long kExchWaitNs = 2000000000ull;
 
 // ------------------------------------------------------------ reductions --
 __device__ __forceinline__ float warp_sum(float v) {
@@ -474,6 +483,102 @@ __global__ void argmax_advance_kernel(const float *logits, int n, Top2 *part, in
     }
 }
 
+// Greedy token of a row-sharded LM head: every rank reduces its slice of the
+// logits (rows row0 .. row0 + n) to (top-1 value, its global index, top-2
+// value) like argmax_advance_kernel; the last block sends the three values to
+// every rank as epoch-tagged 8-byte words (an aligned 8-byte store arrives
+// whole), waits (bounded) for every rank's words of this epoch, and merges
+// them in rank order with the same rule, lowest index on ties - so every rank
+// picks the same token as the unsharded argmax (src/utils/utils.c:145-156)
+// having exchanged 8 * 3 bytes per rank instead of the logits.  Buffers
+// alternate by epoch parity: a rank writes parity p again two steps later,
+// after its own wait of the step between, which needed every rank's words of
+// that step, written after that rank's kernel of this step had completed.
+__global__ void argmax_sharded_kernel(const float *logits, int n, int row0, Top2 *part, int *counter, DecState *st,
+                                      int *out_tokens, float *out_margins, PeerSlots peers, int world, int rank,
+                                      const unsigned long long *mine, int *err) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ Top2 sh[32];
+    __shared__ int last;
+    __shared__ Top2 ranks[kMaxPeers];
+    Top2 t{-INFINITY, 0x7fffffff, -INFINITY};
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        top2_push(t, logits[i], row0 + i);
+    t = block_top2(t, sh);
+    if (threadIdx.x == 0) {
+        part[blockIdx.x] = t;
+        __threadfence();
+        last = (atomicAdd(counter, 1) == (int)gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    Top2 r{-INFINITY, 0x7fffffff, -INFINITY};
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
+        Top2 u;
+        u.v1 = __ldcg(&part[b].v1);
+        u.i1 = __ldcg(&part[b].i1);
+        u.v2 = __ldcg(&part[b].v2);
+        r = top2_merge(r, u);
+    }
+    r = block_top2(r, sh);
+    const unsigned epoch = st->epoch + 1;
+    const int parity = (int)(epoch & 1u);
+    const unsigned long long tag = (unsigned long long)epoch << 32;
+    if (threadIdx.x < world) {
+        unsigned long long *dst = peers.p[threadIdx.x] + ((size_t)parity * kMaxPeers + rank) * kExchWords;
+        const unsigned long long w0 = tag | __float_as_uint(r.v1), w1 = tag | (unsigned)r.i1,
+                                 w2 = tag | __float_as_uint(r.v2);
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(w0) : "memory");
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + 1), "l"(w1) : "memory");
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + 2), "l"(w2) : "memory");
+    }
+    if (threadIdx.x < world) {
+        const unsigned long long *src = mine + ((size_t)parity * kMaxPeers + threadIdx.x) * kExchWords;
+        unsigned long long w[3];
+        bool ok = true;
+        uint64_t t0;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+        for (int k = 0; k < 3 && ok; ++k) {
+            for (;;) {
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[k]) : "l"(src + k) : "memory");
+                if ((unsigned)(w[k] >> 32) == epoch) break;
+                uint64_t now;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+                if (now - t0 > kExchWaitNs) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        Top2 u{-INFINITY, 0x7fffffff, -INFINITY};
+        if (ok) {
+            u.v1 = __uint_as_float((unsigned)w[0]);
+            u.i1 = (int)(unsigned)w[1];
+            u.v2 = __uint_as_float((unsigned)w[2]);
+        } else {
+            atomicOr(err, 8);
+        }
+        ranks[threadIdx.x] = u;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        Top2 g = ranks[0];
+        for (int k = 1; k < world; ++k) g = top2_merge(g, ranks[k]);
+        const int tok = (g.i1 >= 0 && g.i1 < 0x7fffffff) ? g.i1 : 0;
+        const int gi = st->gen_index;
+        out_tokens[gi] = tok;
+        out_margins[gi] = g.v1 - g.v2;
+        st->gen_index = gi + 1;
+        st->cur_token = tok;
+        st->pos = st->pos + 1;
+        st->epoch = epoch;
+        *counter = 0;
+    }
+}
+
 // Prompt phase: the next prompt token becomes the input at the next position.
 __global__ void prompt_advance_kernel(DecState *st, const int *prompt) {
     pdl_trigger();
@@ -518,6 +623,14 @@ struct sapphire_decoder {
     float *out_margins = nullptr;
     std::vector<void *> allocations;
 
+    // Sharded LM head (context with world > 1): exchange buffers and the
+    // number of generated steps so far (the next step's epoch - 1).
+    bool sharded = false;
+    void *exch_local = nullptr;
+    void *exch_peers[kMaxPeers] = {};
+    unsigned epochs = 0;
+    float *logits_all = nullptr;    // [world * ceil(vocab / world)] gathered logits (last_logits)
+
     cudaGraphExec_t g_prompt = nullptr, g_gen = nullptr;
     int launches_prompt = 0, launches_gen = 0;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
@@ -549,7 +662,10 @@ int upload_floats(sapphire_decoder_t *d, float **dst, const float *src, size_t n
 
 // A Q4_0 tensor over the concatenation of `parts` (rows back to back),
 // uploaded to the context.
-tensor_t *concat_q4(sapphire_decoder_t *d, const std::vector<std::pair<const void *, int>> &parts, int cols) {
+// Every rank of a sharded context holds the whole weight unless `whole` is
+// false (the LM head, whose rows are sharded).
+tensor_t *concat_q4(sapphire_decoder_t *d, const std::vector<std::pair<const void *, int>> &parts, int cols,
+                    bool whole = true) {
     const size_t rb = sapphire_row_bytes_internal(DTYPE_Q4_0, cols);
     int rows = 0;
     for (auto &p : parts) rows += p.second;
@@ -571,11 +687,11 @@ tensor_t *concat_q4(sapphire_decoder_t *d, const std::vector<std::pair<const voi
         return nullptr;
     }
     d->tensors.push_back(t);
-    if (kernel_tensor_upload(d->ctx, t) != 0) return nullptr;
+    if (!ctx_weight(d->ctx, t, whole)) return nullptr;
     return t;
 }
 
-const DevWeight *weight_of(sapphire_decoder_t *d, tensor_t *t) { return ctx_weight(d->ctx, t); }
+const DevWeight *weight_of(sapphire_decoder_t *d, tensor_t *t) { return ctx_weight(d->ctx, t, t != d->lm_head); }
 
 // The reference's table (rope_precompute_freqs, src/transformer/rope.c:19-37):
 // half-split storage, cos / sin of pos * base^(-2m/d) in float.
@@ -664,9 +780,18 @@ int enqueue_step(sapphire_decoder_t *d, bool generate, cudaStream_t st) {
         const DevWeight *head = weight_of(d, d->lm_head);
         if (!head) return -1;
         if (launch_gemv_best(ctx, *head, d->norm, d->logits, st)) return -1;
-        launch_pdl(argmax_advance_kernel, dim3(kArgmaxBlocks), dim3(kArgmaxThreads), 0, st, (const float *)d->logits,
-                   c.vocab, reinterpret_cast<Top2 *>(d->top2_part), d->counters + 1, d->state, d->out_tokens,
-                   d->out_margins);
+        if (d->sharded) {
+            PeerSlots peers{};
+            for (int k = 0; k < ctx->world; ++k) peers.p[k] = static_cast<unsigned long long *>(d->exch_peers[k]);
+            launch_pdl(argmax_sharded_kernel, dim3(kArgmaxBlocks), dim3(kArgmaxThreads), 0, st,
+                       (const float *)d->logits, head->nrows, head->row0, reinterpret_cast<Top2 *>(d->top2_part),
+                       d->counters + 1, d->state, d->out_tokens, d->out_margins, peers, ctx->world, ctx->rank,
+                       (const unsigned long long *)d->exch_local, ctx->d_err);
+        } else {
+            launch_pdl(argmax_advance_kernel, dim3(kArgmaxBlocks), dim3(kArgmaxThreads), 0, st,
+                       (const float *)d->logits, c.vocab, reinterpret_cast<Top2 *>(d->top2_part), d->counters + 1,
+                       d->state, d->out_tokens, d->out_margins);
+        }
         if (check_launch(d, "argmax")) return -1;
         launches += 3;
     } else {
@@ -704,7 +829,7 @@ int capture(sapphire_decoder_t *d, bool generate, cudaGraphExec_t *exec, int *la
 }
 
 int set_state(sapphire_decoder_t *d, int first_token, int n_prompt, cudaStream_t st) {
-    DecState s{0, first_token, 0, n_prompt, 0};
+    DecState s{0, first_token, 0, n_prompt, 0, d->epochs};
     CUDA_TRY(d->ctx, cudaMemcpyAsync(d->state, &s, sizeof s, cudaMemcpyHostToDevice, st));
     return 0;
 }
@@ -724,6 +849,7 @@ extern "C" SAPPHIRE_API void sapphire_decoder_destroy(sapphire_decoder_t *d) {
         for (cudaEvent_t e : d->ev)
             if (e) cudaEventDestroy(e);
         for (void *p : d->allocations) cudaFree(p);
+        if (d->exch_local) shard_unmap_buffers(d->ctx, d->exch_local, d->exch_peers);
         if (prev >= 0) cudaSetDevice(prev);
     }
     for (tensor_t *t : d->tensors) tensor_release(t);   // drops the device copies
@@ -747,8 +873,8 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
         return nullptr;
     }
     std::lock_guard<std::recursive_mutex> lk(ctx->exec_mutex);
-    if (!ctx->initialized || ctx->world > 1) {
-        ctx_fail(ctx, "sapphire_decoder_create", "needs an initialized, unsharded context");
+    if (!ctx->initialized || ctx->world > kMaxPeers) {
+        ctx_fail(ctx, "sapphire_decoder_create", "needs an initialized context of at most %d ranks", kMaxPeers);
         return nullptr;
     }
     int prev = -1;
@@ -757,6 +883,7 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
     sapphire_decoder_t *d = new sapphire_decoder();
     d->ctx = ctx;
     d->cfg = c;
+    d->sharded = ctx->world > 1;
     d->q_dim = c.heads * c.head_dim;
     d->kv_dim = c.kv_heads * c.head_dim;
     bool ok = false;
@@ -794,7 +921,15 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
                      kDirectMaxTiles * 32);
             break;
         }
-        if (!(d->lm_head = concat_q4(d, {{w->lm_head, c.vocab}}, c.hidden))) break;
+        if (!(d->lm_head = concat_q4(d, {{w->lm_head, c.vocab}}, c.hidden, !d->sharded))) break;
+        if (d->sharded) {
+            // Collective: every rank creates its decoder at the same point.
+            if (shard_map_buffers(ctx, (size_t)2 * kMaxPeers * kExchWords * sizeof(unsigned long long),
+                                  &d->exch_local, d->exch_peers))
+                break;
+            const size_t per = ((size_t)c.vocab + ctx->world - 1) / ctx->world;
+            if (dev_alloc(d, (void **)&d->logits_all, per * (ctx->world + 1) * sizeof(float))) break;
+        }
         if (upload_floats(d, &d->w_final, w->final_norm, c.hidden)) break;
         const size_t emb = (size_t)c.vocab * c.hidden;
         if (dev_alloc(d, (void **)&d->embed, emb * 2)) break;
@@ -843,6 +978,7 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
         // One eager pass of each step kind (also checks every launch), then capture.
         cudaStream_t st = ctx->stream;
         if (set_state(d, 0, 1, st) || enqueue_step(d, false, st) < 0 || enqueue_step(d, true, st) < 0) break;
+        d->epochs += 1;
         if (cudaStreamSynchronize(st) != cudaSuccess || check_kernel_error(ctx, "sapphire_decoder_create")) {
             ctx_fail(ctx, "sapphire_decoder_create", "warm-up step failed");
             break;
@@ -912,6 +1048,7 @@ extern "C" SAPPHIRE_API int sapphire_decoder_generate(sapphire_decoder_t *d, con
             ctx_fail(ctx, "sapphire_decoder_generate", "GPU execution failed: %s", cudaGetErrorString(e));
             break;
         }
+        d->epochs += (unsigned)n_gen;
         if (check_kernel_error(ctx, "sapphire_decoder_generate")) break;
         cudaEventElapsedTime(&d->last_prompt_ms, d->ev[0], d->ev[1]);
         cudaEventElapsedTime(&d->last_gen_ms, d->ev[1], d->ev[2]);
@@ -928,7 +1065,22 @@ extern "C" SAPPHIRE_API int sapphire_decoder_last_logits(sapphire_decoder_t *d, 
     int prev = -1;
     cudaGetDevice(&prev);
     cudaSetDevice(d->ctx->device);
-    cudaError_t e = cudaMemcpyAsync(out, d->logits, (size_t)d->cfg.vocab * 4, cudaMemcpyDefault, d->ctx->stream);
+    const float *src = d->logits;
+    cudaError_t e = cudaSuccess;
+    if (d->sharded) {
+        // Collective: the slices of every rank, all-gathered (NCCL).
+        kernel_context_t *ctx = d->ctx;
+        const size_t per = ((size_t)d->cfg.vocab + ctx->world - 1) / ctx->world;
+        const DevWeight *head = weight_of(d, d->lm_head);
+        float *send = d->logits_all + per * ctx->world;
+        e = cudaMemsetAsync(send, 0, per * sizeof(float), ctx->stream);
+        if (e == cudaSuccess && head && head->nrows > 0)
+            e = cudaMemcpyAsync(send, d->logits, (size_t)head->nrows * sizeof(float), cudaMemcpyDeviceToDevice,
+                                ctx->stream);
+        if (e == cudaSuccess && shard_allgather(ctx, send, d->logits_all, per, ctx->stream)) e = cudaErrorUnknown;
+        src = d->logits_all;
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, src, (size_t)d->cfg.vocab * 4, cudaMemcpyDefault, d->ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(d->ctx->stream);
     if (prev >= 0) cudaSetDevice(prev);
     if (e != cudaSuccess) {

@@ -174,8 +174,10 @@ kernel_context_t *default_context();
 // Grow a device scratch buffer (on ctx's device) to at least `bytes`.
 int ensure_scratch(kernel_context_t *ctx, float **buf, size_t *cap, size_t bytes);
 
-// Device copy of A for ctx (uploads on first use).  nullptr on error.
-const DevWeight *ctx_weight(kernel_context_t *ctx, const tensor_t *A);
+// Device copy of A for ctx (uploads on first use).  On a sharded context the
+// copy holds the rank's rows, or every row when `whole` (weights a decoder
+// replicates on every rank).  nullptr on error.
+const DevWeight *ctx_weight(kernel_context_t *ctx, const tensor_t *A, bool whole = false);
 
 // Logical (rows, cols) of a 2-D tensor; false if not a usable 2-D tensor.
 bool weight_shape(const tensor_t *A, int *rows, int *cols);
@@ -286,6 +288,12 @@ int launch_gemm_tc_bf16(kernel_context_t *ctx, const DevWeight &w, const void *x
 int shard_allgather(kernel_context_t *ctx, const float *send, float *recv, size_t count,
                     cudaStream_t stream);
 void shard_destroy(kernel_context_t *ctx);
+// Collective over the ranks of a sharded context: allocates `bytes` of zeroed
+// device memory on this rank and maps every rank's allocation (CUDA IPC,
+// handles exchanged over NCCL); peers[k] is rank k's (peers[rank] = *local).
+// 0 when every rank mapped every peer, else -1 on every rank.
+int shard_map_buffers(kernel_context_t *ctx, size_t bytes, void **local, void **peers);
+void shard_unmap_buffers(kernel_context_t *ctx, void *local, void **peers);
 // Batch-1 sharded product gathered over peer memory into y[0, rows): true if
 // it ran (every rank decides the same from the arguments); false means use the
 // NCCL path.  -1 through *rc on error.

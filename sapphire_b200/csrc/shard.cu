@@ -219,6 +219,35 @@ int nccl_allgather_bytes(kernel_context_t *ctx, const void *mine, void *all, siz
     return rc;
 }
 
+// Collective mapping of one device allocation per rank into every rank.
+int map_buffers(kernel_context_t *ctx, size_t bytes, void **local, void **peers) {
+    for (int k = 0; k < kMaxPeers; ++k) peers[k] = nullptr;
+    *local = nullptr;
+    if (ctx->world > kMaxPeers) return -1;
+    int ok = 1;
+    cudaIpcMemHandle_t mine{};
+    if (cudaMalloc(local, bytes) != cudaSuccess || cudaMemset(*local, 0, bytes) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&mine, *local) != cudaSuccess)
+        ok = 0;
+    cudaGetLastError();
+    std::vector<cudaIpcMemHandle_t> all(ctx->world);
+    if (nccl_allgather_bytes(ctx, &mine, all.data(), sizeof mine)) return -1;
+    for (int k = 0; k < ctx->world && ok; ++k) {
+        if (k == ctx->rank) {
+            peers[k] = *local;
+        } else if (cudaIpcOpenMemHandle(&peers[k], all[k], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            peers[k] = nullptr;
+            ok = 0;
+        }
+    }
+    cudaGetLastError();
+    std::vector<int> oks(ctx->world, 0);
+    if (nccl_allgather_bytes(ctx, &ok, oks.data(), sizeof ok)) return -1;
+    for (int v : oks)
+        if (v != 1) return -1;
+    return 0;
+}
+
 // Collective: every rank of the group calls it at the same product.  The
 // gather is used only if every rank mapped every peer (agreed over NCCL).
 void peer_gather_setup(kernel_context_t *ctx) {
@@ -366,4 +395,27 @@ extern "C" SAPPHIRE_API int sapphire_test_pull_expiry(kernel_context_t *ctx, flo
     cudaGetLastError();
     if (prev >= 0) cudaSetDevice(prev);
     return rc;
+}
+
+int shard_map_buffers(kernel_context_t *ctx, size_t bytes, void **local, void **peers) {
+    if (!ctx->nccl_comm) {
+        ctx_fail(ctx, "shard_map_buffers", "context has no communicator");
+        return -1;
+    }
+    if (map_buffers(ctx, bytes, local, peers)) {
+        shard_unmap_buffers(ctx, *local, peers);
+        *local = nullptr;
+        ctx_fail(ctx, "shard_map_buffers", "not every rank could map every peer's memory");
+        return -1;
+    }
+    return 0;
+}
+
+void shard_unmap_buffers(kernel_context_t *ctx, void *local, void **peers) {
+    for (int k = 0; k < kMaxPeers; ++k) {
+        if (peers[k] && k != ctx->rank) cudaIpcCloseMemHandle(peers[k]);
+        peers[k] = nullptr;
+    }
+    if (local) cudaFree(local);
+    cudaGetLastError();
 }

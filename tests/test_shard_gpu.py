@@ -5,12 +5,18 @@ Each rank binds its context to its GPU, joins the NCCL group (unique id from
 rank 0, passed over a gloo group), and runs the same calls an unsharded
 context would: every rank receives the full result, which must match the
 oracle (the reference row kernels) within the GEMV bar and be the same bytes
-on both ranks.  Batch-1 products of the pipelined GEMV are gathered over peer
-memory (NVLink stores and an epoch-flag barrier); batched products over NCCL.
+on both ranks.  Batch-1 products of the streaming GEMV are gathered over peer
+memory inside the GEMV (epoch-tagged NVLink stores); batched products over
+NCCL.  Then the Gemma-3-270M decode runs with its LM head row-sharded: each
+rank reduces its logits slice to (value, index) pairs exchanged over peer
+memory, and both ranks must emit the reference decode's 64 greedy ids (twice:
+the exchange's epochs carry over between requests) with the same margins;
+the gathered logits (the parity mode) must peak at the last id.
 """
 from __future__ import annotations
 
 import multiprocessing as mp
+import os
 import socket
 
 import numpy as np
@@ -89,7 +95,28 @@ def _rank_main(rank, world, port, out):
                 ref = o.gemv(dtype, packed, rows, cols, Xr)
                 err = float(np.max(np.abs(Y - ref)) / np.max(np.abs(ref)))
                 results.append((dtype, rows, batch, same, err))
+        # Gemma-3-270M decode with the LM head row-sharded: every rank runs the
+        # layers, computes its slice of the logits and exchanges (value, index)
+        # pairs; both ranks must produce the reference decode's greedy ids.
+        from sapphire_b200 import workloads
+        from sapphire_b200.decode import Decoder
+        cfg = workloads.C3
+        model = workloads.make_decode_model(cfg, lambda a: sp.quantize(ctx, 3, a), seed=0)
+        dec = Decoder(ctx, cfg, model)
+        ids, margins = dec.generate(model["prompt"], cfg.generate)
+        ids2, _ = dec.generate(model["prompt"], cfg.generate)          # a second request, epochs continue
+        logits = dec.last_logits()                                    # collective: gathered slices
+        dec.close()
+        golden = np.load(os.path.join(ROOT, "tests", "golden", "decode_gemma3_270m_seed0.npz"))
+        dec_ok = bool(np.array_equal(ids, golden["tokens"]) and np.array_equal(ids2, ids))
+        top = int(np.argmax(logits))
+        mine_ids = torch.from_numpy(ids.astype(np.int64))
+        all_ids = [torch.zeros_like(mine_ids) for _ in range(world)]
+        dist.all_gather(all_ids, mine_ids)
+        dec_same = all(torch.equal(all_ids[0], t) for t in all_ids)
         if rank == 0:
+            results.append(("decode", dec_ok, dec_same, top == int(ids[-1]),
+                            float(np.max(np.abs(margins - golden["margins"])))))
             out.put(results)
     finally:
         if ctx is not None:
@@ -118,7 +145,10 @@ def test_sharded_products_two_gpus():
             p.kill()
     assert codes == [0] * world, codes
     results = out.get(timeout=10)
-    assert len(results) == len(CASES)
-    for dtype, rows, batch, same, err in results:
+    assert len(results) == len(CASES) + 1
+    for dtype, rows, batch, same, err in results[:-1]:
         assert same, (dtype, rows, batch)
         assert err < GEMV_RTOL, (dtype, rows, batch, err)
+    _, dec_ok, dec_same, last_is_argmax, margin_err = results[-1]
+    assert dec_ok and dec_same and last_is_argmax, results[-1]
+    assert margin_err < 2e-3, margin_err
