@@ -103,6 +103,13 @@ _SIGNATURES = {
     "kernel_ctx_shard_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32)]),
     "sapphire_test_stream_unarmed": (i32, [i32]),
     "sapphire_test_pull_expiry": (i32, [vp, vp, C.c_longlong, C.c_ulonglong]),
+    # include/sapphire_safetensors.h
+    "sapphire_safetensors_open": (vp, [C.c_char_p]),
+    "sapphire_safetensors_count": (i32, [vp]),
+    "sapphire_safetensors_name": (C.c_char_p, [vp, i32]),
+    "sapphire_safetensors_tensor": (vp, [vp, C.c_char_p]),
+    "sapphire_safetensors_close": (None, [vp]),
+    "sapphire_decoder_create_from_safetensors": (vp, [vp, vp, vp]),
     # include/sapphire_decode.h
     "sapphire_decoder_create": (vp, [vp, vp, vp]),
     "sapphire_decoder_generate": (i32, [vp, vp, i32, i32, vp, vp]),

@@ -41,6 +41,7 @@
 
 #include "internal.cuh"
 #include "../../include/sapphire_decode.h"
+#include "../../include/sapphire_safetensors.h"
 
 namespace {
 
@@ -1099,4 +1100,102 @@ extern "C" SAPPHIRE_API int sapphire_decoder_last_times(sapphire_decoder_t *d, f
 
 extern "C" SAPPHIRE_API int sapphire_decoder_launches_per_token(sapphire_decoder_t *d) {
     return d ? d->launches_gen : -1;
+}
+
+// ------------------------------------------------- model from a file ------
+// Names as the reference's tensor map (src/loader/gemma3_map.c).
+namespace {
+const void *st_data(sapphire_safetensors_t *st, const std::string &name, tensor_dtype_t dt, int rows, int cols,
+                    kernel_context_t *ctx) {
+    tensor_t *t = sapphire_safetensors_tensor(st, name.c_str());
+    if (!t) {
+        ctx_fail(ctx, "sapphire_decoder_create_from_safetensors", "tensor '%s' missing", name.c_str());
+        return nullptr;
+    }
+    const int *sh = tensor_shape(t);
+    if (tensor_dtype(t) != dt || tensor_ndim(t) != 2 || sh[0] != rows || sh[1] != cols) {
+        ctx_fail(ctx, "sapphire_decoder_create_from_safetensors", "tensor '%s' is not %s [%d, %d]", name.c_str(),
+                 dtype_name(dt), rows, cols);
+        return nullptr;
+    }
+    return tensor_data(t);
+}
+
+// A norm vector as fp32 in `out` (zeros when absent); false on a bad tensor.
+bool st_norm(sapphire_safetensors_t *st, const std::string &name, int n, std::vector<float> &out,
+             kernel_context_t *ctx) {
+    out.assign((size_t)n, 0.0f);
+    tensor_t *t = sapphire_safetensors_tensor(st, name.c_str());
+    if (!t) return true;
+    if (tensor_ndim(t) != 1 || tensor_shape(t)[0] != n ||
+        (tensor_dtype(t) != DTYPE_F32 && tensor_dtype(t) != DTYPE_BF16)) {
+        ctx_fail(ctx, "sapphire_decoder_create_from_safetensors", "norm '%s' is not F32 or BF16 [%d]", name.c_str(),
+                 n);
+        return false;
+    }
+    if (tensor_dtype(t) == DTYPE_F32) {
+        memcpy(out.data(), tensor_data(t), (size_t)n * sizeof(float));
+    } else {
+        const uint16_t *b = static_cast<const uint16_t *>(tensor_data(t));
+        for (int i = 0; i < n; ++i) {
+            const uint32_t bits = (uint32_t)b[i] << 16;
+            memcpy(&out[i], &bits, sizeof bits);
+        }
+    }
+    return true;
+}
+}  // namespace
+
+extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create_from_safetensors(
+    kernel_context_t *ctx, const sapphire_gemma3_config_t *cfg, sapphire_safetensors_t *st) {
+    if (!ctx || !cfg || !st) {
+        LOG_ERROR("NULL argument");
+        return nullptr;
+    }
+    const sapphire_gemma3_config_t &c = *cfg;
+    if (c.layers <= 0 || c.hidden <= 0 || c.ffn <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.head_dim <= 0 ||
+        c.vocab <= 0) {
+        ctx_fail(ctx, "sapphire_decoder_create_from_safetensors", "invalid model shape");
+        return nullptr;
+    }
+    const int qd = c.heads * c.head_dim, kvd = c.kv_heads * c.head_dim;
+    std::vector<const void *> proj((size_t)7 * c.layers);
+    std::vector<std::vector<float>> norm_store((size_t)6 * c.layers + 1);
+    std::vector<const float *> norms((size_t)6 * c.layers);
+    for (int l = 0; l < c.layers; ++l) {
+        const std::string p = "model.layers." + std::to_string(l) + ".";
+        const struct {
+            const char *name;
+            int rows, cols;
+        } pr[7] = {{"self_attn.q_proj.weight", qd, c.hidden},   {"self_attn.k_proj.weight", kvd, c.hidden},
+                   {"self_attn.v_proj.weight", kvd, c.hidden},  {"self_attn.o_proj.weight", c.hidden, qd},
+                   {"mlp.gate_proj.weight", c.ffn, c.hidden},   {"mlp.up_proj.weight", c.ffn, c.hidden},
+                   {"mlp.down_proj.weight", c.hidden, c.ffn}};
+        for (int k = 0; k < 7; ++k)
+            if (!(proj[(size_t)7 * l + k] = st_data(st, p + pr[k].name, DTYPE_Q4_0, pr[k].rows, pr[k].cols, ctx)))
+                return nullptr;
+        const struct {
+            const char *name;
+            int n;
+        } nr[6] = {{"input_layernorm.weight", c.hidden},           {"post_attention_layernorm.weight", c.hidden},
+                   {"pre_feedforward_layernorm.weight", c.hidden}, {"post_feedforward_layernorm.weight", c.hidden},
+                   {"self_attn.q_norm.weight", c.head_dim},        {"self_attn.k_norm.weight", c.head_dim}};
+        for (int k = 0; k < 6; ++k) {
+            std::vector<float> &v = norm_store[(size_t)6 * l + k];
+            if (!st_norm(st, p + nr[k].name, nr[k].n, v, ctx)) return nullptr;
+            norms[(size_t)6 * l + k] = v.data();
+        }
+    }
+    std::vector<float> &final_norm = norm_store.back();
+    if (!st_norm(st, "model.norm.weight", c.hidden, final_norm, ctx)) return nullptr;
+    const void *embed = st_data(st, "model.embed_tokens.weight", DTYPE_BF16, c.vocab, c.hidden, ctx);
+    const void *head = embed ? st_data(st, "lm_head.weight", DTYPE_Q4_0, c.vocab, c.hidden, ctx) : nullptr;
+    if (!embed || !head) return nullptr;
+    sapphire_gemma3_weights_t w{};
+    w.embed_bf16 = static_cast<const uint16_t *>(embed);
+    w.lm_head = head;
+    w.final_norm = final_norm.data();
+    w.proj = proj.data();
+    w.norms = norms.data();
+    return sapphire_decoder_create(ctx, cfg, &w);
 }

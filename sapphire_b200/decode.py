@@ -35,6 +35,19 @@ class Decoder:
         if not self.handle:
             raise SapphireError(f"sapphire_decoder_create failed: {ctx.last_error}")
 
+    @classmethod
+    def from_safetensors(cls, ctx, cfg, st):
+        """A decoder loaded from a quantized safetensors file
+        (sapphire_decoder_create_from_safetensors); `st` is a
+        safetensors.SafeTensors, which may be closed afterwards."""
+        self = cls.__new__(cls)
+        self.ctx, self.cfg = ctx, cfg
+        c = config_struct(cfg)
+        self.handle = lib.sapphire_decoder_create_from_safetensors(ctx.handle, C.byref(c), st.handle)
+        if not self.handle:
+            raise SapphireError(f"sapphire_decoder_create_from_safetensors failed: {ctx.last_error}")
+        return self
+
     def generate(self, prompt, n_gen: int):
         """(generated ids int32 [n_gen], top-1 minus top-2 margins f32 [n_gen])."""
         p = np.ascontiguousarray(prompt, dtype=np.int32)

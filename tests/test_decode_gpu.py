@@ -8,6 +8,7 @@ greedy tokens.  The GPU decoder must produce the same 64 ids.
 """
 from __future__ import annotations
 
+import dataclasses
 import os
 
 import numpy as np
@@ -77,3 +78,44 @@ def test_generate_rejects_bad_input(sp, decoder):
         dec.generate(np.array([cfg.vocab], dtype=np.int32), 1)
     with pytest.raises(sp.SapphireError):
         dec.generate(model["prompt"], cfg.context)
+
+
+def test_decoder_from_quantized_safetensors(sp, ctx, decoder, golden, tmp_path):
+    """The same model written as a quantized safetensors file (Q4_0
+    projections and LM head under the reference's tensor names) loads through
+    sapphire_decoder_create_from_safetensors and decodes the reference's ids."""
+    from sapphire_b200 import safetensors
+    from sapphire_b200.decode import Decoder
+    cfg, model, _ = decoder
+    path = str(tmp_path / "gemma3_q4_0.safetensors")
+    safetensors.save_decode_model(path, cfg, model)
+    with safetensors.SafeTensors(path) as st:
+        assert st.info("lm_head.weight")[:2] == ("Q4_0", (cfg.vocab, cfg.hidden))
+        dec = Decoder.from_safetensors(ctx, cfg, st)
+    # The file is closed: everything the decoder uses lives on the GPU.
+    os.remove(path)
+    try:
+        ids, _ = dec.generate(model["prompt"], cfg.generate)
+        assert np.array_equal(ids, golden["tokens"])
+    finally:
+        dec.close()
+
+
+def test_from_safetensors_rejects_wrong_dtype(sp, ctx, decoder, tmp_path):
+    """An LM head stored as BF16 (the reference's tied-embedding layout) is not
+    a quantized product here: creation fails with the tensor named."""
+    from sapphire_b200 import safetensors
+    from sapphire_b200.decode import Decoder
+    cfg, model, _ = decoder
+    small = dataclasses.replace(cfg, layers=1)
+    path = str(tmp_path / "bad.safetensors")
+    t = {"model.embed_tokens.weight": ("BF16", (cfg.vocab, cfg.hidden), model["embed"]),
+         "lm_head.weight": ("BF16", (cfg.vocab, cfg.hidden), model["embed"])}
+    hf = {"q": "self_attn.q_proj", "k": "self_attn.k_proj", "v": "self_attn.v_proj", "o": "self_attn.o_proj",
+          "gate": "mlp.gate_proj", "up": "mlp.up_proj", "down": "mlp.down_proj"}
+    for name, rows, cols in small.projections():
+        t[f"model.layers.0.{hf[name]}.weight"] = ("Q4_0", (rows, cols), model["layers"][0][name])
+    safetensors.save(path, t)
+    with safetensors.SafeTensors(path) as st:
+        with pytest.raises(sp.SapphireError, match="lm_head.weight"):
+            Decoder.from_safetensors(ctx, small, st)
