@@ -381,6 +381,10 @@ int check_kernel_error(kernel_context_t *ctx, const char *who) {
     if (ctx->d_cnt && ctx->d_cnt_cap) cudaMemsetAsync(ctx->d_cnt, 0, ctx->d_cnt_cap, ctx->stream);
     if (bits & 8)
         ctx_fail(ctx, who, "a peer-memory gather gave up waiting for another rank's rows (bounded wait expired)");
+    else if (bits & 16)
+        ctx_fail(ctx, who, "a persistent decode step gave up waiting at a grid barrier (bounded wait expired)");
+    else if (bits == 4)
+        ctx_fail(ctx, who, "a token id outside the vocabulary reached the embedding");
     else
         ctx_fail(ctx, who, "a kernel gave up waiting for its asynchronous copies (bounded wait expired)");
     return -1;

@@ -36,10 +36,12 @@
 // generated step); a generation is a sequence of graph launches with no host
 // round trip.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
 #include "internal.cuh"
+#include "decode_common.cuh"
 #include "../../include/sapphire_decode.h"
 #include "../../include/sapphire_safetensors.h"
 
@@ -49,22 +51,8 @@ constexpr int kNormThreads = 256;
 constexpr int kAttnSplit = 32;        // CTAs per layer's attention
 static_assert(kAttnSplit == 32, "the combine maps one split to one warp lane");
 constexpr int kAttnThreads = 256;
-constexpr int kMaxGroup = 8;          // query heads per KV head
-constexpr int kMaxHeads = 32;
-constexpr int kMaxHeadDim = 256;
-constexpr int kMaxContext = 4096;
 constexpr int kArgmaxBlocks = 148;
 constexpr int kArgmaxThreads = 512;
-
-// Device-side step state.
-struct DecState {
-    int pos;            // position of the token being processed
-    int cur_token;      // token being processed
-    int prompt_index;   // index of cur_token in the prompt during the prompt phase
-    int n_prompt;
-    int gen_index;      // next output slot
-    unsigned epoch;     // sharded LM head: generated steps so far (tag of the exchange words)
-};
 
 // Sharded LM head: every rank's mapped exchange buffer, [2 parities][kMaxPeers
 // ranks][4 words] of (epoch << 32 | 32 bits).
@@ -73,29 +61,6 @@ struct PeerSlots {
 };
 constexpr int kExchWords = 4;
 constexpr unsigned long long kExchWaitNs = 2000000000ull;
-
-// ------------------------------------------------------------ reductions --
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-// Sum over the block (blockDim.x a multiple of 32, at most 1024); every thread
-// receives the result.  `red` holds 32 floats.
-__device__ float block_sum(float v, float *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    v = warp_sum(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = lane < nw ? red[lane] : 0.0f;
-    return warp_sum(t);
-}
 
 // out[i] = (in[i] * rms_inv) * (1 + w[i]),  rms_inv = 1 / sqrt(mean(in^2) + eps)
 // (rmsnorm_delta, src/transformer/normalization.c:103-116).  One block; in and
@@ -120,7 +85,7 @@ __global__ void embed_norm_kernel(const DecState *st, const uint16_t *__restrict
     __shared__ float red[32];
     int tok = st->cur_token;
     if (tok < 0 || tok >= vocab) {
-        if (threadIdx.x == 0) atomicOr(err, 4);
+        if (threadIdx.x == 0) atomicOr(err, kErrToken);
         tok = 0;
     }
     const uint16_t *row = embed + (size_t)tok * dim;
@@ -161,35 +126,6 @@ __global__ void residual_norm_kernel(const float *t, const float *w_post, float 
 // src/transformer/rope.c:65-80), and block 0 writes the new K and V rows;
 // the block whose range holds pos reads them from shared memory.
 constexpr int kSub = 16;
-
-// rmsnorm_delta of one head (hd values at x) then the half-split rotation, by
-// one warp; lane owns the pairs (i, i + hd/2) for i = lane + 32 j.
-__device__ __forceinline__ void warp_norm_rope(const float *x, const float *w, float eps, const float *cs,
-                                               const float *sn, int hd, float *dst) {
-    const int lane = threadIdx.x & 31, half = hd >> 1;
-    float a[kMaxHeadDim / 64], b[kMaxHeadDim / 64];
-    float ss = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kMaxHeadDim / 64; ++j) {
-        const int i = lane + 32 * j;
-        a[j] = i < half ? x[i] : 0.0f;
-        b[j] = i < half ? x[i + half] : 0.0f;
-        ss += a[j] * a[j] + b[j] * b[j];
-    }
-    ss = warp_sum(ss);
-    const float r = 1.0f / sqrtf(ss / (float)hd + eps);
-#pragma unroll
-    for (int j = 0; j < kMaxHeadDim / 64; ++j) {
-        const int i = lane + 32 * j;
-        if (i < half) {
-            const float y0 = (a[j] * r) * (1.0f + (w ? w[i] : 0.0f));
-            const float y1 = (b[j] * r) * (1.0f + (w ? w[i + half] : 0.0f));
-            const float c = cs[i], sv = sn[i];
-            dst[i] = y0 * c - y1 * sv;
-            dst[i + half] = y1 * c + y0 * sv;
-        }
-    }
-}
 
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     const DecState *st, const float *qkv, float *kcache, float *vcache, float *out, float *part, int *counter,
@@ -632,6 +568,16 @@ struct sapphire_decoder {
     unsigned epochs = 0;
     float *logits_all = nullptr;    // [world * ceil(vocab / world)] gathered logits (last_logits)
 
+    // Persistent step (decode_persistent.cu): used when the model fits its
+    // plan, unless SAPPHIRE_DECODE_PERSISTENT=0.  Projections live in its
+    // row layout only; the LM head stays a context weight.
+    bool persist = false;
+    bool coop = true;               // launched cooperatively (false: capture refused it)
+    PersistPlan plan;
+    PersistParams pp{};
+    uint8_t *wrows = nullptr;
+    unsigned *bar = nullptr;        // [0] arrivals, [1] exits, [2] abort flag
+
     cudaGraphExec_t g_prompt = nullptr, g_gen = nullptr;
     int launches_prompt = 0, launches_gen = 0;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
@@ -724,10 +670,47 @@ int check_launch(sapphire_decoder_t *d, const char *what) {
 
 // Enqueue one step: embedding, the layers and either the prompt advance or
 // the LM head + greedy argmax.  Returns the number of kernels, -1 on error.
+// The LM head and the greedy argmax of a generated step (the argmax advances
+// the state).  Returns the number of kernels, -1 on error.
+int enqueue_head(sapphire_decoder_t *d, cudaStream_t st) {
+    kernel_context_t *ctx = d->ctx;
+    const DevWeight *head = weight_of(d, d->lm_head);
+    if (!head) return -1;
+    if (launch_gemv_best(ctx, *head, d->norm, d->logits, st)) return -1;
+    if (d->sharded) {
+        PeerSlots peers{};
+        for (int k = 0; k < ctx->world; ++k) peers.p[k] = static_cast<unsigned long long *>(d->exch_peers[k]);
+        launch_pdl(argmax_sharded_kernel, dim3(kArgmaxBlocks), dim3(kArgmaxThreads), 0, st, (const float *)d->logits,
+                   head->nrows, head->row0, reinterpret_cast<Top2 *>(d->top2_part), d->counters + 1, d->state,
+                   d->out_tokens, d->out_margins, peers, ctx->world, ctx->rank, (const unsigned long long *)d->exch_local,
+                   ctx->d_err);
+    } else {
+        launch_pdl(argmax_advance_kernel, dim3(kArgmaxBlocks), dim3(kArgmaxThreads), 0, st, (const float *)d->logits,
+                   d->cfg.vocab, reinterpret_cast<Top2 *>(d->top2_part), d->counters + 1, d->state, d->out_tokens,
+                   d->out_margins);
+    }
+    if (check_launch(d, "argmax")) return -1;
+    return 2;
+}
+
 int enqueue_step(sapphire_decoder_t *d, bool generate, cudaStream_t st) {
     const sapphire_gemma3_config_t &c = d->cfg;
     kernel_context_t *ctx = d->ctx;
     int launches = 0;
+    if (d->persist) {
+        // One persistent kernel for the layers (and the prompt advance or the
+        // final norm), then the LM head and the argmax.
+        d->pp.generate = generate ? 1 : 0;
+        cudaError_t e = launch_persist(d->plan, d->pp, d->coop, st);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            ctx_fail(ctx, "sapphire_decoder", "persistent step launch failed: %s", cudaGetErrorString(e));
+            return -1;
+        }
+        if (!generate) return 1;
+        const int h = enqueue_head(d, st);
+        return h < 0 ? -1 : 1 + h;
+    }
     const float eps = c.rms_eps;
     const float emb_scale = sqrtf((float)c.hidden);
     const float att_scale = 1.0f / sqrtf(c.query_pre_attn_scalar > 0.0f ? c.query_pre_attn_scalar : (float)c.head_dim);
@@ -778,23 +761,9 @@ int enqueue_step(sapphire_decoder_t *d, bool generate, cudaStream_t st) {
                    (const float *)d->layers[c.layers - 1].w_ffn_post, cur, (const float *)d->w_final, d->norm,
                    c.hidden, eps);
         if (check_launch(d, "final norm")) return -1;
-        const DevWeight *head = weight_of(d, d->lm_head);
-        if (!head) return -1;
-        if (launch_gemv_best(ctx, *head, d->norm, d->logits, st)) return -1;
-        if (d->sharded) {
-            PeerSlots peers{};
-            for (int k = 0; k < ctx->world; ++k) peers.p[k] = static_cast<unsigned long long *>(d->exch_peers[k]);
-            launch_pdl(argmax_sharded_kernel, dim3(kArgmaxBlocks), dim3(kArgmaxThreads), 0, st,
-                       (const float *)d->logits, head->nrows, head->row0, reinterpret_cast<Top2 *>(d->top2_part),
-                       d->counters + 1, d->state, d->out_tokens, d->out_margins, peers, ctx->world, ctx->rank,
-                       (const unsigned long long *)d->exch_local, ctx->d_err);
-        } else {
-            launch_pdl(argmax_advance_kernel, dim3(kArgmaxBlocks), dim3(kArgmaxThreads), 0, st,
-                       (const float *)d->logits, c.vocab, reinterpret_cast<Top2 *>(d->top2_part), d->counters + 1,
-                       d->state, d->out_tokens, d->out_margins);
-        }
-        if (check_launch(d, "argmax")) return -1;
-        launches += 3;
+        const int h = enqueue_head(d, st);
+        if (h < 0) return -1;
+        launches += 1 + h;
     } else {
         launch_pdl(prompt_advance_kernel, dim3(1), dim3(1), 0, st, d->state, (const int *)d->prompt);
         if (check_launch(d, "prompt advance")) return -1;
@@ -890,14 +859,84 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
     bool ok = false;
     do {
         d->layers.resize(c.layers);
+        // The persistent step when the model fits it.
+        PersistParams &pp = d->pp;
+        pp.layers = c.layers;
+        pp.hidden = c.hidden;
+        pp.ffn = c.ffn;
+        pp.heads = c.heads;
+        pp.kv_heads = c.kv_heads;
+        pp.hd = c.head_dim;
+        pp.context = c.context;
+        pp.vocab = c.vocab;
+        pp.window = c.sliding_window > 0 ? c.sliding_window : 1024;
+        pp.norm_stride = 4 * c.hidden + 2 * c.head_dim;
+        const int stage_shape[kNumStages][2] = {
+            {d->q_dim + 2 * d->kv_dim, c.hidden}, {c.hidden, d->q_dim}, {2 * c.ffn, c.hidden}, {c.hidden, c.ffn}};
+        unsigned long long lb = 0;
+        for (int s = 0; s < kNumStages; ++s) {
+            pp.stage_rows[s] = stage_shape[s][0];
+            pp.stage_nb[s] = (stage_shape[s][1] + 31) / 32;
+            pp.stage_stride[s] = (pp.stage_nb[s] * 20 + 15) / 16 * 16;
+            pp.stage_off[s] = lb;
+            lb += (unsigned long long)pp.stage_rows[s] * pp.stage_stride[s];
+        }
+        pp.layer_bytes = lb;
+        {
+            const char *why = nullptr;
+            const char *env = getenv("SAPPHIRE_DECODE_PERSISTENT");
+            d->plan = persist_plan(ctx->device, pp, &why);
+            d->persist = d->plan.ok && !(env && strcmp(env, "0") == 0);
+            if (!d->plan.ok) LOG_INFO("decoder: one kernel per stage (persistent step does not fit: %s)", why);
+        }
+        bool null_proj = false;
+        for (int k = 0; k < 7 * c.layers; ++k) null_proj = null_proj || !w->proj[k];
+        if (null_proj) {
+            ctx_fail(ctx, "sapphire_decoder_create", "a projection pointer is NULL");
+            break;
+        }
+        if (d->persist) {
+            // Projections in the persistent step's row layout: per row the nb
+            // blocks' 16 code bytes, then their nb fp32 scales.
+            std::vector<uint8_t> rows((size_t)lb * c.layers, 0);
+            for (int l = 0; l < c.layers; ++l) {
+                const void *const *p = w->proj + 7 * l;
+                const std::vector<std::pair<const void *, int>> parts[kNumStages] = {
+                    {{p[0], d->q_dim}, {p[1], d->kv_dim}, {p[2], d->kv_dim}},
+                    {{p[3], c.hidden}},
+                    {{p[4], c.ffn}, {p[5], c.ffn}},
+                    {{p[6], c.hidden}}};
+                for (int s = 0; s < kNumStages; ++s) {
+                    const int nb = pp.stage_nb[s], stride = pp.stage_stride[s];
+                    const size_t src_rb = sapphire_row_bytes_internal(DTYPE_Q4_0, stage_shape[s][1]);
+                    uint8_t *dst = rows.data() + (size_t)l * lb + pp.stage_off[s];
+                    for (const auto &part : parts[s]) {
+                        const uint8_t *src = static_cast<const uint8_t *>(part.first);
+                        for (int r = 0; r < part.second; ++r, dst += stride, src += src_rb) {
+                            for (int b = 0; b < nb; ++b) {
+                                memcpy(dst + 16 * b, src + 20 * b + 4, 16);
+                                memcpy(dst + 16 * nb + 4 * b, src + 20 * b, 4);
+                            }
+                        }
+                    }
+                }
+            }
+            if (dev_alloc(d, (void **)&d->wrows, rows.size()) ||
+                cudaMemcpy(d->wrows, rows.data(), rows.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+                ctx_fail(ctx, "sapphire_decoder_create", "projection upload failed");
+                break;
+            }
+        }
         for (int l = 0; l < c.layers; ++l) {
             const void *const *p = w->proj + 7 * l;
             sapphire_decoder::Layer &L = d->layers[l];
             L.global = c.global_mask ? ((c.global_mask >> l) & 1ULL) != 0 : ((l + 1) % 6 == 0);
-            if (!(L.qkv = concat_q4(d, {{p[0], d->q_dim}, {p[1], d->kv_dim}, {p[2], d->kv_dim}}, c.hidden))) break;
-            if (!(L.o = concat_q4(d, {{p[3], c.hidden}}, d->q_dim))) break;
-            if (!(L.gu = concat_q4(d, {{p[4], c.ffn}, {p[5], c.ffn}}, c.hidden))) break;
-            if (!(L.down = concat_q4(d, {{p[6], c.hidden}}, c.ffn))) break;
+            if (!d->persist) {
+                if (!(L.qkv = concat_q4(d, {{p[0], d->q_dim}, {p[1], d->kv_dim}, {p[2], d->kv_dim}}, c.hidden))) break;
+                if (!(L.o = concat_q4(d, {{p[3], c.hidden}}, d->q_dim))) break;
+                if (!(L.gu = concat_q4(d, {{p[4], c.ffn}, {p[5], c.ffn}}, c.hidden))) break;
+                if (!(L.down = concat_q4(d, {{p[6], c.hidden}}, c.ffn))) break;
+            }
             const float *const *nw = w->norms ? w->norms + 6 * l : nullptr;
             if (upload_floats(d, &L.w_attn, nw ? nw[0] : nullptr, c.hidden) ||
                 upload_floats(d, &L.w_attn_post, nw ? nw[1] : nullptr, c.hidden) ||
@@ -913,6 +952,7 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
         bool direct = true;
         for (auto &L : d->layers)
             for (tensor_t *t : {L.qkv, L.o, L.gu, L.down}) {
+                if (d->persist) break;
                 const DevWeight *dw = weight_of(d, t);
                 direct = direct && dw && dw->ntiles <= kDirectMaxTiles && direct_supported(*dw);
             }
@@ -963,10 +1003,68 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             dev_alloc(d, (void **)&d->out_margins, (size_t)c.context * 4))
             break;
         if (dev_alloc(d, (void **)&d->counters, 16) || cudaMemset(d->counters, 0, 16) != cudaSuccess) break;
+        if (d->persist) {
+            // Norm weights of every layer back to back (attn, attn_post, ffn,
+            // ffn_post, q, k), copied from their uploaded vectors.
+            std::vector<int> glob;
+            for (auto &L : d->layers) glob.push_back(L.global ? 1 : 0);
+            float *d_norms = nullptr;
+            int *d_glob = nullptr;
+            if (dev_alloc(d, (void **)&d_norms, (size_t)c.layers * pp.norm_stride * 4)) break;
+            bool copied = true;
+            for (int l = 0; l < c.layers && copied; ++l) {
+                const sapphire_decoder::Layer &L = d->layers[l];
+                float *dst = d_norms + (size_t)l * pp.norm_stride;
+                const std::pair<const float *, int> parts[6] = {{L.w_attn, c.hidden},   {L.w_attn_post, c.hidden},
+                                                                {L.w_ffn, c.hidden},    {L.w_ffn_post, c.hidden},
+                                                                {L.w_q, c.head_dim},    {L.w_k, c.head_dim}};
+                for (const auto &pr : parts) {
+                    copied = copied && cudaMemcpy(dst, pr.first, (size_t)pr.second * 4, cudaMemcpyDeviceToDevice) ==
+                                           cudaSuccess;
+                    dst += pr.second;
+                }
+            }
+            if (!copied || dev_alloc(d, (void **)&d_glob, glob.size() * sizeof(int)) ||
+                dev_alloc(d, (void **)&d_glob, glob.size() * sizeof(int)) ||
+                dev_alloc(d, (void **)&pp.o_out, (size_t)c.hidden * 4) ||
+                dev_alloc(d, (void **)&pp.down_out, (size_t)c.hidden * 4) ||
+                dev_alloc(d, (void **)&pp.part, d->plan.part_floats * 4) ||
+                dev_alloc(d, (void **)&d->bar, 4 * sizeof(unsigned)))
+                break;
+            if (cudaMemcpy(d_glob, glob.data(), glob.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemset(d->bar, 0, 4 * sizeof(unsigned)) != cudaSuccess) {
+                ctx_fail(ctx, "sapphire_decoder_create", "persistent step tables upload failed");
+                break;
+            }
+            pp.st = d->state;
+            pp.prompt = d->prompt;
+            pp.eps = c.rms_eps;
+            pp.emb_scale = sqrtf((float)c.hidden);
+            pp.att_scale = 1.0f / sqrtf(c.query_pre_attn_scalar > 0.0f ? c.query_pre_attn_scalar : (float)c.head_dim);
+            pp.embed = d->embed;
+            pp.wrows = d->wrows;
+            pp.norms = d_norms;
+            pp.w_final = d->w_final;
+            pp.layer_global = d_glob;
+            pp.rope_cos_g = d->rope_cos_g;
+            pp.rope_sin_g = d->rope_sin_g;
+            pp.rope_cos_l = d->rope_cos_l;
+            pp.rope_sin_l = d->rope_sin_l;
+            pp.kcache = d->kcache;
+            pp.vcache = d->vcache;
+            pp.qkv = d->qkv;
+            pp.gu = d->gu;
+            pp.norm_out = d->norm;
+            pp.bar = d->bar;
+            pp.err = ctx->d_err;
+            pp.wait_ns = 2000000000ull;
+            persist_layout(d->plan, pp);
+        }
         // Scratch of the GEMVs sized for the largest weight, before capture.
         size_t pf = 0, ci = 0;
         std::vector<tensor_t *> all = {d->lm_head};
-        for (auto &L : d->layers) all.insert(all.end(), {L.qkv, L.o, L.gu, L.down});
+        if (!d->persist)
+            for (auto &L : d->layers) all.insert(all.end(), {L.qkv, L.o, L.gu, L.down});
         for (tensor_t *t : all) {
             const DevWeight *dw = weight_of(d, t);
             if (!dw) break;
@@ -985,8 +1083,20 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             break;
         }
         if (capture(d, false, &d->g_prompt, &d->launches_prompt) ||
-            capture(d, true, &d->g_gen, &d->launches_gen))
-            break;
+            capture(d, true, &d->g_gen, &d->launches_gen)) {
+            if (!d->persist || !d->coop) break;
+            // Capture refused the cooperative launch: capture a plain one (its
+            // CTAs are resident together all the same - one per SM, with
+            // nothing else running during the step - and its waits are bounded).
+            cudaGetLastError();
+            if (d->g_prompt) cudaGraphExecDestroy(d->g_prompt);
+            d->g_prompt = nullptr;
+            d->coop = false;
+            LOG_INFO("decoder: persistent step captured without the cooperative attribute");
+            if (capture(d, false, &d->g_prompt, &d->launches_prompt) ||
+                capture(d, true, &d->g_gen, &d->launches_gen))
+                break;
+        }
         bool evs = true;
         for (cudaEvent_t &e : d->ev) evs = evs && cudaEventCreate(&e) == cudaSuccess;
         if (!evs) break;
@@ -1027,6 +1137,9 @@ extern "C" SAPPHIRE_API int sapphire_decoder_generate(sapphire_decoder_t *d, con
     do {
         if (cudaMemcpyAsync(d->prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) break;
         if (set_state(d, prompt[0], n_prompt, st)) break;
+        // Clear the persistent step's barrier words (a step that gave up
+        // waiting may have left them set).
+        if (d->persist && cudaMemsetAsync(d->bar, 0, 4 * sizeof(unsigned), st) != cudaSuccess) break;
         if (cudaEventRecord(d->ev[0], st) != cudaSuccess) break;
         bool ok = true;
         for (int i = 0; ok && i + 1 < n_prompt; ++i) ok = cudaGraphLaunch(d->g_prompt, st) == cudaSuccess;

@@ -1,0 +1,737 @@
+// decode_persistent.cu - one Gemma-3 decode step as ONE persistent kernel.
+//
+// The step of decode.cu (the reference's inference_forward,
+// src/inference/inference.c:616-651, with the layer stages of
+// src/transformer/attention.c:311-375 and transformer.c:96-283) is a chain of
+// small dependent products: per layer 0.2 - 1.6 MB of Q4_0 weights, each
+// needing the whole output of the stage before.  Run as one kernel per stage
+// it is bound by launch and drain latency (5 - 12 us per kernel for 1 - 3 us
+// of memory traffic).  Here one CTA per SM runs the whole token and the stages
+// are separated by grid barriers (an arrival counter in global memory):
+//
+//   per layer l (5 barriers):
+//     QKV   every CTA: h += rmsnorm_delta(down_out, ffn_post[l-1]) (l > 0),
+//           x = rmsnorm_delta(h, attn[l]); its rows of [Wq; Wk; Wv] . x
+//     ATT   CTA c < nsplit: q / k rmsnorm_delta + RoPE of the token, keys
+//           [k0, k0 + chunk) of the layer's window: scores, softmax partial
+//           (max m, sum l, sum p v) per query head -> part[c]; the CTA whose
+//           range holds pos writes the token's K / V rows
+//     O     every CTA: attn = combine of the nsplit partials, its rows of Wo . attn
+//     GU    every CTA: h += rmsnorm_delta(o_out, attn_post[l]),
+//           x = rmsnorm_delta(h, ffn[l]); its rows of [Wgate; Wup] . x
+//     DOWN  every CTA: x = gelu_tanh(gate) * up; its rows of Wdown . x
+//   then CTA 0: h += rmsnorm_delta(down_out, ffn_post[L-1]) and either the
+//   final norm (the LM head's input) or the prompt-state advance.
+//
+// Every CTA keeps its own copy of the residual stream h in shared memory and
+// updates it with the same arithmetic in the same order, so the copies stay
+// identical and h never crosses the barrier.  A CTA's rows of each product
+// are a contiguous range of the row layout (PersistParams::wrows), fetched
+// into shared memory with one cp.async.bulk per stage a whole layer ahead
+// (right after the same stage of the layer before used the buffer); the keys
+// of a CTA's attention split are fetched the same way one layer ahead.  So
+// after a barrier a stage reads only its small input vector from L2.
+//
+// Arithmetic is fp32 and per element the same as decode.cu's kernels (and the
+// reference): Q4_0 dot products as sum_b scale_b * sum_j (q_j - 8) x_j, one
+// lane per 8 weights of a block, then a warp tree; sums run in a different
+// order than the reference's, so results agree to rounding.
+//
+// Waits are bounded: a grid barrier that does not fill within wait_ns sets
+// kErrGridBarrier in the error word and a device abort flag, after which no
+// CTA waits again (the step's results are then garbage, and the host reports
+// the error); an mbarrier wait that expires sets bit 0.  All CTAs must be
+// resident at once: the kernel is launched cooperatively (one CTA per SM).
+#include <cmath>
+#include <cstdlib>
+
+#include "internal.cuh"
+#include "decode_common.cuh"
+
+namespace {
+
+constexpr int kPWarps = kPersistThreads / 32;
+constexpr int kDefaultChunk = 32;
+
+// ------------------------------------------------------------ PTX helpers --
+__device__ __forceinline__ uint32_t saddr(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(saddr(dst)),
+        "l"(src), "r"(bytes), "r"(saddr(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(saddr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Every thread waits for phase `parity` of an mbarrier (bounded).
+__device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, const PersistParams &p) {
+    if (mbar_try_wait(bar, parity)) return;
+    const uint64_t t0 = gtimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (gtimer() - t0 > p.wait_ns) {
+            atomicOr(p.err, 1);
+            return;
+        }
+    }
+}
+
+// Grid barrier number k of the launch: every CTA's arrival is counted in
+// p.bar[0] (a release add after the CTA's writes); a CTA proceeds once an
+// acquire load sees k * gridDim.x.  bar[2] is the abort flag of an expired wait.
+__device__ void grid_sync(const PersistParams &p, unsigned &target, int *s_fail) {
+    __syncthreads();
+    target += gridDim.x;
+    if (threadIdx.x == 0) {
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
+        if (!*s_fail) {
+            const uint64_t t0 = gtimer();
+            unsigned it = 0;
+            while (ld_acquire(p.bar) < target) {
+                if ((++it & 31u) == 0 &&
+                    (gtimer() - t0 > p.wait_ns || *reinterpret_cast<volatile unsigned *>(p.bar + 2) != 0)) {
+                    atomicOr(p.err, kErrGridBarrier);
+                    atomicExch(p.bar + 2, 1u);
+                    *s_fail = 1;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// Rows [r0, r1) of stage s that CTA c computes (balanced split of the rows).
+__device__ __forceinline__ void stage_rows(const PersistParams &p, int s, int &r0, int &r1) {
+    const long long R = p.stage_rows[s], G = gridDim.x, c = blockIdx.x;
+    r0 = (int)(c * R / G);
+    r1 = (int)((c + 1) * R / G);
+}
+
+// Keys [k0, k0 + n) of the CTA's attention split at layer l (n = 0: none).
+__device__ __forceinline__ void split_keys(const PersistParams &p, int l, int pos, int c, int &k0, int &n,
+                                           int &nsplit) {
+    const int seq = pos + 1;
+    const int start = (!__ldg(p.layer_global + l) && seq > p.window) ? seq - p.window : 0;
+    nsplit = (seq - start + p.chunk - 1) / p.chunk;
+    k0 = start + c * p.chunk;
+    n = c < nsplit ? min(p.chunk, seq - k0) : 0;
+}
+
+// Thread 0: fetch this CTA's rows of stage s of layer l into its buffer.
+__device__ void issue_stage(const PersistParams &p, int l, int s, uint8_t *smem, uint64_t *bar) {
+    int r0, r1;
+    stage_rows(p, s, r0, r1);
+    const uint32_t bytes = (uint32_t)(r1 - r0) * (uint32_t)p.stage_stride[s];
+    if (bytes == 0) {
+        mbar_arrive(bar);
+        return;
+    }
+    mbar_arrive_tx(bar, bytes);
+    const uint8_t *src = p.wrows + (size_t)l * p.layer_bytes + p.stage_off[s] + (size_t)r0 * p.stage_stride[s];
+    bulk_g2s(smem + p.off_w[s], src, bytes, bar);
+}
+
+// Thread 0: fetch the K and V rows of this CTA's split of layer l.  The row
+// of pos itself is stale (this step writes it) and is replaced after the wait.
+__device__ void issue_kv(const PersistParams &p, int l, int pos, uint8_t *smem, uint64_t *bar) {
+    int k0, n, nsplit;
+    split_keys(p, l, pos, blockIdx.x, k0, n, nsplit);
+    if (n <= 0) {
+        mbar_arrive(bar);
+        return;
+    }
+    const uint32_t row = (uint32_t)p.hd * 4u, bytes = (uint32_t)n * row;
+    mbar_arrive_tx(bar, 2u * (uint32_t)p.kv_heads * bytes);
+    for (int kh = 0; kh < p.kv_heads; ++kh) {
+        const size_t off = (((size_t)l * p.kv_heads + kh) * p.context + k0) * p.hd;
+        bulk_g2s(smem + p.off_k + (size_t)kh * p.chunk * row, p.kcache + off, bytes, bar);
+        bulk_g2s(smem + p.off_v + (size_t)kh * p.chunk * row, p.vcache + off, bytes, bar);
+    }
+}
+
+// Thread 0: fetch layer l's norm weights into buffer l & 1 (and, with `rope`,
+// the RoPE rows of pos for both tables, which stay for the whole step).
+__device__ void issue_norms(const PersistParams &p, int l, int pos, bool rope, uint8_t *smem, uint64_t *bar) {
+    const uint32_t nbytes = (uint32_t)p.norm_stride * 4u, rbytes = (uint32_t)p.hd * 4u;
+    mbar_arrive_tx(bar, nbytes + (rope ? 4u * rbytes : 0u));
+    bulk_g2s(smem + p.off_nrm[l & 1], p.norms + (size_t)l * p.norm_stride, nbytes, bar);
+    if (rope) {
+        const size_t r = (size_t)pos * p.hd;
+        bulk_g2s(smem + p.off_rope, p.rope_cos_g + r, rbytes, bar);
+        bulk_g2s(smem + p.off_rope + rbytes, p.rope_sin_g + r, rbytes, bar);
+        bulk_g2s(smem + p.off_rope + 2 * rbytes, p.rope_cos_l + r, rbytes, bar);
+        bulk_g2s(smem + p.off_rope + 3 * rbytes, p.rope_sin_l + r, rbytes, bar);
+    }
+}
+
+// hidden += rmsnorm_delta(t, w) for t written by the stage before (L2 loads,
+// all issued before the reduction); xs is scratch.  Same per-element
+// arithmetic as residual_norm_kernel.
+__device__ void residual_add(float *hidden, const float *t, const float *w, int n, float eps, float *xs, float *red) {
+    float ss = 0.0f;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n; i += kPersistThreads) {
+        const float v = __ldcg(t + i);
+        xs[i] = v;
+        ss += v * v;
+    }
+    ss = block_sum(ss, red);
+    const float r = 1.0f / sqrtf(ss / (float)n + eps);
+    for (int i = threadIdx.x; i < n; i += kPersistThreads) hidden[i] = hidden[i] + (xs[i] * r) * (1.0f + w[i]);
+}
+
+// out = rmsnorm_delta(hidden, w), zero-padded to `padded` values.
+__device__ void norm_to(const float *hidden, const float *w, int n, int padded, float eps, float *out, float *red) {
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += kPersistThreads) ss += hidden[i] * hidden[i];
+    ss = block_sum(ss, red);
+    const float r = 1.0f / sqrtf(ss / (float)n + eps);
+    for (int i = threadIdx.x; i < padded; i += kPersistThreads) out[i] = i < n ? (hidden[i] * r) * (1.0f + w[i]) : 0.0f;
+}
+
+// Partial dot product of one 4-byte Q4_0 code word (8 weights) with its x values.
+__device__ __forceinline__ float q4_word_dot(uint32_t code, float4 x0, float4 x1) {
+    const uint32_t lo = code & 0x0F0F0F0Fu, hi = (code >> 4) & 0x0F0F0F0Fu;
+    // 0x4B0000nn is the float 2^23 + n; subtracting 2^23 + 8 leaves n - 8 exactly.
+#define Q4F(word, m) (__int_as_float((int)__byte_perm((word), 0x4B000000u, 0x7440u | (m))) - 8388616.0f)
+    float dot = 0.0f;
+    dot = fmaf(Q4F(lo, 0), x0.x, dot);
+    dot = fmaf(Q4F(hi, 0), x0.y, dot);
+    dot = fmaf(Q4F(lo, 1), x0.z, dot);
+    dot = fmaf(Q4F(hi, 1), x0.w, dot);
+    dot = fmaf(Q4F(lo, 2), x1.x, dot);
+    dot = fmaf(Q4F(hi, 2), x1.y, dot);
+    dot = fmaf(Q4F(lo, 3), x1.z, dot);
+    dot = fmaf(Q4F(hi, 3), x1.w, dot);
+#undef Q4F
+    return dot;
+}
+
+// y[r] = W[r] . xs for this CTA's rows of stage s (weights in shared memory),
+// one warp per row, two rows at a time; lane k of a row takes 4-byte code
+// word k (8 weights of block k / 4) and its x values xs[8k .. 8k + 8).
+__device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, const float *xs, float *y) {
+    int r0, r1;
+    stage_rows(p, s, r0, r1);
+    const int nb = p.stage_nb[s], stride = p.stage_stride[s], nwords = nb * 4, nr = r1 - r0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int r = warp; r < nr; r += 2 * kPWarps) {
+        const int r2 = r + kPWarps;
+        const bool two = r2 < nr;
+        const uint8_t *row = w + (size_t)r * stride, *row2 = w + (size_t)(two ? r2 : r) * stride;
+        const float *sc = reinterpret_cast<const float *>(row + (size_t)nb * 16);
+        const float *sc2 = reinterpret_cast<const float *>(row2 + (size_t)nb * 16);
+        float acc = 0.0f, acc2 = 0.0f;
+        for (int k = lane; k < nwords; k += 32) {
+            const uint32_t c1 = *reinterpret_cast<const uint32_t *>(row + 4 * k);
+            const uint32_t c2 = *reinterpret_cast<const uint32_t *>(row2 + 4 * k);
+            const float4 x0 = *reinterpret_cast<const float4 *>(xs + 8 * k);
+            const float4 x1 = *reinterpret_cast<const float4 *>(xs + 8 * k + 4);
+            acc = fmaf(sc[k >> 2], q4_word_dot(c1, x0, x1), acc);
+            acc2 = fmaf(sc2[k >> 2], q4_word_dot(c2, x0, x1), acc2);
+        }
+        acc = warp_sum(acc);
+        acc2 = warp_sum(acc2);
+        if (lane == 0) {
+            y[r0 + r] = acc;
+            if (two) y[r0 + r2] = acc2;
+        }
+    }
+}
+
+// Scores, softmax partial and weighted value sum of the GROUP query heads of
+// one KV head over the CTA's n staged keys; results go to part_h (the part
+// rows of the group's first head): [m, l, -, -, acc...] per head.
+template <int GROUP>
+__device__ void attend_group(const PersistParams &p, const float *qg, const float *Kh, const float *Vh, int n,
+                             float *sc, float *accs, float *part_h) {
+    constexpr int NJ = kMaxHeadDim / 32;
+    const int hd = p.hd, nj = hd / 32, chunk = p.chunk;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t hstride = (size_t)hd + 4;
+    // Scores: one warp per key, the group's q rows in registers (lane holds
+    // the values d = lane + 32 j), four heads' reductions interleaved.
+    {
+        float q[GROUP][NJ];
+#pragma unroll
+        for (int h = 0; h < GROUP; ++h)
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) q[h][j] = j < nj ? qg[(size_t)h * hd + lane + 32 * j] : 0.0f;
+        for (int t = warp; t < n; t += kPWarps) {
+            float kv[NJ];
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) kv[j] = j < nj ? Kh[(size_t)t * hd + lane + 32 * j] : 0.0f;
+            float a[GROUP];
+#pragma unroll
+            for (int h = 0; h < GROUP; ++h) {
+                a[h] = 0.0f;
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) a[h] = fmaf(q[h][j], kv[j], a[h]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int h = 0; h < GROUP; ++h) a[h] += __shfl_xor_sync(0xffffffffu, a[h], o);
+            if (lane == 0)
+#pragma unroll
+                for (int h = 0; h < GROUP; ++h) sc[h * chunk + t] = a[h] * p.att_scale;
+        }
+    }
+    __syncthreads();
+    // Softmax partial per head: m = max score, p = exp(s - m), l = sum p.
+    for (int h = warp; h < GROUP; h += kPWarps) {
+        float m = -INFINITY;
+        for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[h * chunk + t]);
+        m = warp_max(m);
+        float s = 0.0f;
+        for (int t = lane; t < n; t += 32) {
+            const float e = expf(sc[h * chunk + t] - m);
+            sc[h * chunk + t] = e;
+            s += e;
+        }
+        s = warp_sum(s);
+        if (lane == 0) {
+            part_h[h * hstride] = m;
+            part_h[h * hstride + 1] = s;
+        }
+    }
+    __syncthreads();
+    // acc = sum_t p_t v_t: thread (part q, dimension d) sums the keys
+    // t = q, q + parts, ... for every head of the group; then the parts are
+    // added in order.
+    const int parts = kPersistThreads / hd;
+    {
+        const int d = threadIdx.x % hd, q = threadIdx.x / hd;
+        float a[GROUP];
+#pragma unroll
+        for (int h = 0; h < GROUP; ++h) a[h] = 0.0f;
+        for (int t = q; t < n; t += parts) {
+            const float v = Vh[(size_t)t * hd + d];
+#pragma unroll
+            for (int h = 0; h < GROUP; ++h) a[h] = fmaf(sc[h * chunk + t], v, a[h]);
+        }
+#pragma unroll
+        for (int h = 0; h < GROUP; ++h) accs[((size_t)q * GROUP + h) * hd + d] = a[h];
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < GROUP * hd; j += kPersistThreads) {
+        float a = accs[j];
+        for (int q = 1; q < parts; ++q) a += accs[(size_t)q * GROUP * hd + j];
+        part_h[(size_t)(j / hd) * hstride + 4 + j % hd] = a;
+    }
+    __syncthreads();
+}
+
+// Attention of the current token over this CTA's keys at layer l (see the
+// file comment); partial results go to p.part[c][head][m, l, -, -, acc...].
+// nrm: the layer's norm weights in shared memory; the RoPE rows of pos are
+// in shared memory too.
+__device__ void attention_stage(const PersistParams &p, int l, int pos, uint8_t *smem, uint64_t *kv_bar,
+                                const float *nrm) {
+    int k0, n, nsplit;
+    split_keys(p, l, pos, blockIdx.x, k0, n, nsplit);
+    mbar_wait(kv_bar, (uint32_t)(l & 1), p);
+    if (n <= 0) return;
+    const int heads = p.heads, kvh = p.kv_heads, hd = p.hd, group = heads / kvh, chunk = p.chunk;
+    const int warp = threadIdx.x >> 5;
+    const bool is_g = __ldg(p.layer_global + l) != 0;
+    const float *rope = reinterpret_cast<const float *>(smem + p.off_rope) + (is_g ? 0 : 2 * hd);
+    const float *wq = nrm + 4 * p.hidden, *wk = wq + hd;
+    float *qs = reinterpret_cast<float *>(smem + p.off_q);
+    float *kcur = reinterpret_cast<float *>(smem + p.off_kcur);
+    float *vcur = reinterpret_cast<float *>(smem + p.off_vcur);
+    float *K = reinterpret_cast<float *>(smem + p.off_k);
+    float *V = reinterpret_cast<float *>(smem + p.off_v);
+    float *sc = reinterpret_cast<float *>(smem + p.off_sc);
+    float *accs = reinterpret_cast<float *>(smem + p.off_acc);
+
+    // The token's q and k (rmsnorm_delta per head with q_norm / k_norm, then
+    // RoPE at pos) and v.
+    for (int i = warp; i < heads + kvh; i += kPWarps)
+        warp_norm_rope(p.qkv + (size_t)i * hd, i < heads ? wq : wk, p.eps, rope, rope + hd, hd,
+                       i < heads ? qs + (size_t)i * hd : kcur + (size_t)(i - heads) * hd);
+    for (int i = threadIdx.x; i < kvh * hd; i += kPersistThreads) vcur[i] = __ldcg(p.qkv + (size_t)(heads + kvh) * hd + i);
+    __syncthreads();
+    if (pos >= k0 && pos < k0 + n) {
+        // This split holds the token: its K / V rows replace the stale rows
+        // fetched with the split and are stored for later steps.
+        const int t = pos - k0;
+        for (int i = threadIdx.x; i < kvh * hd; i += kPersistThreads) {
+            const int kh = i / hd, d = i % hd;
+            K[((size_t)kh * chunk + t) * hd + d] = kcur[i];
+            V[((size_t)kh * chunk + t) * hd + d] = vcur[i];
+            const size_t g = (((size_t)l * kvh + kh) * p.context + pos) * hd + d;
+            p.kcache[g] = kcur[i];
+            p.vcache[g] = vcur[i];
+        }
+        // The next layer's keys are fetched into these buffers by the async
+        // proxy: order these generic writes before that.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+    }
+    for (int kh = 0; kh < kvh; ++kh) {
+        const float *Kh = K + (size_t)kh * chunk * hd, *Vh = V + (size_t)kh * chunk * hd;
+        const float *qg = qs + (size_t)kh * group * hd;
+        float *part_h = p.part + ((size_t)blockIdx.x * heads + kh * group) * (hd + 4);
+        switch (group) {   // persist_plan admits groups of 1, 2, 4 and 8
+            case 1: attend_group<1>(p, qg, Kh, Vh, n, sc, accs, part_h); break;
+            case 2: attend_group<2>(p, qg, Kh, Vh, n, sc, accs, part_h); break;
+            case 4: attend_group<4>(p, qg, Kh, Vh, n, sc, accs, part_h); break;
+            default: attend_group<8>(p, qg, Kh, Vh, n, sc, accs, part_h); break;
+        }
+    }
+}
+
+// attn = (sum_b exp(m_b - M) acc_b) / (sum_b exp(m_b - M) l_b) over the
+// splits of layer l (M = max_b m_b), into xs (zero-padded to the O stage's
+// width).  Thread (half q, quad j) reads the partials of splits b = q, q + 2,
+// ... for outputs 4j .. 4j + 3 (all loads of a batch issued together, a
+// running maximum rescales as it goes); the two halves are merged in order.
+__device__ void combine_stage(const PersistParams &p, int l, int pos, float *xs, float *scratch) {
+    int k0, n, nsplit;
+    split_keys(p, l, pos, 0, k0, n, nsplit);
+    const int heads = p.heads, hd = p.hd, width = p.stage_nb[kStO] * 32;
+    const size_t hstride = (size_t)hd + 4;
+    const int quads = heads * hd / 4;
+    constexpr int kHalves = 2, kBatch = 8;
+    for (int i = threadIdx.x; i < kHalves * quads; i += kPersistThreads) {
+        const int q = i / quads, j = i % quads;
+        const int h = (4 * j) / hd, d = (4 * j) % hd;
+        const float *base = p.part + (size_t)h * hstride;
+        float M = -INFINITY, L = 0.0f;
+        float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int b0 = q; b0 < nsplit; b0 += kHalves * kBatch) {
+            float m[kBatch], lv[kBatch];
+            float4 a[kBatch];
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k) {
+                const int b = b0 + kHalves * k;
+                const float *pp = base + (size_t)b * heads * hstride;
+                m[k] = b < nsplit ? __ldcg(pp) : -INFINITY;
+                lv[k] = b < nsplit ? __ldcg(pp + 1) : 0.0f;
+                a[k] = b < nsplit ? __ldcg(reinterpret_cast<const float4 *>(pp + 4 + d)) : make_float4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int k = 0; k < kBatch; ++k) {
+                if (m[k] == -INFINITY) continue;
+                const float Mn = fmaxf(M, m[k]);
+                const float c = expf(M - Mn), e = expf(m[k] - Mn);   // c = 0 while M is -inf
+                L = L * c + e * lv[k];
+                O.x = O.x * c + e * a[k].x;
+                O.y = O.y * c + e * a[k].y;
+                O.z = O.z * c + e * a[k].z;
+                O.w = O.w * c + e * a[k].w;
+                M = Mn;
+            }
+        }
+        float *sp = scratch + (size_t)i * 8;
+        sp[0] = M;
+        sp[1] = L;
+        sp[4] = O.x;
+        sp[5] = O.y;
+        sp[6] = O.z;
+        sp[7] = O.w;
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < quads; j += kPersistThreads) {
+        const float *s0 = scratch + (size_t)j * 8, *s1 = scratch + (size_t)(quads + j) * 8;
+        const float M = fmaxf(s0[0], s1[0]);
+        const float c0 = s0[0] == -INFINITY ? 0.0f : expf(s0[0] - M);
+        const float c1 = s1[0] == -INFINITY ? 0.0f : expf(s1[0] - M);
+        const float inv = 1.0f / (s0[1] * c0 + s1[1] * c1);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) xs[4 * j + k] = (s0[4 + k] * c0 + s1[4 + k] * c1) * inv;
+    }
+    for (int j = heads * hd + threadIdx.x; j < width; j += kPersistThreads) xs[j] = 0.0f;
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(const __grid_constant__ PersistParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    // mbarriers: one per weight stage, the keys, the two norm buffers.
+    constexpr int kBarKv = kNumStages, kBarNorm = kNumStages + 1, kNumBars = kNumStages + 3;
+    __shared__ __align__(8) uint64_t mbar[kNumBars];
+    __shared__ float red[32];
+    __shared__ int s_fail;
+    float *hidden = reinterpret_cast<float *>(smem + p.off_hidden);
+    float *xs = reinterpret_cast<float *>(smem + p.off_x);
+    float *scratch = reinterpret_cast<float *>(smem + p.off_acc);
+    const int H = p.hidden;
+    // The state is read once, before the first barrier (CTA 0 advances it
+    // after the last one in the prompt phase).
+    const int pos = *reinterpret_cast<volatile const int *>(&p.st->pos);
+    int tok = *reinterpret_cast<volatile const int *>(&p.st->cur_token);
+    unsigned target = 0;
+
+    if (threadIdx.x == 0) {
+        s_fail = 0;
+        for (int i = 0; i < kNumBars; ++i) mbar_init(&mbar[i], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        issue_norms(p, 0, pos, true, smem, &mbar[kBarNorm]);
+        if (p.layers > 1) issue_norms(p, 1, pos, false, smem, &mbar[kBarNorm + 1]);
+        for (int s = 0; s < kNumStages; ++s) issue_stage(p, 0, s, smem, &mbar[s]);
+        issue_kv(p, 0, pos, smem, &mbar[kBarKv]);
+    }
+    // h = embedding row * sqrt(hidden) (transformer.c:367-380).
+    if (tok < 0 || tok >= p.vocab) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(p.err, kErrToken);
+        tok = 0;
+    }
+    const uint16_t *erow = p.embed + (size_t)tok * H;
+    for (int i = threadIdx.x; i < H; i += kPersistThreads)
+        hidden[i] = __uint_as_float((uint32_t)__ldg(erow + i) << 16) * p.emb_scale;
+
+    for (int l = 0; l < p.layers; ++l) {
+        const uint32_t par = (uint32_t)(l & 1);
+        const bool more = l + 1 < p.layers;
+        // Norm weights of this layer (buffer l & 1, phase l / 2 of its barrier).
+        mbar_wait(&mbar[kBarNorm + (l & 1)], (uint32_t)((l >> 1) & 1), p);
+        const float *nrm = reinterpret_cast<const float *>(smem + p.off_nrm[l & 1]);
+        const float *prev = reinterpret_cast<const float *>(smem + p.off_nrm[(l + 1) & 1]);
+        __syncthreads();
+        // QKV
+        if (l > 0) residual_add(hidden, p.down_out, prev + 3 * H, H, p.eps, xs, red);
+        norm_to(hidden, nrm, H, p.stage_nb[kStQkv] * 32, p.eps, xs, red);
+        mbar_wait(&mbar[kStQkv], par, p);
+        __syncthreads();
+        gemv_stage(p, kStQkv, smem + p.off_w[kStQkv], xs, p.qkv);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            if (more) issue_stage(p, l + 1, kStQkv, smem, &mbar[kStQkv]);
+            // The previous layer's norms are no longer read: fetch layer l + 1's.
+            if (l >= 1 && more) issue_norms(p, l + 1, pos, false, smem, &mbar[kBarNorm + ((l + 1) & 1)]);
+        }
+        grid_sync(p, target, &s_fail);
+        // ATT
+        attention_stage(p, l, pos, smem, &mbar[kBarKv], nrm);
+        __syncthreads();
+        if (threadIdx.x == 0 && more) issue_kv(p, l + 1, pos, smem, &mbar[kBarKv]);
+        grid_sync(p, target, &s_fail);
+        // O
+        combine_stage(p, l, pos, xs, scratch);
+        mbar_wait(&mbar[kStO], par, p);
+        gemv_stage(p, kStO, smem + p.off_w[kStO], xs, p.o_out);
+        __syncthreads();
+        if (threadIdx.x == 0 && more) issue_stage(p, l + 1, kStO, smem, &mbar[kStO]);
+        grid_sync(p, target, &s_fail);
+        // GU
+        residual_add(hidden, p.o_out, nrm + H, H, p.eps, xs, red);
+        norm_to(hidden, nrm + 2 * H, H, p.stage_nb[kStGu] * 32, p.eps, xs, red);
+        mbar_wait(&mbar[kStGu], par, p);
+        __syncthreads();
+        gemv_stage(p, kStGu, smem + p.off_w[kStGu], xs, p.gu);
+        __syncthreads();
+        if (threadIdx.x == 0 && more) issue_stage(p, l + 1, kStGu, smem, &mbar[kStGu]);
+        grid_sync(p, target, &s_fail);
+        // DOWN: x = gelu_tanh(gate) * up, four values per thread and load.
+        {
+            const int F = p.ffn, width = p.stage_nb[kStDown] * 32;
+            for (int i = 4 * threadIdx.x; i < width; i += 4 * kPersistThreads) {
+                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (i + 3 < F) {
+                    const float4 g = __ldcg(reinterpret_cast<const float4 *>(p.gu + i));
+                    const float4 u = __ldcg(reinterpret_cast<const float4 *>(p.gu + F + i));
+                    v = make_float4(geglu_tanh(g.x, u.x), geglu_tanh(g.y, u.y), geglu_tanh(g.z, u.z),
+                                    geglu_tanh(g.w, u.w));
+                } else {
+                    float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    for (int k = 0; k < 4; ++k)
+                        if (i + k < F) t[k] = geglu_tanh(__ldcg(p.gu + i + k), __ldcg(p.gu + F + i + k));
+                    v = make_float4(t[0], t[1], t[2], t[3]);
+                }
+                *reinterpret_cast<float4 *>(xs + i) = v;
+            }
+        }
+        mbar_wait(&mbar[kStDown], par, p);
+        __syncthreads();
+        gemv_stage(p, kStDown, smem + p.off_w[kStDown], xs, p.down_out);
+        __syncthreads();
+        if (threadIdx.x == 0 && more) issue_stage(p, l + 1, kStDown, smem, &mbar[kStDown]);
+        grid_sync(p, target, &s_fail);
+    }
+
+    if (blockIdx.x == 0) {
+        if (p.generate) {
+            // logits input: rmsnorm_delta(h + rmsnorm_delta(down_out, ffn_post), final) (transformer.c:393-408)
+            const float *last = reinterpret_cast<const float *>(smem + p.off_nrm[(p.layers - 1) & 1]);
+            residual_add(hidden, p.down_out, last + 3 * H, H, p.eps, xs, red);
+            float ss = 0.0f;
+            for (int i = threadIdx.x; i < H; i += kPersistThreads) ss += hidden[i] * hidden[i];
+            ss = block_sum(ss, red);
+            const float r = 1.0f / sqrtf(ss / (float)H + p.eps);
+            for (int i = threadIdx.x; i < H; i += kPersistThreads)
+                p.norm_out[i] = (hidden[i] * r) * (1.0f + __ldg(p.w_final + i));
+        } else if (threadIdx.x == 0) {
+            // Prompt phase: the next prompt token becomes the input at the next position.
+            const int i = p.st->prompt_index + 1;
+            p.st->prompt_index = i;
+            p.st->pos = pos + 1;
+            if (i < p.st->n_prompt) p.st->cur_token = p.prompt[i];
+        }
+    }
+    // Exit: the last CTA out clears the barrier words for the next launch
+    // (every CTA has finished waiting by the time it counts itself out).
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(p.bar + 1, 1u) == gridDim.x - 1) {
+            atomicExch(p.bar, 0u);
+            atomicExch(p.bar + 2, 0u);
+            atomicExch(p.bar + 1, 0u);
+        }
+    }
+}
+
+size_t align128(size_t v) { return (v + 127) & ~(size_t)127; }
+
+// Dynamic shared-memory layout for grid G and `chunk` keys per split: fills
+// p's offsets and returns the total bytes.
+size_t smem_layout(PersistParams &p, int G, int chunk) {
+    size_t off = 0;
+    for (int st = 0; st < kNumStages; ++st) {
+        p.off_w[st] = (unsigned)off;
+        const size_t rows_max = ((size_t)p.stage_rows[st] + G - 1) / G;
+        off = align128(off + rows_max * p.stage_stride[st]);
+    }
+    const size_t kv_bytes = (size_t)p.kv_heads * chunk * p.hd * 4;
+    p.off_k = (unsigned)off;
+    off = align128(off + kv_bytes);
+    p.off_v = (unsigned)off;
+    off = align128(off + kv_bytes);
+    p.off_hidden = (unsigned)off;
+    off = align128(off + (size_t)p.hidden * 4);
+    size_t xw = std::max((size_t)p.heads * p.hd, (size_t)p.hidden);
+    for (int st = 0; st < kNumStages; ++st) xw = std::max(xw, (size_t)p.stage_nb[st] * 32);
+    p.off_x = (unsigned)off;
+    off = align128(off + xw * 4);
+    p.off_q = (unsigned)off;
+    off = align128(off + (size_t)p.heads * p.hd * 4);
+    p.off_kcur = (unsigned)off;
+    off = align128(off + (size_t)p.kv_heads * p.hd * 4);
+    p.off_vcur = (unsigned)off;
+    off = align128(off + (size_t)p.kv_heads * p.hd * 4);
+    p.off_sc = (unsigned)off;
+    off = align128(off + (size_t)kMaxGroup * chunk * 4);
+    for (int b = 0; b < 2; ++b) {
+        p.off_nrm[b] = (unsigned)off;
+        off = align128(off + (size_t)p.norm_stride * 4);
+    }
+    p.off_rope = (unsigned)off;
+    off = align128(off + (size_t)4 * p.hd * 4);
+    // Scratch of the weighted key sums and of the split combine.
+    const size_t group = (size_t)p.heads / p.kv_heads;
+    p.off_acc = (unsigned)off;
+    off = align128(off + std::max((size_t)kPersistThreads * group, (size_t)4 * p.heads * p.hd) * 4);
+    p.off_cw = p.off_ml = 0;
+    p.chunk = chunk;
+    return off;
+}
+
+}  // namespace
+
+PersistPlan persist_plan(int device, const PersistParams &s, const char **why) {
+    PersistPlan plan;
+    *why = nullptr;
+    const int G = sm_count(device);
+    if (G <= 0) {
+        *why = "no SM count";
+        return plan;
+    }
+    const int group = s.kv_heads > 0 ? s.heads / s.kv_heads : 0;
+    if (s.hd % 64 || s.hd > kMaxHeadDim || s.kv_heads <= 0 || s.heads % s.kv_heads ||
+        (group != 1 && group != 2 && group != 4 && group != 8)) {
+        *why = "head shape";
+        return plan;
+    }
+    if (s.hidden % 4 || s.ffn % 4 || s.norm_stride != 4 * s.hidden + 2 * s.hd || kPersistThreads % s.hd) {
+        *why = "hidden / ffn / head_dim alignment";
+        return plan;
+    }
+    for (int st = 0; st < kNumStages; ++st)
+        if (s.stage_stride[st] % 16 || s.stage_rows[st] <= 0) {
+            *why = "row layout";
+            return plan;
+        }
+    int chunk = kDefaultChunk;
+    if (const char *e = getenv("SAPPHIRE_DECODE_CHUNK")) {
+        const int v = atoi(e);
+        if (v >= 1 && v <= 256) chunk = v;
+    }
+    // Every split count of a window up to the context fits the grid.
+    chunk = std::max(chunk, (s.context + G - 1) / G);
+    PersistParams lay = s;
+    const size_t bytes = smem_layout(lay, G, chunk);
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    const size_t static_bytes = 1024;   // mbarriers, reduction scratch, flags
+    if (bytes + static_bytes > (size_t)optin) {
+        *why = "shared memory";
+        return plan;
+    }
+    if (cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        *why = "shared-memory attribute";
+        return plan;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_persistent_kernel, kPersistThreads, bytes) !=
+            cudaSuccess ||
+        per_sm < 1) {
+        cudaGetLastError();
+        *why = "occupancy";
+        return plan;
+    }
+    plan.ok = true;
+    plan.grid = G;
+    plan.chunk = chunk;
+    plan.smem = bytes;
+    plan.part_floats = (size_t)G * s.heads * (s.hd + 4);
+    return plan;
+}
+
+void persist_layout(const PersistPlan &plan, PersistParams &p) { smem_layout(p, plan.grid, plan.chunk); }
+
+cudaError_t launch_persist(const PersistPlan &plan, const PersistParams &p, bool cooperative, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(plan.grid);
+    cfg.blockDim = dim3(kPersistThreads);
+    cfg.dynamicSmemBytes = plan.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = cooperative ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, decode_persistent_kernel, p);
+}
