@@ -382,7 +382,7 @@ int check_kernel_error(kernel_context_t *ctx, const char *who) {
     if (bits & 8)
         ctx_fail(ctx, who, "a peer-memory gather gave up waiting for another rank's rows (bounded wait expired)");
     else if (bits & 16)
-        ctx_fail(ctx, who, "a persistent decode step gave up waiting at a grid barrier (bounded wait expired)");
+        ctx_fail(ctx, who, "a persistent decode step gave up waiting for another block's output (bounded wait expired)");
     else if (bits == 4)
         ctx_fail(ctx, who, "a token id outside the vocabulary reached the embedding");
     else

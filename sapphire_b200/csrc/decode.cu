@@ -576,7 +576,7 @@ struct sapphire_decoder {
     PersistPlan plan;
     PersistParams pp{};
     uint8_t *wrows = nullptr;
-    unsigned *bar = nullptr;        // [0] arrivals, [1] exits, [2] abort flag
+    unsigned *ctl = nullptr;        // [0] abort flag, [1] launches so far
 
     cudaGraphExec_t g_prompt = nullptr, g_gen = nullptr;
     int launches_prompt = 0, launches_gen = 0;
@@ -1026,13 +1026,24 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             }
             if (!copied || dev_alloc(d, (void **)&d_glob, glob.size() * sizeof(int)) ||
                 dev_alloc(d, (void **)&d_glob, glob.size() * sizeof(int)) ||
-                dev_alloc(d, (void **)&pp.o_out, (size_t)c.hidden * 4) ||
-                dev_alloc(d, (void **)&pp.down_out, (size_t)c.hidden * 4) ||
+                dev_alloc(d, (void **)&pp.qkv, (size_t)(d->q_dim + 2 * d->kv_dim) * 8) ||
+                dev_alloc(d, (void **)&pp.o_out, (size_t)c.hidden * 8 * kPersistReplicas) ||
+                dev_alloc(d, (void **)&pp.gu, (size_t)2 * c.ffn * 8 * kPersistReplicas) ||
+                dev_alloc(d, (void **)&pp.down_out, (size_t)c.hidden * 8 * kPersistReplicas) ||
                 dev_alloc(d, (void **)&pp.part, d->plan.part_floats * 4) ||
-                dev_alloc(d, (void **)&d->bar, 4 * sizeof(unsigned)))
+                dev_alloc(d, (void **)&d->ctl, 4 * sizeof(unsigned)))
                 break;
+            // Tagged words start with epoch 0, which no launch uses.
+            if (cudaMemset(pp.qkv, 0, (size_t)(d->q_dim + 2 * d->kv_dim) * 8) != cudaSuccess ||
+                cudaMemset(pp.o_out, 0, (size_t)c.hidden * 8 * kPersistReplicas) != cudaSuccess ||
+                cudaMemset(pp.gu, 0, (size_t)2 * c.ffn * 8 * kPersistReplicas) != cudaSuccess ||
+                cudaMemset(pp.down_out, 0, (size_t)c.hidden * 8 * kPersistReplicas) != cudaSuccess ||
+                cudaMemset(pp.part, 0, d->plan.part_floats * 4) != cudaSuccess) {
+                ctx_fail(ctx, "sapphire_decoder_create", "persistent step buffers could not be cleared");
+                break;
+            }
             if (cudaMemcpy(d_glob, glob.data(), glob.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess ||
-                cudaMemset(d->bar, 0, 4 * sizeof(unsigned)) != cudaSuccess) {
+                cudaMemset(d->ctl, 0, 4 * sizeof(unsigned)) != cudaSuccess) {
                 ctx_fail(ctx, "sapphire_decoder_create", "persistent step tables upload failed");
                 break;
             }
@@ -1052,10 +1063,8 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             pp.rope_sin_l = d->rope_sin_l;
             pp.kcache = d->kcache;
             pp.vcache = d->vcache;
-            pp.qkv = d->qkv;
-            pp.gu = d->gu;
             pp.norm_out = d->norm;
-            pp.bar = d->bar;
+            pp.ctl = d->ctl;
             pp.err = ctx->d_err;
             pp.wait_ns = 2000000000ull;
             persist_layout(d->plan, pp);
@@ -1137,9 +1146,9 @@ extern "C" SAPPHIRE_API int sapphire_decoder_generate(sapphire_decoder_t *d, con
     do {
         if (cudaMemcpyAsync(d->prompt, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) break;
         if (set_state(d, prompt[0], n_prompt, st)) break;
-        // Clear the persistent step's barrier words (a step that gave up
-        // waiting may have left them set).
-        if (d->persist && cudaMemsetAsync(d->bar, 0, 4 * sizeof(unsigned), st) != cudaSuccess) break;
+        // Clear the persistent step's abort flag (a step that gave up waiting
+        // leaves it set); the launch count stays.
+        if (d->persist && cudaMemsetAsync(d->ctl, 0, sizeof(unsigned), st) != cudaSuccess) break;
         if (cudaEventRecord(d->ev[0], st) != cudaSuccess) break;
         bool ok = true;
         for (int i = 0; ok && i + 1 < n_prompt; ++i) ok = cudaGraphLaunch(d->g_prompt, st) == cudaSuccess;

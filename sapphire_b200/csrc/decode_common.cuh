@@ -23,7 +23,7 @@ struct DecState {
 
 // Error bits of the context's error word set by the decode kernels.
 constexpr int kErrToken = 4;          // a token id outside the vocabulary
-constexpr int kErrGridBarrier = 16;   // a persistent step gave up waiting at a grid barrier
+constexpr int kErrStepWait = 16;     // a persistent step gave up waiting for another CTA's output
 
 #ifdef __CUDACC__
 static __device__ __forceinline__ float warp_sum(float v) {
@@ -113,18 +113,27 @@ struct PersistParams {
     const int *layer_global;      // [layers] 1 for global attention
     const float *rope_cos_g, *rope_sin_g, *rope_cos_l, *rope_sin_l;
     float *kcache, *vcache;       // [layers][kv_heads][context][hd]
-    float *qkv, *part, *o_out, *gu, *down_out, *norm_out;
+    // Stage outputs as epoch-tagged words (epoch << 32 | fp32 bits): a
+    // consumer polls the words it needs until they carry the stage's epoch.
+    // o_out, gu and down_out, which every CTA reads, are written in
+    // kPersistReplicas copies ([replica][row]); CTA c polls copy c % kPersistReplicas.
+    unsigned long long *qkv, *o_out, *gu, *down_out;
+    // Attention partials per split and head: [m word, l word, acc (hd floats)]
+    // (the m / l words are tagged and stored with release after acc).
+    float *part;
+    float *norm_out;              // the LM head's input (plain floats)
     int chunk;                    // keys per attention split
-    unsigned *bar;                // [0] barrier arrivals, [1] exits (zero between launches)
+    unsigned *ctl;                // [0] abort flag, [1] launches so far (never cleared: the epoch base)
     int *err;
     unsigned long long wait_ns;   // bound of every wait
     // Dynamic shared-memory offsets (bytes).
     unsigned off_w[kNumStages], off_k, off_v, off_hidden, off_x, off_q, off_kcur, off_vcur, off_cw, off_sc, off_ml;
-    unsigned off_nrm[2], off_rope, off_acc;
+    unsigned off_nrm[2], off_rope, off_acc, off_vin;
 };
 
 // Host side (decode_persistent.cu).
 constexpr int kPersistThreads = 512;
+constexpr int kPersistReplicas = 8;
 struct PersistPlan {
     bool ok = false;
     int grid = 0, chunk = 0;

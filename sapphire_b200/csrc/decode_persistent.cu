@@ -6,15 +6,18 @@
 // small dependent products: per layer 0.2 - 1.6 MB of Q4_0 weights, each
 // needing the whole output of the stage before.  Run as one kernel per stage
 // it is bound by launch and drain latency (5 - 12 us per kernel for 1 - 3 us
-// of memory traffic).  Here one CTA per SM runs the whole token and the stages
-// are separated by grid barriers (an arrival counter in global memory):
+// of memory traffic).  Here one CTA per SM runs the whole token, and a stage
+// waits for exactly the data it reads: every stage output is written as
+// epoch-tagged 8-byte words, and a consumer polls the words it needs until
+// they carry the stage's epoch (no grid barrier, no separate flag):
 //
-//   per layer l (5 barriers):
+//   per layer l:
 //     QKV   every CTA: h += rmsnorm_delta(down_out, ffn_post[l-1]) (l > 0),
 //           x = rmsnorm_delta(h, attn[l]); its rows of [Wq; Wk; Wv] . x
 //     ATT   CTA c < nsplit: q / k rmsnorm_delta + RoPE of the token, keys
 //           [k0, k0 + chunk) of the layer's window: scores, softmax partial
-//           (max m, sum l, sum p v) per query head -> part[c]; the CTA whose
+//           (max m, sum l, sum p v) per query head -> part[c] (m and l as
+//           tagged words stored with release after the sums); the CTA whose
 //           range holds pos writes the token's K / V rows
 //     O     every CTA: attn = combine of the nsplit partials, its rows of Wo . attn
 //     GU    every CTA: h += rmsnorm_delta(o_out, attn_post[l]),
@@ -23,22 +26,27 @@
 //   then CTA 0: h += rmsnorm_delta(down_out, ffn_post[L-1]) and either the
 //   final norm (the LM head's input) or the prompt-state advance.
 //
+// Buffers need no double buffering: every CTA has rows in every product, so
+// before any CTA can write a stage's buffer again (one layer later) it must
+// have consumed outputs that every CTA produced after its last read of that
+// buffer.
+//
 // Every CTA keeps its own copy of the residual stream h in shared memory and
 // updates it with the same arithmetic in the same order, so the copies stay
-// identical and h never crosses the barrier.  A CTA's rows of each product
-// are a contiguous range of the row layout (PersistParams::wrows), fetched
-// into shared memory with one cp.async.bulk per stage a whole layer ahead
-// (right after the same stage of the layer before used the buffer); the keys
-// of a CTA's attention split are fetched the same way one layer ahead.  So
-// after a barrier a stage reads only its small input vector from L2.
+// identical and h never crosses CTAs.  A CTA's rows of each product are a
+// contiguous range of the row layout (PersistParams::wrows), fetched into
+// shared memory with one cp.async.bulk per stage a whole layer ahead (right
+// after the same stage of the layer before used the buffer); the keys of a
+// CTA's attention split and the norm weights are fetched the same way one
+// layer ahead.  So a stage reads only its small input vector from L2.
 //
 // Arithmetic is fp32 and per element the same as decode.cu's kernels (and the
 // reference): Q4_0 dot products as sum_b scale_b * sum_j (q_j - 8) x_j, one
 // lane per 8 weights of a block, then a warp tree; sums run in a different
 // order than the reference's, so results agree to rounding.
 //
-// Waits are bounded: a grid barrier that does not fill within wait_ns sets
-// kErrGridBarrier in the error word and a device abort flag, after which no
+// Waits are bounded: a word that does not arrive within wait_ns sets
+// kErrStepWait in the error word and a device abort flag, after which no
 // CTA waits again (the step's results are then garbage, and the host reports
 // the error); an mbarrier wait that expires sets bit 0.  All CTAs must be
 // resident at once: the kernel is launched cooperatively (one CTA per SM).
@@ -102,26 +110,87 @@ __device__ __forceinline__ void mbar_wait(uint64_t *bar, uint32_t parity, const 
     }
 }
 
-// Grid barrier number k of the launch: every CTA's arrival is counted in
-// p.bar[0] (a release add after the CTA's writes); a CTA proceeds once an
-// acquire load sees k * gridDim.x.  bar[2] is the abort flag of an expired wait.
-__device__ void grid_sync(const PersistParams &p, unsigned &target, int *s_fail) {
-    __syncthreads();
-    target += gridDim.x;
-    if (threadIdx.x == 0) {
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
-        if (!*s_fail) {
+// ------------------------------------------------------ tagged words ----
+// A stage's outputs are 8-byte words (epoch << 32 | fp32 bits): an aligned
+// 8-byte store is seen whole, so a word that carries the stage's epoch holds
+// its value and needs no separate flag or barrier.  Every launch has its own
+// range of epochs (ctl[1], the launches so far, never repeats within 2^32
+// stages), and every word a consumer waits for is rewritten in every launch.
+__device__ __forceinline__ unsigned long long ld_word(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long ld_word_acquire(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_word(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_word_release(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long tagged(unsigned epoch, float v) {
+    return ((unsigned long long)epoch << 32) | __float_as_uint(v);
+}
+
+// Gives up the launch's waits after an expiry: sets kErrStepWait, the
+// device abort flag and the CTA's own flag.
+__device__ __noinline__ void give_up(const PersistParams &p, int *s_abort) {
+    atomicOr(p.err, kErrStepWait);
+    atomicExch(p.ctl, 1u);
+    *reinterpret_cast<volatile int *>(s_abort) = 1;
+}
+
+// True while the wait begun at t0 may go on (bounded by wait_ns; false once
+// this CTA or any other has given up).  The clock and the device abort flag
+// are read every 16th poll only, so a poll costs one round trip.
+__device__ __forceinline__ bool keep_waiting(const PersistParams &p, int *s_abort, uint64_t t0, unsigned &it) {
+    if (*reinterpret_cast<volatile int *>(s_abort)) return false;
+    if ((++it & 15u) == 0 && (gtimer() - t0 > p.wait_ns || *reinterpret_cast<volatile unsigned *>(p.ctl) != 0)) {
+        give_up(p, s_abort);
+        return false;
+    }
+    return true;
+}
+
+// dst[i] = value of src[i] for i < n once every word carries `epoch`.  A
+// thread issues the loads of all its words (up to kFetch at a time) before
+// checking any, and re-loads all of its words still pending together, so a
+// wait costs one L2 round trip per poll, not one per word.  Ends with
+// __syncthreads.
+constexpr int kFetch = 8;
+__device__ void fetch_vec(const unsigned long long *src, int n, unsigned epoch, float *dst, const PersistParams &p,
+                          int *s_abort) {
+    for (int base = 0; base < n; base += kFetch * kPersistThreads) {
+        unsigned long long v[kFetch];
+        unsigned pending = 0;
+#pragma unroll
+        for (int k = 0; k < kFetch; ++k) {
+            const int i = base + k * kPersistThreads + threadIdx.x;
+            v[k] = i < n ? ld_word(src + i) : ((unsigned long long)epoch << 32);
+        }
+#pragma unroll
+        for (int k = 0; k < kFetch; ++k)
+            if ((unsigned)(v[k] >> 32) != epoch) pending |= 1u << k;
+        if (pending) {
             const uint64_t t0 = gtimer();
             unsigned it = 0;
-            while (ld_acquire(p.bar) < target) {
-                if ((++it & 31u) == 0 &&
-                    (gtimer() - t0 > p.wait_ns || *reinterpret_cast<volatile unsigned *>(p.bar + 2) != 0)) {
-                    atomicOr(p.err, kErrGridBarrier);
-                    atomicExch(p.bar + 2, 1u);
-                    *s_fail = 1;
-                    break;
-                }
+            while (pending && keep_waiting(p, s_abort, t0, it)) {
+#pragma unroll
+                for (int k = 0; k < kFetch; ++k)
+                    if (pending & (1u << k)) v[k] = ld_word(src + base + k * kPersistThreads + threadIdx.x);
+#pragma unroll
+                for (int k = 0; k < kFetch; ++k)
+                    if ((unsigned)(v[k] >> 32) == epoch) pending &= ~(1u << k);
             }
+        }
+#pragma unroll
+        for (int k = 0; k < kFetch; ++k) {
+            const int i = base + k * kPersistThreads + threadIdx.x;
+            if (i < n) dst[i] = __uint_as_float((unsigned)v[k]);
         }
     }
     __syncthreads();
@@ -191,19 +260,15 @@ __device__ void issue_norms(const PersistParams &p, int l, int pos, bool rope, u
     }
 }
 
-// hidden += rmsnorm_delta(t, w) for t written by the stage before (L2 loads,
-// all issued before the reduction); xs is scratch.  Same per-element
-// arithmetic as residual_norm_kernel.
-__device__ void residual_add(float *hidden, const float *t, const float *w, int n, float eps, float *xs, float *red) {
+// hidden += rmsnorm_delta(t, w) for t the tagged output of the stage before
+// (fetched into xs).  Same per-element arithmetic as residual_norm_kernel.
+__device__ void residual_add(float *hidden, const unsigned long long *t, unsigned epoch, const float *w, int n,
+                             float *xs, float *red, const PersistParams &p, int *s_abort) {
+    fetch_vec(t, n, epoch, xs, p, s_abort);
     float ss = 0.0f;
-#pragma unroll 4
-    for (int i = threadIdx.x; i < n; i += kPersistThreads) {
-        const float v = __ldcg(t + i);
-        xs[i] = v;
-        ss += v * v;
-    }
+    for (int i = threadIdx.x; i < n; i += kPersistThreads) ss += xs[i] * xs[i];
     ss = block_sum(ss, red);
-    const float r = 1.0f / sqrtf(ss / (float)n + eps);
+    const float r = 1.0f / sqrtf(ss / (float)n + p.eps);
     for (int i = threadIdx.x; i < n; i += kPersistThreads) hidden[i] = hidden[i] + (xs[i] * r) * (1.0f + w[i]);
 }
 
@@ -234,10 +299,12 @@ __device__ __forceinline__ float q4_word_dot(uint32_t code, float4 x0, float4 x1
     return dot;
 }
 
-// y[r] = W[r] . xs for this CTA's rows of stage s (weights in shared memory),
-// one warp per row, two rows at a time; lane k of a row takes 4-byte code
-// word k (8 weights of block k / 4) and its x values xs[8k .. 8k + 8).
-__device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, const float *xs, float *y) {
+// y[r] = W[r] . xs (as tagged words of `epoch`, in `replicas` copies) for
+// this CTA's rows of stage s (weights in shared memory), one warp per row, two rows at a time; lane k
+// of a row takes 4-byte code word k (8 weights of block k / 4) and its x
+// values xs[8k .. 8k + 8).
+__device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, const float *xs, unsigned long long *y,
+                           unsigned epoch, int replicas) {
     int r0, r1;
     stage_rows(p, s, r0, r1);
     const int nb = p.stage_nb[s], stride = p.stage_stride[s], nwords = nb * 4, nr = r1 - r0;
@@ -259,9 +326,11 @@ __device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, cons
         }
         acc = warp_sum(acc);
         acc2 = warp_sum(acc2);
-        if (lane == 0) {
-            y[r0 + r] = acc;
-            if (two) y[r0 + r2] = acc2;
+        // Every lane holds the sums (xor reduction): lane k writes copy k.
+        if (lane < replicas) {
+            unsigned long long *yk = y + (size_t)lane * p.stage_rows[s];
+            st_word(yk + r0 + r, tagged(epoch, acc));
+            if (two) st_word(yk + r0 + r2, tagged(epoch, acc2));
         }
     }
 }
@@ -271,7 +340,8 @@ __device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, cons
 // rows of the group's first head): [m, l, -, -, acc...] per head.
 template <int GROUP>
 __device__ void attend_group(const PersistParams &p, const float *qg, const float *Kh, const float *Vh, int n,
-                             float *sc, float *accs, float *part_h) {
+                             float *sc, float *accs, float *part_h, unsigned epoch) {
+    __shared__ float s_ml[2 * GROUP];
     constexpr int NJ = kMaxHeadDim / 32;
     const int hd = p.hd, nj = hd / 32, chunk = p.chunk;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -318,8 +388,8 @@ __device__ void attend_group(const PersistParams &p, const float *qg, const floa
         }
         s = warp_sum(s);
         if (lane == 0) {
-            part_h[h * hstride] = m;
-            part_h[h * hstride + 1] = s;
+            s_ml[2 * h] = m;
+            s_ml[2 * h + 1] = s;
         }
     }
     __syncthreads();
@@ -347,18 +417,58 @@ __device__ void attend_group(const PersistParams &p, const float *qg, const floa
         part_h[(size_t)(j / hd) * hstride + 4 + j % hd] = a;
     }
     __syncthreads();
+    // The m and l words last, with release: a consumer that sees both tagged
+    // with this epoch also sees the head's acc values.
+    if (threadIdx.x < GROUP) {
+        unsigned long long *hw = reinterpret_cast<unsigned long long *>(part_h + (size_t)threadIdx.x * hstride);
+        st_word_release(hw, tagged(epoch, s_ml[2 * threadIdx.x]));
+        st_word_release(hw + 1, tagged(epoch, s_ml[2 * threadIdx.x + 1]));
+    }
 }
 
 // Attention of the current token over this CTA's keys at layer l (see the
 // file comment); partial results go to p.part[c][head][m, l, -, -, acc...].
 // nrm: the layer's norm weights in shared memory; the RoPE rows of pos are
 // in shared memory too.
+// rmsnorm_delta of one head (hd values at x in shared memory) then the
+// half-split rotation (rope_apply_fast, src/transformer/rope.c:65-80), by one
+// warp; lane owns the pairs (i, i + hd/2) for i = lane + 32 j.  The same
+// arithmetic as warp_norm_rope.
+__device__ void norm_rope_smem(const float *x, const float *w, float eps, const float *cs, const float *sn, int hd,
+                               float *dst) {
+    const int lane = threadIdx.x & 31, half = hd >> 1;
+    float a[kMaxHeadDim / 64], b[kMaxHeadDim / 64];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxHeadDim / 64; ++j) {
+        const int i = lane + 32 * j;
+        a[j] = i < half ? x[i] : 0.0f;
+        b[j] = i < half ? x[i + half] : 0.0f;
+        ss += a[j] * a[j] + b[j] * b[j];
+    }
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss / (float)hd + eps);
+#pragma unroll
+    for (int j = 0; j < kMaxHeadDim / 64; ++j) {
+        const int i = lane + 32 * j;
+        if (i < half) {
+            const float y0 = (a[j] * r) * (1.0f + w[i]);
+            const float y1 = (b[j] * r) * (1.0f + w[i + half]);
+            const float c = cs[i], sv = sn[i];
+            dst[i] = y0 * c - y1 * sv;
+            dst[i + half] = y1 * c + y0 * sv;
+        }
+    }
+}
+
 __device__ void attention_stage(const PersistParams &p, int l, int pos, uint8_t *smem, uint64_t *kv_bar,
-                                const float *nrm) {
+                                const float *nrm, unsigned e_qkv, unsigned epoch, int *s_abort) {
     int k0, n, nsplit;
     split_keys(p, l, pos, blockIdx.x, k0, n, nsplit);
     mbar_wait(kv_bar, (uint32_t)(l & 1), p);
     if (n <= 0) return;
+    float *vin = reinterpret_cast<float *>(smem + p.off_vin);
+    fetch_vec(p.qkv, (p.heads + 2 * p.kv_heads) * p.hd, e_qkv, vin, p, s_abort);
     const int heads = p.heads, kvh = p.kv_heads, hd = p.hd, group = heads / kvh, chunk = p.chunk;
     const int warp = threadIdx.x >> 5;
     const bool is_g = __ldg(p.layer_global + l) != 0;
@@ -375,9 +485,9 @@ __device__ void attention_stage(const PersistParams &p, int l, int pos, uint8_t 
     // The token's q and k (rmsnorm_delta per head with q_norm / k_norm, then
     // RoPE at pos) and v.
     for (int i = warp; i < heads + kvh; i += kPWarps)
-        warp_norm_rope(p.qkv + (size_t)i * hd, i < heads ? wq : wk, p.eps, rope, rope + hd, hd,
+        norm_rope_smem(vin + (size_t)i * hd, i < heads ? wq : wk, p.eps, rope, rope + hd, hd,
                        i < heads ? qs + (size_t)i * hd : kcur + (size_t)(i - heads) * hd);
-    for (int i = threadIdx.x; i < kvh * hd; i += kPersistThreads) vcur[i] = __ldcg(p.qkv + (size_t)(heads + kvh) * hd + i);
+    for (int i = threadIdx.x; i < kvh * hd; i += kPersistThreads) vcur[i] = vin[(size_t)(heads + kvh) * hd + i];
     __syncthreads();
     if (pos >= k0 && pos < k0 + n) {
         // This split holds the token: its K / V rows replace the stale rows
@@ -401,73 +511,93 @@ __device__ void attention_stage(const PersistParams &p, int l, int pos, uint8_t 
         const float *qg = qs + (size_t)kh * group * hd;
         float *part_h = p.part + ((size_t)blockIdx.x * heads + kh * group) * (hd + 4);
         switch (group) {   // persist_plan admits groups of 1, 2, 4 and 8
-            case 1: attend_group<1>(p, qg, Kh, Vh, n, sc, accs, part_h); break;
-            case 2: attend_group<2>(p, qg, Kh, Vh, n, sc, accs, part_h); break;
-            case 4: attend_group<4>(p, qg, Kh, Vh, n, sc, accs, part_h); break;
-            default: attend_group<8>(p, qg, Kh, Vh, n, sc, accs, part_h); break;
+            case 1: attend_group<1>(p, qg, Kh, Vh, n, sc, accs, part_h, epoch); break;
+            case 2: attend_group<2>(p, qg, Kh, Vh, n, sc, accs, part_h, epoch); break;
+            case 4: attend_group<4>(p, qg, Kh, Vh, n, sc, accs, part_h, epoch); break;
+            default: attend_group<8>(p, qg, Kh, Vh, n, sc, accs, part_h, epoch); break;
         }
     }
 }
 
-// attn = (sum_b exp(m_b - M) acc_b) / (sum_b exp(m_b - M) l_b) over the
-// splits of layer l (M = max_b m_b), into xs (zero-padded to the O stage's
-// width).  Thread (half q, quad j) reads the partials of splits b = q, q + 2,
-// ... for outputs 4j .. 4j + 3 (all loads of a batch issued together, a
-// running maximum rescales as it goes); the two halves are merged in order.
-__device__ void combine_stage(const PersistParams &p, int l, int pos, float *xs, float *scratch) {
+// attn = sum_b w_b acc_b with w_b = exp(m_b - M) / sum_b' exp(m_b' - M) l_b'
+// (M = max_b m_b) over the splits of layer l, into xs (zero-padded to the O
+// stage's width).  First the (m, l) words of every split and head are waited
+// for (acquire: the acc values behind them are then visible), then the
+// weights per head, then thread (half q, quad j) sums splits b = q, q + 2, ...
+// of outputs 4j .. 4j + 3 with all loads of a batch in flight; the two halves
+// are added in order.
+__device__ void combine_stage(const PersistParams &p, int l, int pos, float *xs, float *scratch, float *wts,
+                              unsigned epoch, int *s_abort) {
     int k0, n, nsplit;
     split_keys(p, l, pos, 0, k0, n, nsplit);
     const int heads = p.heads, hd = p.hd, width = p.stage_nb[kStO] * 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t hstride = (size_t)hd + 4;
+    // (m, l) of split b, head h -> wts[2 (b * heads + h) ..].
+    for (int t = threadIdx.x; t < nsplit * heads; t += kPersistThreads) {
+        const unsigned long long *hw = reinterpret_cast<const unsigned long long *>(p.part + (size_t)t * hstride);
+        unsigned long long m = ld_word_acquire(hw), lv = ld_word_acquire(hw + 1);
+        if ((unsigned)(m >> 32) != epoch || (unsigned)(lv >> 32) != epoch) {
+            const uint64_t t0 = gtimer();
+            unsigned it = 0;
+            while (((unsigned)(m >> 32) != epoch || (unsigned)(lv >> 32) != epoch) &&
+                   keep_waiting(p, s_abort, t0, it)) {
+                m = ld_word_acquire(hw);
+                lv = ld_word_acquire(hw + 1);
+            }
+        }
+        wts[2 * t] = __uint_as_float((unsigned)m);
+        wts[2 * t + 1] = __uint_as_float((unsigned)lv);
+    }
+    __syncthreads();
+    // w_b per head (one warp per head), in place of m_b.
+    for (int h = warp; h < heads; h += kPWarps) {
+        float mx = -INFINITY;
+        for (int b = lane; b < nsplit; b += 32) mx = fmaxf(mx, wts[2 * (b * heads + h)]);
+        const float M = warp_max(mx);
+        float L = 0.0f;
+        for (int b = lane; b < nsplit; b += 32) {
+            const float e = expf(wts[2 * (b * heads + h)] - M);
+            L += e * wts[2 * (b * heads + h) + 1];
+            wts[2 * (b * heads + h) + 1] = e;
+        }
+        L = warp_sum(L);
+        const float inv = 1.0f / L;
+        for (int b = lane; b < nsplit; b += 32) wts[2 * (b * heads + h)] = wts[2 * (b * heads + h) + 1] * inv;
+    }
+    __syncthreads();
     const int quads = heads * hd / 4;
     constexpr int kHalves = 2, kBatch = 8;
     for (int i = threadIdx.x; i < kHalves * quads; i += kPersistThreads) {
         const int q = i / quads, j = i % quads;
         const int h = (4 * j) / hd, d = (4 * j) % hd;
-        const float *base = p.part + (size_t)h * hstride;
-        float M = -INFINITY, L = 0.0f;
+        const float *base = p.part + (size_t)h * hstride + 4 + d;
         float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         for (int b0 = q; b0 < nsplit; b0 += kHalves * kBatch) {
-            float m[kBatch], lv[kBatch];
             float4 a[kBatch];
 #pragma unroll
             for (int k = 0; k < kBatch; ++k) {
                 const int b = b0 + kHalves * k;
-                const float *pp = base + (size_t)b * heads * hstride;
-                m[k] = b < nsplit ? __ldcg(pp) : -INFINITY;
-                lv[k] = b < nsplit ? __ldcg(pp + 1) : 0.0f;
-                a[k] = b < nsplit ? __ldcg(reinterpret_cast<const float4 *>(pp + 4 + d)) : make_float4(0, 0, 0, 0);
+                a[k] = b < nsplit ? __ldcg(reinterpret_cast<const float4 *>(base + (size_t)b * heads * hstride))
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             }
 #pragma unroll
             for (int k = 0; k < kBatch; ++k) {
-                if (m[k] == -INFINITY) continue;
-                const float Mn = fmaxf(M, m[k]);
-                const float c = expf(M - Mn), e = expf(m[k] - Mn);   // c = 0 while M is -inf
-                L = L * c + e * lv[k];
-                O.x = O.x * c + e * a[k].x;
-                O.y = O.y * c + e * a[k].y;
-                O.z = O.z * c + e * a[k].z;
-                O.w = O.w * c + e * a[k].w;
-                M = Mn;
+                const int b = b0 + kHalves * k;
+                const float w = b < nsplit ? wts[2 * (b * heads + h)] : 0.0f;
+                O.x = fmaf(w, a[k].x, O.x);
+                O.y = fmaf(w, a[k].y, O.y);
+                O.z = fmaf(w, a[k].z, O.z);
+                O.w = fmaf(w, a[k].w, O.w);
             }
         }
-        float *sp = scratch + (size_t)i * 8;
-        sp[0] = M;
-        sp[1] = L;
-        sp[4] = O.x;
-        sp[5] = O.y;
-        sp[6] = O.z;
-        sp[7] = O.w;
+        reinterpret_cast<float4 *>(scratch)[i] = O;
     }
     __syncthreads();
     for (int j = threadIdx.x; j < quads; j += kPersistThreads) {
-        const float *s0 = scratch + (size_t)j * 8, *s1 = scratch + (size_t)(quads + j) * 8;
-        const float M = fmaxf(s0[0], s1[0]);
-        const float c0 = s0[0] == -INFINITY ? 0.0f : expf(s0[0] - M);
-        const float c1 = s1[0] == -INFINITY ? 0.0f : expf(s1[0] - M);
-        const float inv = 1.0f / (s0[1] * c0 + s1[1] * c1);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) xs[4 * j + k] = (s0[4 + k] * c0 + s1[4 + k] * c1) * inv;
+        const float4 a = reinterpret_cast<const float4 *>(scratch)[j];
+        const float4 b = reinterpret_cast<const float4 *>(scratch)[quads + j];
+        reinterpret_cast<float4 *>(xs)[j] = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
     }
     for (int j = heads * hd + threadIdx.x; j < width; j += kPersistThreads) xs[j] = 0.0f;
     __syncthreads();
@@ -479,19 +609,27 @@ __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(c
     constexpr int kBarKv = kNumStages, kBarNorm = kNumStages + 1, kNumBars = kNumStages + 3;
     __shared__ __align__(8) uint64_t mbar[kNumBars];
     __shared__ float red[32];
-    __shared__ int s_fail;
+    __shared__ int s_abort;
     float *hidden = reinterpret_cast<float *>(smem + p.off_hidden);
     float *xs = reinterpret_cast<float *>(smem + p.off_x);
     float *scratch = reinterpret_cast<float *>(smem + p.off_acc);
+    float *vin = reinterpret_cast<float *>(smem + p.off_vin);
     const int H = p.hidden;
-    // The state is read once, before the first barrier (CTA 0 advances it
-    // after the last one in the prompt phase).
+    // This CTA's copies of the vectors every CTA reads.
+    const int rep = blockIdx.x % kPersistReplicas;
+    const unsigned long long *o_rep = p.o_out + (size_t)rep * H, *down_rep = p.down_out + (size_t)rep * H,
+                             *gu_rep = p.gu + (size_t)rep * 2 * p.ffn;
+    // The state and the launch count are read once, at the start: CTA 0
+    // changes them only after it has consumed the last stage, which every
+    // CTA contributed to.
     const int pos = *reinterpret_cast<volatile const int *>(&p.st->pos);
     int tok = *reinterpret_cast<volatile const int *>(&p.st->cur_token);
-    unsigned target = 0;
+    const unsigned launch = *reinterpret_cast<volatile const unsigned *>(p.ctl + 1);
+    // Epochs of this launch: 5 per layer (qkv, partials, o, gu, down).
+    const unsigned e0 = launch * (5u * (unsigned)p.layers + 1u);
 
     if (threadIdx.x == 0) {
-        s_fail = 0;
+        s_abort = 0;
         for (int i = 0; i < kNumBars; ++i) mbar_init(&mbar[i], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -514,100 +652,79 @@ __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(c
     for (int l = 0; l < p.layers; ++l) {
         const uint32_t par = (uint32_t)(l & 1);
         const bool more = l + 1 < p.layers;
+        const unsigned e_qkv = e0 + 5u * l + 1u, e_part = e_qkv + 1u, e_o = e_qkv + 2u, e_gu = e_qkv + 3u,
+                       e_down = e_qkv + 4u;
         // Norm weights of this layer (buffer l & 1, phase l / 2 of its barrier).
         mbar_wait(&mbar[kBarNorm + (l & 1)], (uint32_t)((l >> 1) & 1), p);
         const float *nrm = reinterpret_cast<const float *>(smem + p.off_nrm[l & 1]);
         const float *prev = reinterpret_cast<const float *>(smem + p.off_nrm[(l + 1) & 1]);
         __syncthreads();
         // QKV
-        if (l > 0) residual_add(hidden, p.down_out, prev + 3 * H, H, p.eps, xs, red);
+        if (l > 0) residual_add(hidden, down_rep, e_qkv - 1u, prev + 3 * H, H, xs, red, p, &s_abort);
         norm_to(hidden, nrm, H, p.stage_nb[kStQkv] * 32, p.eps, xs, red);
         mbar_wait(&mbar[kStQkv], par, p);
         __syncthreads();
-        gemv_stage(p, kStQkv, smem + p.off_w[kStQkv], xs, p.qkv);
+        gemv_stage(p, kStQkv, smem + p.off_w[kStQkv], xs, p.qkv, e_qkv, 1);
         __syncthreads();
         if (threadIdx.x == 0) {
             if (more) issue_stage(p, l + 1, kStQkv, smem, &mbar[kStQkv]);
             // The previous layer's norms are no longer read: fetch layer l + 1's.
             if (l >= 1 && more) issue_norms(p, l + 1, pos, false, smem, &mbar[kBarNorm + ((l + 1) & 1)]);
         }
-        grid_sync(p, target, &s_fail);
         // ATT
-        attention_stage(p, l, pos, smem, &mbar[kBarKv], nrm);
+        attention_stage(p, l, pos, smem, &mbar[kBarKv], nrm, e_qkv, e_part, &s_abort);
         __syncthreads();
         if (threadIdx.x == 0 && more) issue_kv(p, l + 1, pos, smem, &mbar[kBarKv]);
-        grid_sync(p, target, &s_fail);
         // O
-        combine_stage(p, l, pos, xs, scratch);
+        combine_stage(p, l, pos, xs, scratch, vin, e_part, &s_abort);
         mbar_wait(&mbar[kStO], par, p);
-        gemv_stage(p, kStO, smem + p.off_w[kStO], xs, p.o_out);
+        gemv_stage(p, kStO, smem + p.off_w[kStO], xs, p.o_out, e_o, kPersistReplicas);
         __syncthreads();
         if (threadIdx.x == 0 && more) issue_stage(p, l + 1, kStO, smem, &mbar[kStO]);
-        grid_sync(p, target, &s_fail);
         // GU
-        residual_add(hidden, p.o_out, nrm + H, H, p.eps, xs, red);
+        residual_add(hidden, o_rep, e_o, nrm + H, H, xs, red, p, &s_abort);
         norm_to(hidden, nrm + 2 * H, H, p.stage_nb[kStGu] * 32, p.eps, xs, red);
         mbar_wait(&mbar[kStGu], par, p);
         __syncthreads();
-        gemv_stage(p, kStGu, smem + p.off_w[kStGu], xs, p.gu);
+        gemv_stage(p, kStGu, smem + p.off_w[kStGu], xs, p.gu, e_gu, kPersistReplicas);
         __syncthreads();
         if (threadIdx.x == 0 && more) issue_stage(p, l + 1, kStGu, smem, &mbar[kStGu]);
-        grid_sync(p, target, &s_fail);
-        // DOWN: x = gelu_tanh(gate) * up, four values per thread and load.
+        // DOWN: x = gelu_tanh(gate) * up.
         {
             const int F = p.ffn, width = p.stage_nb[kStDown] * 32;
-            for (int i = 4 * threadIdx.x; i < width; i += 4 * kPersistThreads) {
-                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (i + 3 < F) {
-                    const float4 g = __ldcg(reinterpret_cast<const float4 *>(p.gu + i));
-                    const float4 u = __ldcg(reinterpret_cast<const float4 *>(p.gu + F + i));
-                    v = make_float4(geglu_tanh(g.x, u.x), geglu_tanh(g.y, u.y), geglu_tanh(g.z, u.z),
-                                    geglu_tanh(g.w, u.w));
-                } else {
-                    float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    for (int k = 0; k < 4; ++k)
-                        if (i + k < F) t[k] = geglu_tanh(__ldcg(p.gu + i + k), __ldcg(p.gu + F + i + k));
-                    v = make_float4(t[0], t[1], t[2], t[3]);
-                }
-                *reinterpret_cast<float4 *>(xs + i) = v;
-            }
+            fetch_vec(gu_rep, 2 * F, e_gu, vin, p, &s_abort);
+            for (int i = threadIdx.x; i < width; i += kPersistThreads) xs[i] = i < F ? geglu_tanh(vin[i], vin[F + i]) : 0.0f;
         }
         mbar_wait(&mbar[kStDown], par, p);
         __syncthreads();
-        gemv_stage(p, kStDown, smem + p.off_w[kStDown], xs, p.down_out);
+        gemv_stage(p, kStDown, smem + p.off_w[kStDown], xs, p.down_out, e_down, kPersistReplicas);
         __syncthreads();
         if (threadIdx.x == 0 && more) issue_stage(p, l + 1, kStDown, smem, &mbar[kStDown]);
-        grid_sync(p, target, &s_fail);
     }
 
     if (blockIdx.x == 0) {
+        const float *last = reinterpret_cast<const float *>(smem + p.off_nrm[(p.layers - 1) & 1]);
+        // h + rmsnorm_delta(down_out, ffn_post) of the last layer; waiting for
+        // it also means every CTA has passed its last read of this launch.
+        residual_add(hidden, down_rep, e0 + 5u * p.layers, last + 3 * H, H, xs, red, p, &s_abort);
         if (p.generate) {
-            // logits input: rmsnorm_delta(h + rmsnorm_delta(down_out, ffn_post), final) (transformer.c:393-408)
-            const float *last = reinterpret_cast<const float *>(smem + p.off_nrm[(p.layers - 1) & 1]);
-            residual_add(hidden, p.down_out, last + 3 * H, H, p.eps, xs, red);
+            // logits input: rmsnorm_delta(h, final) (transformer.c:393-408)
             float ss = 0.0f;
             for (int i = threadIdx.x; i < H; i += kPersistThreads) ss += hidden[i] * hidden[i];
             ss = block_sum(ss, red);
             const float r = 1.0f / sqrtf(ss / (float)H + p.eps);
             for (int i = threadIdx.x; i < H; i += kPersistThreads)
                 p.norm_out[i] = (hidden[i] * r) * (1.0f + __ldg(p.w_final + i));
-        } else if (threadIdx.x == 0) {
-            // Prompt phase: the next prompt token becomes the input at the next position.
-            const int i = p.st->prompt_index + 1;
-            p.st->prompt_index = i;
-            p.st->pos = pos + 1;
-            if (i < p.st->n_prompt) p.st->cur_token = p.prompt[i];
         }
-    }
-    // Exit: the last CTA out clears the barrier words for the next launch
-    // (every CTA has finished waiting by the time it counts itself out).
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        if (atomicAdd(p.bar + 1, 1u) == gridDim.x - 1) {
-            atomicExch(p.bar, 0u);
-            atomicExch(p.bar + 2, 0u);
-            atomicExch(p.bar + 1, 0u);
+        if (threadIdx.x == 0) {
+            if (!p.generate) {
+                // Prompt phase: the next prompt token becomes the input at the next position.
+                const int i = p.st->prompt_index + 1;
+                p.st->prompt_index = i;
+                p.st->pos = pos + 1;
+                if (i < p.st->n_prompt) p.st->cur_token = p.prompt[i];
+            }
+            p.ctl[1] = launch + 1u;
         }
     }
 }
@@ -652,6 +769,11 @@ size_t smem_layout(PersistParams &p, int G, int chunk) {
     const size_t group = (size_t)p.heads / p.kv_heads;
     p.off_acc = (unsigned)off;
     off = align128(off + std::max((size_t)kPersistThreads * group, (size_t)4 * p.heads * p.hd) * 4);
+    // Staged input vectors (qkv, gate / up) and the combine's (m, l) pairs.
+    size_t vin = std::max((size_t)(p.heads + 2 * p.kv_heads) * p.hd, (size_t)2 * p.ffn);
+    vin = std::max(vin, std::max((size_t)p.hidden, (size_t)2 * G * p.heads));
+    p.off_vin = (unsigned)off;
+    off = align128(off + vin * 4);
     p.off_cw = p.off_ml = 0;
     p.chunk = chunk;
     return off;
@@ -677,8 +799,9 @@ PersistPlan persist_plan(int device, const PersistParams &s, const char **why) {
         *why = "hidden / ffn / head_dim alignment";
         return plan;
     }
+    // Every CTA must have rows in every product (the buffers' reuse relies on it).
     for (int st = 0; st < kNumStages; ++st)
-        if (s.stage_stride[st] % 16 || s.stage_rows[st] <= 0) {
+        if (s.stage_stride[st] % 16 || s.stage_rows[st] < G) {
             *why = "row layout";
             return plan;
         }
