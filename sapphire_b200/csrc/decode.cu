@@ -871,8 +871,15 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
         pp.vocab = c.vocab;
         pp.window = c.sliding_window > 0 ? c.sliding_window : 1024;
         pp.norm_stride = 4 * c.hidden + 2 * c.head_dim;
-        const int stage_shape[kNumStages][2] = {
-            {d->q_dim + 2 * d->kv_dim, c.hidden}, {c.hidden, d->q_dim}, {2 * c.ffn, c.hidden}, {c.hidden, c.ffn}};
+        // Stage O is split by head: its row h * hidden + r is row r of Wo
+        // over head h's head_dim columns.
+        const int stage_shape[kNumStages][2] = {{d->q_dim + 2 * d->kv_dim, c.hidden},
+                                                 {c.heads * c.hidden, c.head_dim},
+                                                 {2 * c.ffn, c.hidden},
+                                                 {c.hidden, c.ffn}};
+        pp.global_mask = 0;
+        for (int l = 0; l < c.layers && l < 64; ++l)
+            if (c.global_mask ? ((c.global_mask >> l) & 1ULL) != 0 : ((l + 1) % 6 == 0)) pp.global_mask |= 1ULL << l;
         unsigned long long lb = 0;
         for (int s = 0; s < kNumStages; ++s) {
             pp.stage_rows[s] = stage_shape[s][0];
@@ -901,24 +908,32 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             std::vector<uint8_t> rows((size_t)lb * c.layers, 0);
             for (int l = 0; l < c.layers; ++l) {
                 const void *const *p = w->proj + 7 * l;
-                const std::vector<std::pair<const void *, int>> parts[kNumStages] = {
-                    {{p[0], d->q_dim}, {p[1], d->kv_dim}, {p[2], d->kv_dim}},
-                    {{p[3], c.hidden}},
-                    {{p[4], c.ffn}, {p[5], c.ffn}},
-                    {{p[6], c.hidden}}};
+                // Blocks [b0, b0 + nb) of a packed Q4_0 row into one row of the layout.
+                auto put_row = [](uint8_t *dst, const uint8_t *src, int nb, int b0) {
+                    for (int b = 0; b < nb; ++b) {
+                        memcpy(dst + 16 * b, src + 20 * (b0 + b) + 4, 16);
+                        memcpy(dst + 16 * nb + 4 * b, src + 20 * (b0 + b), 4);
+                    }
+                };
+                // (source, rows, source columns) of each stage; stage O by head.
+                const struct {
+                    const void *src;
+                    int rows, cols;
+                } parts[kNumStages][3] = {{{p[0], d->q_dim, c.hidden}, {p[1], d->kv_dim, c.hidden}, {p[2], d->kv_dim, c.hidden}},
+                                          {{p[3], c.hidden, d->q_dim}, {nullptr, 0, 0}, {nullptr, 0, 0}},
+                                          {{p[4], c.ffn, c.hidden}, {p[5], c.ffn, c.hidden}, {nullptr, 0, 0}},
+                                          {{p[6], c.hidden, c.ffn}, {nullptr, 0, 0}, {nullptr, 0, 0}}};
                 for (int s = 0; s < kNumStages; ++s) {
                     const int nb = pp.stage_nb[s], stride = pp.stage_stride[s];
-                    const size_t src_rb = sapphire_row_bytes_internal(DTYPE_Q4_0, stage_shape[s][1]);
                     uint8_t *dst = rows.data() + (size_t)l * lb + pp.stage_off[s];
-                    for (const auto &part : parts[s]) {
-                        const uint8_t *src = static_cast<const uint8_t *>(part.first);
-                        for (int r = 0; r < part.second; ++r, dst += stride, src += src_rb) {
-                            for (int b = 0; b < nb; ++b) {
-                                memcpy(dst + 16 * b, src + 20 * b + 4, 16);
-                                memcpy(dst + 16 * nb + 4 * b, src + 20 * b, 4);
-                            }
+                    const int pieces = s == kStO ? c.heads : 1;
+                    for (int h = 0; h < pieces; ++h)
+                        for (const auto &part : parts[s]) {
+                            if (!part.src) continue;
+                            const size_t src_rb = sapphire_row_bytes_internal(DTYPE_Q4_0, part.cols);
+                            const uint8_t *src = static_cast<const uint8_t *>(part.src);
+                            for (int r = 0; r < part.rows; ++r, dst += stride, src += src_rb) put_row(dst, src, nb, h * nb);
                         }
-                    }
                 }
             }
             if (dev_alloc(d, (void **)&d->wrows, rows.size()) ||
@@ -1006,10 +1021,7 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
         if (d->persist) {
             // Norm weights of every layer back to back (attn, attn_post, ffn,
             // ffn_post, q, k), copied from their uploaded vectors.
-            std::vector<int> glob;
-            for (auto &L : d->layers) glob.push_back(L.global ? 1 : 0);
             float *d_norms = nullptr;
-            int *d_glob = nullptr;
             if (dev_alloc(d, (void **)&d_norms, (size_t)c.layers * pp.norm_stride * 4)) break;
             bool copied = true;
             for (int l = 0; l < c.layers && copied; ++l) {
@@ -1024,10 +1036,9 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
                     dst += pr.second;
                 }
             }
-            if (!copied || dev_alloc(d, (void **)&d_glob, glob.size() * sizeof(int)) ||
-                dev_alloc(d, (void **)&d_glob, glob.size() * sizeof(int)) ||
+            if (!copied ||
                 dev_alloc(d, (void **)&pp.qkv, (size_t)(d->q_dim + 2 * d->kv_dim) * 8) ||
-                dev_alloc(d, (void **)&pp.o_out, (size_t)c.hidden * 8 * kPersistReplicas) ||
+                dev_alloc(d, (void **)&pp.o_out, (size_t)c.heads * c.hidden * 8 * kPersistReplicas) ||
                 dev_alloc(d, (void **)&pp.gu, (size_t)2 * c.ffn * 8 * kPersistReplicas) ||
                 dev_alloc(d, (void **)&pp.down_out, (size_t)c.hidden * 8 * kPersistReplicas) ||
                 dev_alloc(d, (void **)&pp.part, d->plan.part_floats * 4) ||
@@ -1035,16 +1046,12 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
                 break;
             // Tagged words start with epoch 0, which no launch uses.
             if (cudaMemset(pp.qkv, 0, (size_t)(d->q_dim + 2 * d->kv_dim) * 8) != cudaSuccess ||
-                cudaMemset(pp.o_out, 0, (size_t)c.hidden * 8 * kPersistReplicas) != cudaSuccess ||
+                cudaMemset(pp.o_out, 0, (size_t)c.heads * c.hidden * 8 * kPersistReplicas) != cudaSuccess ||
                 cudaMemset(pp.gu, 0, (size_t)2 * c.ffn * 8 * kPersistReplicas) != cudaSuccess ||
                 cudaMemset(pp.down_out, 0, (size_t)c.hidden * 8 * kPersistReplicas) != cudaSuccess ||
-                cudaMemset(pp.part, 0, d->plan.part_floats * 4) != cudaSuccess) {
-                ctx_fail(ctx, "sapphire_decoder_create", "persistent step buffers could not be cleared");
-                break;
-            }
-            if (cudaMemcpy(d_glob, glob.data(), glob.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemset(pp.part, 0, d->plan.part_floats * 4) != cudaSuccess ||
                 cudaMemset(d->ctl, 0, 4 * sizeof(unsigned)) != cudaSuccess) {
-                ctx_fail(ctx, "sapphire_decoder_create", "persistent step tables upload failed");
+                ctx_fail(ctx, "sapphire_decoder_create", "persistent step buffers could not be cleared");
                 break;
             }
             pp.st = d->state;
@@ -1056,7 +1063,6 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             pp.wrows = d->wrows;
             pp.norms = d_norms;
             pp.w_final = d->w_final;
-            pp.layer_global = d_glob;
             pp.rope_cos_g = d->rope_cos_g;
             pp.rope_sin_g = d->rope_sin_g;
             pp.rope_cos_l = d->rope_cos_l;

@@ -110,7 +110,7 @@ struct PersistParams {
     const float *norms;
     int norm_stride;
     const float *w_final;
-    const int *layer_global;      // [layers] 1 for global attention
+    unsigned long long global_mask;   // bit l: layer l attends globally (layers <= 64)
     const float *rope_cos_g, *rope_sin_g, *rope_cos_l, *rope_sin_l;
     float *kcache, *vcache;       // [layers][kv_heads][context][hd]
     // Stage outputs as epoch-tagged words (epoch << 32 | fp32 bits): a
@@ -118,11 +118,17 @@ struct PersistParams {
     // o_out, gu and down_out, which every CTA reads, are written in
     // kPersistReplicas copies ([replica][row]); CTA c polls copy c % kPersistReplicas.
     unsigned long long *qkv, *o_out, *gu, *down_out;
-    // Attention partials per split and head: [m word, l word, acc (hd floats)]
-    // (the m / l words are tagged and stored with release after acc).
+    // Attention partials per split and head, part[(b * heads + h)]: [m word,
+    // l word, acc (hd floats)] (the m / l words are tagged and stored with
+    // release after acc).  The O product is split by head: stage O's row
+    // h * hidden + r is row r of Wo restricted to head h's columns, and the
+    // residual adds the heads' partial rows in head order.
     float *part;
     float *norm_out;              // the LM head's input (plain floats)
-    int chunk;                    // keys per attention split
+    // Attention: CTA c works for query head c / splits on split c % splits;
+    // a window of len keys is cut into splits of max(chunk, ceil(len / splits))
+    // keys (at most chunk_max, what the key buffers hold).
+    int chunk, chunk_max, splits;
     unsigned *ctl;                // [0] abort flag, [1] launches so far (never cleared: the epoch base)
     int *err;
     unsigned long long wait_ns;   // bound of every wait

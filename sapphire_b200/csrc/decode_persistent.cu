@@ -59,7 +59,7 @@
 namespace {
 
 constexpr int kPWarps = kPersistThreads / 32;
-constexpr int kDefaultChunk = 32;
+constexpr int kDefaultChunk = 16;
 
 // ------------------------------------------------------------ PTX helpers --
 __device__ __forceinline__ uint32_t saddr(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -203,14 +203,26 @@ __device__ __forceinline__ void stage_rows(const PersistParams &p, int s, int &r
     r1 = (int)((c + 1) * R / G);
 }
 
-// Keys [k0, k0 + n) of the CTA's attention split at layer l (n = 0: none).
-__device__ __forceinline__ void split_keys(const PersistParams &p, int l, int pos, int c, int &k0, int &n,
-                                           int &nsplit) {
+// Attention work of CTA c at layer l: query head h = c / splits and keys
+// [k0, k0 + n) of split b = c % splits (n = 0: none); the window of the
+// layer (all positions for a global layer, the last `window` otherwise) is
+// cut into nsplit splits of `chunk` keys.
+struct Split {
+    int h, b, k0, n, chunk, nsplit;
+};
+__device__ __forceinline__ Split split_of(const PersistParams &p, int l, int pos, int c) {
+    Split sp;
     const int seq = pos + 1;
-    const int start = (!__ldg(p.layer_global + l) && seq > p.window) ? seq - p.window : 0;
-    nsplit = (seq - start + p.chunk - 1) / p.chunk;
-    k0 = start + c * p.chunk;
-    n = c < nsplit ? min(p.chunk, seq - k0) : 0;
+    const bool global = (p.global_mask >> l) & 1ull;
+    const int start = (!global && seq > p.window) ? seq - p.window : 0;
+    const int len = seq - start;
+    sp.chunk = max(p.chunk, (len + p.splits - 1) / p.splits);
+    sp.nsplit = (len + sp.chunk - 1) / sp.chunk;
+    sp.h = c / p.splits;
+    sp.b = c % p.splits;
+    sp.k0 = start + sp.b * sp.chunk;
+    sp.n = (sp.h < p.heads && sp.b < sp.nsplit) ? min(sp.chunk, seq - sp.k0) : 0;
+    return sp;
 }
 
 // Thread 0: fetch this CTA's rows of stage s of layer l into its buffer.
@@ -227,22 +239,21 @@ __device__ void issue_stage(const PersistParams &p, int l, int s, uint8_t *smem,
     bulk_g2s(smem + p.off_w[s], src, bytes, bar);
 }
 
-// Thread 0: fetch the K and V rows of this CTA's split of layer l.  The row
-// of pos itself is stale (this step writes it) and is replaced after the wait.
+// Thread 0: fetch the K and V rows of this CTA's split of layer l (of its
+// head's KV head).  The row of pos itself is stale (this step writes it) and
+// is replaced after the wait.
 __device__ void issue_kv(const PersistParams &p, int l, int pos, uint8_t *smem, uint64_t *bar) {
-    int k0, n, nsplit;
-    split_keys(p, l, pos, blockIdx.x, k0, n, nsplit);
-    if (n <= 0) {
+    const Split sp = split_of(p, l, pos, blockIdx.x);
+    if (sp.n <= 0) {
         mbar_arrive(bar);
         return;
     }
-    const uint32_t row = (uint32_t)p.hd * 4u, bytes = (uint32_t)n * row;
-    mbar_arrive_tx(bar, 2u * (uint32_t)p.kv_heads * bytes);
-    for (int kh = 0; kh < p.kv_heads; ++kh) {
-        const size_t off = (((size_t)l * p.kv_heads + kh) * p.context + k0) * p.hd;
-        bulk_g2s(smem + p.off_k + (size_t)kh * p.chunk * row, p.kcache + off, bytes, bar);
-        bulk_g2s(smem + p.off_v + (size_t)kh * p.chunk * row, p.vcache + off, bytes, bar);
-    }
+    const int kh = sp.h / (p.heads / p.kv_heads);
+    const uint32_t bytes = (uint32_t)sp.n * (uint32_t)p.hd * 4u;
+    mbar_arrive_tx(bar, 2u * bytes);
+    const size_t off = (((size_t)l * p.kv_heads + kh) * p.context + sp.k0) * p.hd;
+    bulk_g2s(smem + p.off_k, p.kcache + off, bytes, bar);
+    bulk_g2s(smem + p.off_v, p.vcache + off, bytes, bar);
 }
 
 // Thread 0: fetch layer l's norm weights into buffer l & 1 (and, with `rope`,
@@ -260,11 +271,21 @@ __device__ void issue_norms(const PersistParams &p, int l, int pos, bool rope, u
     }
 }
 
-// hidden += rmsnorm_delta(t, w) for t the tagged output of the stage before
-// (fetched into xs).  Same per-element arithmetic as residual_norm_kernel.
-__device__ void residual_add(float *hidden, const unsigned long long *t, unsigned epoch, const float *w, int n,
-                             float *xs, float *red, const PersistParams &p, int *s_abort) {
-    fetch_vec(t, n, epoch, xs, p, s_abort);
+// hidden += rmsnorm_delta(t, w) for t the tagged output of the stage before,
+// given as `nparts` partial vectors added in order (fetched through vin into
+// xs).  Same per-element arithmetic as residual_norm_kernel.
+__device__ void residual_add(float *hidden, const unsigned long long *t, int nparts, unsigned epoch, const float *w,
+                             int n, float *xs, float *vin, float *red, const PersistParams &p, int *s_abort) {
+    if (nparts == 1) {
+        fetch_vec(t, n, epoch, xs, p, s_abort);
+    } else {
+        fetch_vec(t, nparts * n, epoch, vin, p, s_abort);
+        for (int i = threadIdx.x; i < n; i += kPersistThreads) {
+            float v = vin[i];
+            for (int k = 1; k < nparts; ++k) v += vin[(size_t)k * n + i];
+            xs[i] = v;
+        }
+    }
     float ss = 0.0f;
     for (int i = threadIdx.x; i < n; i += kPersistThreads) ss += xs[i] * xs[i];
     ss = block_sum(ss, red);
@@ -304,7 +325,7 @@ __device__ __forceinline__ float q4_word_dot(uint32_t code, float4 x0, float4 x1
 // of a row takes 4-byte code word k (8 weights of block k / 4) and its x
 // values xs[8k .. 8k + 8).
 __device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, const float *xs, unsigned long long *y,
-                           unsigned epoch, int replicas) {
+                           unsigned epoch, int replicas, int seg = 0, int seg0 = 0) {
     int r0, r1;
     stage_rows(p, s, r0, r1);
     const int nb = p.stage_nb[s], stride = p.stage_stride[s], nwords = nb * 4, nr = r1 - r0;
@@ -315,14 +336,20 @@ __device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, cons
         const uint8_t *row = w + (size_t)r * stride, *row2 = w + (size_t)(two ? r2 : r) * stride;
         const float *sc = reinterpret_cast<const float *>(row + (size_t)nb * 16);
         const float *sc2 = reinterpret_cast<const float *>(row2 + (size_t)nb * 16);
+        // With seg > 0, row r' of the stage reads x segment r' / seg - seg0
+        // (nb * 32 values each); otherwise every row reads xs.
+        const float *x1p = seg ? xs + (size_t)((r0 + r) / seg - seg0) * nb * 32 : xs;
+        const float *x2p = seg ? xs + (size_t)((r0 + (two ? r2 : r)) / seg - seg0) * nb * 32 : xs;
         float acc = 0.0f, acc2 = 0.0f;
         for (int k = lane; k < nwords; k += 32) {
             const uint32_t c1 = *reinterpret_cast<const uint32_t *>(row + 4 * k);
             const uint32_t c2 = *reinterpret_cast<const uint32_t *>(row2 + 4 * k);
-            const float4 x0 = *reinterpret_cast<const float4 *>(xs + 8 * k);
-            const float4 x1 = *reinterpret_cast<const float4 *>(xs + 8 * k + 4);
-            acc = fmaf(sc[k >> 2], q4_word_dot(c1, x0, x1), acc);
-            acc2 = fmaf(sc2[k >> 2], q4_word_dot(c2, x0, x1), acc2);
+            const float4 a0 = *reinterpret_cast<const float4 *>(x1p + 8 * k);
+            const float4 a1 = *reinterpret_cast<const float4 *>(x1p + 8 * k + 4);
+            const float4 b0 = *reinterpret_cast<const float4 *>(x2p + 8 * k);
+            const float4 b1 = *reinterpret_cast<const float4 *>(x2p + 8 * k + 4);
+            acc = fmaf(sc[k >> 2], q4_word_dot(c1, a0, a1), acc);
+            acc2 = fmaf(sc2[k >> 2], q4_word_dot(c2, b0, b1), acc2);
         }
         acc = warp_sum(acc);
         acc2 = warp_sum(acc2);
@@ -335,101 +362,6 @@ __device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, cons
     }
 }
 
-// Scores, softmax partial and weighted value sum of the GROUP query heads of
-// one KV head over the CTA's n staged keys; results go to part_h (the part
-// rows of the group's first head): [m, l, -, -, acc...] per head.
-template <int GROUP>
-__device__ void attend_group(const PersistParams &p, const float *qg, const float *Kh, const float *Vh, int n,
-                             float *sc, float *accs, float *part_h, unsigned epoch) {
-    __shared__ float s_ml[2 * GROUP];
-    constexpr int NJ = kMaxHeadDim / 32;
-    const int hd = p.hd, nj = hd / 32, chunk = p.chunk;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t hstride = (size_t)hd + 4;
-    // Scores: one warp per key, the group's q rows in registers (lane holds
-    // the values d = lane + 32 j), four heads' reductions interleaved.
-    {
-        float q[GROUP][NJ];
-#pragma unroll
-        for (int h = 0; h < GROUP; ++h)
-#pragma unroll
-            for (int j = 0; j < NJ; ++j) q[h][j] = j < nj ? qg[(size_t)h * hd + lane + 32 * j] : 0.0f;
-        for (int t = warp; t < n; t += kPWarps) {
-            float kv[NJ];
-#pragma unroll
-            for (int j = 0; j < NJ; ++j) kv[j] = j < nj ? Kh[(size_t)t * hd + lane + 32 * j] : 0.0f;
-            float a[GROUP];
-#pragma unroll
-            for (int h = 0; h < GROUP; ++h) {
-                a[h] = 0.0f;
-#pragma unroll
-                for (int j = 0; j < NJ; ++j) a[h] = fmaf(q[h][j], kv[j], a[h]);
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (int h = 0; h < GROUP; ++h) a[h] += __shfl_xor_sync(0xffffffffu, a[h], o);
-            if (lane == 0)
-#pragma unroll
-                for (int h = 0; h < GROUP; ++h) sc[h * chunk + t] = a[h] * p.att_scale;
-        }
-    }
-    __syncthreads();
-    // Softmax partial per head: m = max score, p = exp(s - m), l = sum p.
-    for (int h = warp; h < GROUP; h += kPWarps) {
-        float m = -INFINITY;
-        for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[h * chunk + t]);
-        m = warp_max(m);
-        float s = 0.0f;
-        for (int t = lane; t < n; t += 32) {
-            const float e = expf(sc[h * chunk + t] - m);
-            sc[h * chunk + t] = e;
-            s += e;
-        }
-        s = warp_sum(s);
-        if (lane == 0) {
-            s_ml[2 * h] = m;
-            s_ml[2 * h + 1] = s;
-        }
-    }
-    __syncthreads();
-    // acc = sum_t p_t v_t: thread (part q, dimension d) sums the keys
-    // t = q, q + parts, ... for every head of the group; then the parts are
-    // added in order.
-    const int parts = kPersistThreads / hd;
-    {
-        const int d = threadIdx.x % hd, q = threadIdx.x / hd;
-        float a[GROUP];
-#pragma unroll
-        for (int h = 0; h < GROUP; ++h) a[h] = 0.0f;
-        for (int t = q; t < n; t += parts) {
-            const float v = Vh[(size_t)t * hd + d];
-#pragma unroll
-            for (int h = 0; h < GROUP; ++h) a[h] = fmaf(sc[h * chunk + t], v, a[h]);
-        }
-#pragma unroll
-        for (int h = 0; h < GROUP; ++h) accs[((size_t)q * GROUP + h) * hd + d] = a[h];
-    }
-    __syncthreads();
-    for (int j = threadIdx.x; j < GROUP * hd; j += kPersistThreads) {
-        float a = accs[j];
-        for (int q = 1; q < parts; ++q) a += accs[(size_t)q * GROUP * hd + j];
-        part_h[(size_t)(j / hd) * hstride + 4 + j % hd] = a;
-    }
-    __syncthreads();
-    // The m and l words last, with release: a consumer that sees both tagged
-    // with this epoch also sees the head's acc values.
-    if (threadIdx.x < GROUP) {
-        unsigned long long *hw = reinterpret_cast<unsigned long long *>(part_h + (size_t)threadIdx.x * hstride);
-        st_word_release(hw, tagged(epoch, s_ml[2 * threadIdx.x]));
-        st_word_release(hw + 1, tagged(epoch, s_ml[2 * threadIdx.x + 1]));
-    }
-}
-
-// Attention of the current token over this CTA's keys at layer l (see the
-// file comment); partial results go to p.part[c][head][m, l, -, -, acc...].
-// nrm: the layer's norm weights in shared memory; the RoPE rows of pos are
-// in shared memory too.
 // rmsnorm_delta of one head (hd values at x in shared memory) then the
 // half-split rotation (rope_apply_fast, src/transformer/rope.c:65-80), by one
 // warp; lane owns the pairs (i, i + hd/2) for i = lane + 32 j.  The same
@@ -461,18 +393,24 @@ __device__ void norm_rope_smem(const float *x, const float *w, float eps, const 
     }
 }
 
+// Attention of the current token for query head h over the keys of split b
+// at layer l (see the file comment); the partial result goes to
+// p.part[b * heads + h]: [m, l, -, -, acc...], the m / l words last.
+// nrm: the layer's norm weights in shared memory; the RoPE rows of pos are in
+// shared memory too.
 __device__ void attention_stage(const PersistParams &p, int l, int pos, uint8_t *smem, uint64_t *kv_bar,
                                 const float *nrm, unsigned e_qkv, unsigned epoch, int *s_abort) {
-    int k0, n, nsplit;
-    split_keys(p, l, pos, blockIdx.x, k0, n, nsplit);
+    __shared__ float s_ml[2];
+    const Split sp = split_of(p, l, pos, blockIdx.x);
     mbar_wait(kv_bar, (uint32_t)(l & 1), p);
-    if (n <= 0) return;
+    if (sp.n <= 0) return;
+    const int heads = p.heads, kvh = p.kv_heads, hd = p.hd, group = heads / kvh, n = sp.n, h = sp.h;
+    const int kh = h / group;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float *vin = reinterpret_cast<float *>(smem + p.off_vin);
-    fetch_vec(p.qkv, (p.heads + 2 * p.kv_heads) * p.hd, e_qkv, vin, p, s_abort);
-    const int heads = p.heads, kvh = p.kv_heads, hd = p.hd, group = heads / kvh, chunk = p.chunk;
-    const int warp = threadIdx.x >> 5;
-    const bool is_g = __ldg(p.layer_global + l) != 0;
-    const float *rope = reinterpret_cast<const float *>(smem + p.off_rope) + (is_g ? 0 : 2 * hd);
+    fetch_vec(p.qkv, (heads + 2 * kvh) * hd, e_qkv, vin, p, s_abort);
+    const bool global = (p.global_mask >> l) & 1ull;
+    const float *rope = reinterpret_cast<const float *>(smem + p.off_rope) + (global ? 0 : 2 * hd);
     const float *wq = nrm + 4 * p.hidden, *wk = wq + hd;
     float *qs = reinterpret_cast<float *>(smem + p.off_q);
     float *kcur = reinterpret_cast<float *>(smem + p.off_kcur);
@@ -482,125 +420,182 @@ __device__ void attention_stage(const PersistParams &p, int l, int pos, uint8_t 
     float *sc = reinterpret_cast<float *>(smem + p.off_sc);
     float *accs = reinterpret_cast<float *>(smem + p.off_acc);
 
-    // The token's q and k (rmsnorm_delta per head with q_norm / k_norm, then
-    // RoPE at pos) and v.
-    for (int i = warp; i < heads + kvh; i += kPWarps)
-        norm_rope_smem(vin + (size_t)i * hd, i < heads ? wq : wk, p.eps, rope, rope + hd, hd,
-                       i < heads ? qs + (size_t)i * hd : kcur + (size_t)(i - heads) * hd);
-    for (int i = threadIdx.x; i < kvh * hd; i += kPersistThreads) vcur[i] = vin[(size_t)(heads + kvh) * hd + i];
+    // The token's q of head h and k of its KV head (rmsnorm_delta with
+    // q_norm / k_norm, then RoPE at pos), and v.
+    if (warp == 0) norm_rope_smem(vin + (size_t)h * hd, wq, p.eps, rope, rope + hd, hd, qs);
+    if (warp == 1) norm_rope_smem(vin + (size_t)(heads + kh) * hd, wk, p.eps, rope, rope + hd, hd, kcur);
+    for (int i = threadIdx.x; i < hd; i += kPersistThreads) vcur[i] = vin[(size_t)(heads + kvh + kh) * hd + i];
     __syncthreads();
-    if (pos >= k0 && pos < k0 + n) {
+    if (pos >= sp.k0 && pos < sp.k0 + n) {
         // This split holds the token: its K / V rows replace the stale rows
-        // fetched with the split and are stored for later steps.
-        const int t = pos - k0;
-        for (int i = threadIdx.x; i < kvh * hd; i += kPersistThreads) {
-            const int kh = i / hd, d = i % hd;
-            K[((size_t)kh * chunk + t) * hd + d] = kcur[i];
-            V[((size_t)kh * chunk + t) * hd + d] = vcur[i];
-            const size_t g = (((size_t)l * kvh + kh) * p.context + pos) * hd + d;
-            p.kcache[g] = kcur[i];
-            p.vcache[g] = vcur[i];
+        // fetched with the split; the group's first head stores them for
+        // later steps.
+        const int t = pos - sp.k0;
+        const bool store = h % group == 0;
+        const size_t g = (((size_t)l * kvh + kh) * p.context + pos) * hd;
+        for (int d = threadIdx.x; d < hd; d += kPersistThreads) {
+            K[(size_t)t * hd + d] = kcur[d];
+            V[(size_t)t * hd + d] = vcur[d];
+            if (store) {
+                p.kcache[g + d] = kcur[d];
+                p.vcache[g + d] = vcur[d];
+            }
         }
         // The next layer's keys are fetched into these buffers by the async
         // proxy: order these generic writes before that.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
     }
-    for (int kh = 0; kh < kvh; ++kh) {
-        const float *Kh = K + (size_t)kh * chunk * hd, *Vh = V + (size_t)kh * chunk * hd;
-        const float *qg = qs + (size_t)kh * group * hd;
-        float *part_h = p.part + ((size_t)blockIdx.x * heads + kh * group) * (hd + 4);
-        switch (group) {   // persist_plan admits groups of 1, 2, 4 and 8
-            case 1: attend_group<1>(p, qg, Kh, Vh, n, sc, accs, part_h, epoch); break;
-            case 2: attend_group<2>(p, qg, Kh, Vh, n, sc, accs, part_h, epoch); break;
-            case 4: attend_group<4>(p, qg, Kh, Vh, n, sc, accs, part_h, epoch); break;
-            default: attend_group<8>(p, qg, Kh, Vh, n, sc, accs, part_h, epoch); break;
+    constexpr int NJ = kMaxHeadDim / 32;
+    const int nj = hd / 32;
+    // Scores: one warp per key, q in registers (lane holds d = lane + 32 j).
+    {
+        float q[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) q[j] = j < nj ? qs[lane + 32 * j] : 0.0f;
+        for (int t = warp; t < n; t += kPWarps) {
+            float a = 0.0f;
+#pragma unroll
+            for (int j = 0; j < NJ; ++j)
+                if (j < nj) a = fmaf(q[j], K[(size_t)t * hd + lane + 32 * j], a);
+            a = warp_sum(a);
+            if (lane == 0) sc[t] = a * p.att_scale;
         }
+    }
+    __syncthreads();
+    // Softmax partial: m = max score, p = exp(s - m), l = sum p.
+    if (warp == 0) {
+        float m = -INFINITY;
+        for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[t]);
+        m = warp_max(m);
+        float s = 0.0f;
+        for (int t = lane; t < n; t += 32) {
+            const float e = expf(sc[t] - m);
+            sc[t] = e;
+            s += e;
+        }
+        s = warp_sum(s);
+        if (lane == 0) {
+            s_ml[0] = m;
+            s_ml[1] = s;
+        }
+    }
+    __syncthreads();
+    // acc = sum_t p_t v_t: thread (part q, dimension d) sums the keys
+    // t = q, q + parts, ...; then the parts are added in order.
+    const int parts = kPersistThreads / hd;
+    {
+        const int d = threadIdx.x % hd, q = threadIdx.x / hd;
+        float a = 0.0f;
+        for (int t = q; t < n; t += parts) a = fmaf(sc[t], V[(size_t)t * hd + d], a);
+        accs[(size_t)q * hd + d] = a;
+    }
+    __syncthreads();
+    float *row = p.part + ((size_t)sp.b * heads + h) * (hd + 4);
+    for (int d = threadIdx.x; d < hd; d += kPersistThreads) {
+        float a = accs[d];
+        for (int q = 1; q < parts; ++q) a += accs[(size_t)q * hd + d];
+        row[4 + d] = a;
+    }
+    __syncthreads();
+    // The m and l words last, with release: a consumer that sees both tagged
+    // with this epoch also sees the acc values.
+    if (threadIdx.x == 0) {
+        unsigned long long *hw = reinterpret_cast<unsigned long long *>(row);
+        st_word_release(hw, tagged(epoch, s_ml[0]));
+        st_word_release(hw + 1, tagged(epoch, s_ml[1]));
     }
 }
 
-// attn = sum_b w_b acc_b with w_b = exp(m_b - M) / sum_b' exp(m_b' - M) l_b'
-// (M = max_b m_b) over the splits of layer l, into xs (zero-padded to the O
-// stage's width).  First the (m, l) words of every split and head are waited
-// for (acquire: the acc values behind them are then visible), then the
-// weights per head, then thread (half q, quad j) sums splits b = q, q + 2, ...
-// of outputs 4j .. 4j + 3 with all loads of a batch in flight; the two halves
-// are added in order.
-__device__ void combine_stage(const PersistParams &p, int l, int pos, float *xs, float *scratch, float *wts,
-                              unsigned epoch, int *s_abort) {
-    int k0, n, nsplit;
-    split_keys(p, l, pos, 0, k0, n, nsplit);
-    const int heads = p.heads, hd = p.hd, width = p.stage_nb[kStO] * 32;
+// attn_h = sum_b w_b acc_b with w_b = exp(m_b - M) / sum_b' exp(m_b' - M) l_b'
+// (M = max_b m_b) over the splits of layer l, for the heads h0 .. h0 + nh - 1
+// that this CTA's rows of the head-split O product use, into xs ([nh][hd]).
+// First one warp per head waits for the (m, l) words of every split (acquire:
+// the acc values behind them are then visible) and forms the weights; then
+// thread (part q, quad j) sums splits b = q, q + P, ... of outputs
+// 4j .. 4j + 3 with all loads of a batch in flight; the parts are added in
+// order.  Returns h0.
+__device__ int combine_stage(const PersistParams &p, int l, int pos, float *xs, float *scratch, float *wts,
+                             unsigned epoch, int *s_abort) {
+    int r0, r1;
+    stage_rows(p, kStO, r0, r1);
+    const int H = p.hidden, hd = p.hd, heads = p.heads, S = p.splits;
+    const int h0 = r0 / H, nh = (r1 - 1) / H - h0 + 1;
+    const int nsplit = split_of(p, l, pos, 0).nsplit;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t hstride = (size_t)hd + 4;
-    // (m, l) of split b, head h -> wts[2 (b * heads + h) ..].
-    for (int t = threadIdx.x; t < nsplit * heads; t += kPersistThreads) {
-        const unsigned long long *hw = reinterpret_cast<const unsigned long long *>(p.part + (size_t)t * hstride);
-        unsigned long long m = ld_word_acquire(hw), lv = ld_word_acquire(hw + 1);
-        if ((unsigned)(m >> 32) != epoch || (unsigned)(lv >> 32) != epoch) {
-            const uint64_t t0 = gtimer();
-            unsigned it = 0;
-            while (((unsigned)(m >> 32) != epoch || (unsigned)(lv >> 32) != epoch) &&
-                   keep_waiting(p, s_abort, t0, it)) {
-                m = ld_word_acquire(hw);
-                lv = ld_word_acquire(hw + 1);
-            }
-        }
-        wts[2 * t] = __uint_as_float((unsigned)m);
-        wts[2 * t + 1] = __uint_as_float((unsigned)lv);
-    }
-    __syncthreads();
-    // w_b per head (one warp per head), in place of m_b.
-    for (int h = warp; h < heads; h += kPWarps) {
+    for (int w = warp; w < nh; w += kPWarps) {
+        const int h = h0 + w;
+        float *wm = wts + (size_t)w * 2 * S, *wl = wm + S;
         float mx = -INFINITY;
-        for (int b = lane; b < nsplit; b += 32) mx = fmaxf(mx, wts[2 * (b * heads + h)]);
+        for (int b = lane; b < nsplit; b += 32) {
+            const unsigned long long *hw =
+                reinterpret_cast<const unsigned long long *>(p.part + ((size_t)b * heads + h) * hstride);
+            unsigned long long m = ld_word_acquire(hw), lv = ld_word_acquire(hw + 1);
+            if ((unsigned)(m >> 32) != epoch || (unsigned)(lv >> 32) != epoch) {
+                const uint64_t t0 = gtimer();
+                unsigned it = 0;
+                while (((unsigned)(m >> 32) != epoch || (unsigned)(lv >> 32) != epoch) &&
+                       keep_waiting(p, s_abort, t0, it)) {
+                    m = ld_word_acquire(hw);
+                    lv = ld_word_acquire(hw + 1);
+                }
+            }
+            wm[b] = __uint_as_float((unsigned)m);
+            wl[b] = __uint_as_float((unsigned)lv);
+            mx = fmaxf(mx, wm[b]);
+        }
         const float M = warp_max(mx);
         float L = 0.0f;
         for (int b = lane; b < nsplit; b += 32) {
-            const float e = expf(wts[2 * (b * heads + h)] - M);
-            L += e * wts[2 * (b * heads + h) + 1];
-            wts[2 * (b * heads + h) + 1] = e;
+            const float e = expf(wm[b] - M);
+            wm[b] = e;
+            L += e * wl[b];
         }
-        L = warp_sum(L);
-        const float inv = 1.0f / L;
-        for (int b = lane; b < nsplit; b += 32) wts[2 * (b * heads + h)] = wts[2 * (b * heads + h) + 1] * inv;
+        const float inv = 1.0f / warp_sum(L);
+        for (int b = lane; b < nsplit; b += 32) wm[b] *= inv;
     }
     __syncthreads();
-    const int quads = heads * hd / 4;
-    constexpr int kHalves = 2, kBatch = 8;
-    for (int i = threadIdx.x; i < kHalves * quads; i += kPersistThreads) {
+    const int quads = nh * hd / 4;
+    const int P = max(1, kPersistThreads / quads);
+    constexpr int kBatch = 8;
+    for (int i = threadIdx.x; i < P * quads; i += kPersistThreads) {
         const int q = i / quads, j = i % quads;
-        const int h = (4 * j) / hd, d = (4 * j) % hd;
-        const float *base = p.part + (size_t)h * hstride + 4 + d;
+        const int w = (4 * j) / hd, d = (4 * j) % hd;
+        const float *base = p.part + (size_t)(h0 + w) * hstride + 4 + d;
+        const float *wm = wts + (size_t)w * 2 * S;
         float4 O = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int b0 = q; b0 < nsplit; b0 += kHalves * kBatch) {
+        for (int b0 = q; b0 < nsplit; b0 += P * kBatch) {
             float4 a[kBatch];
 #pragma unroll
             for (int k = 0; k < kBatch; ++k) {
-                const int b = b0 + kHalves * k;
+                const int b = b0 + P * k;
                 a[k] = b < nsplit ? __ldcg(reinterpret_cast<const float4 *>(base + (size_t)b * heads * hstride))
                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             }
 #pragma unroll
             for (int k = 0; k < kBatch; ++k) {
-                const int b = b0 + kHalves * k;
-                const float w = b < nsplit ? wts[2 * (b * heads + h)] : 0.0f;
-                O.x = fmaf(w, a[k].x, O.x);
-                O.y = fmaf(w, a[k].y, O.y);
-                O.z = fmaf(w, a[k].z, O.z);
-                O.w = fmaf(w, a[k].w, O.w);
+                const int b = b0 + P * k;
+                const float wb = b < nsplit ? wm[b] : 0.0f;
+                O.x = fmaf(wb, a[k].x, O.x);
+                O.y = fmaf(wb, a[k].y, O.y);
+                O.z = fmaf(wb, a[k].z, O.z);
+                O.w = fmaf(wb, a[k].w, O.w);
             }
         }
         reinterpret_cast<float4 *>(scratch)[i] = O;
     }
     __syncthreads();
     for (int j = threadIdx.x; j < quads; j += kPersistThreads) {
-        const float4 a = reinterpret_cast<const float4 *>(scratch)[j];
-        const float4 b = reinterpret_cast<const float4 *>(scratch)[quads + j];
-        reinterpret_cast<float4 *>(xs)[j] = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+        float4 o = reinterpret_cast<const float4 *>(scratch)[j];
+        for (int q = 1; q < P; ++q) {
+            const float4 a = reinterpret_cast<const float4 *>(scratch)[(size_t)q * quads + j];
+            o = make_float4(o.x + a.x, o.y + a.y, o.z + a.z, o.w + a.w);
+        }
+        reinterpret_cast<float4 *>(xs)[j] = o;
     }
-    for (int j = heads * hd + threadIdx.x; j < width; j += kPersistThreads) xs[j] = 0.0f;
     __syncthreads();
+    return h0;
 }
 
 __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(const __grid_constant__ PersistParams p) {
@@ -617,7 +612,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(c
     const int H = p.hidden;
     // This CTA's copies of the vectors every CTA reads.
     const int rep = blockIdx.x % kPersistReplicas;
-    const unsigned long long *o_rep = p.o_out + (size_t)rep * H, *down_rep = p.down_out + (size_t)rep * H,
+    const unsigned long long *o_rep = p.o_out + (size_t)rep * p.stage_rows[kStO],
+                             *down_rep = p.down_out + (size_t)rep * H,
                              *gu_rep = p.gu + (size_t)rep * 2 * p.ffn;
     // The state and the launch count are read once, at the start: CTA 0
     // changes them only after it has consumed the last stage, which every
@@ -660,7 +656,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(c
         const float *prev = reinterpret_cast<const float *>(smem + p.off_nrm[(l + 1) & 1]);
         __syncthreads();
         // QKV
-        if (l > 0) residual_add(hidden, down_rep, e_qkv - 1u, prev + 3 * H, H, xs, red, p, &s_abort);
+        if (l > 0) residual_add(hidden, down_rep, 1, e_qkv - 1u, prev + 3 * H, H, xs, vin, red, p, &s_abort);
         norm_to(hidden, nrm, H, p.stage_nb[kStQkv] * 32, p.eps, xs, red);
         mbar_wait(&mbar[kStQkv], par, p);
         __syncthreads();
@@ -676,13 +672,13 @@ __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(c
         __syncthreads();
         if (threadIdx.x == 0 && more) issue_kv(p, l + 1, pos, smem, &mbar[kBarKv]);
         // O
-        combine_stage(p, l, pos, xs, scratch, vin, e_part, &s_abort);
+        const int h0 = combine_stage(p, l, pos, xs, scratch, vin, e_part, &s_abort);
         mbar_wait(&mbar[kStO], par, p);
-        gemv_stage(p, kStO, smem + p.off_w[kStO], xs, p.o_out, e_o, kPersistReplicas);
+        gemv_stage(p, kStO, smem + p.off_w[kStO], xs, p.o_out, e_o, kPersistReplicas, H, h0);
         __syncthreads();
         if (threadIdx.x == 0 && more) issue_stage(p, l + 1, kStO, smem, &mbar[kStO]);
         // GU
-        residual_add(hidden, o_rep, e_o, nrm + H, H, xs, red, p, &s_abort);
+        residual_add(hidden, o_rep, p.heads, e_o, nrm + H, H, xs, vin, red, p, &s_abort);
         norm_to(hidden, nrm + 2 * H, H, p.stage_nb[kStGu] * 32, p.eps, xs, red);
         mbar_wait(&mbar[kStGu], par, p);
         __syncthreads();
@@ -706,7 +702,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(c
         const float *last = reinterpret_cast<const float *>(smem + p.off_nrm[(p.layers - 1) & 1]);
         // h + rmsnorm_delta(down_out, ffn_post) of the last layer; waiting for
         // it also means every CTA has passed its last read of this launch.
-        residual_add(hidden, down_rep, e0 + 5u * p.layers, last + 3 * H, H, xs, red, p, &s_abort);
+        residual_add(hidden, down_rep, 1, e0 + 5u * p.layers, last + 3 * H, H, xs, vin, red, p, &s_abort);
         if (p.generate) {
             // logits input: rmsnorm_delta(h, final) (transformer.c:393-408)
             float ss = 0.0f;
@@ -731,16 +727,20 @@ __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(c
 
 size_t align128(size_t v) { return (v + 127) & ~(size_t)127; }
 
-// Dynamic shared-memory layout for grid G and `chunk` keys per split: fills
-// p's offsets and returns the total bytes.
+// Dynamic shared-memory layout for grid G and at least `chunk` keys per
+// split: fills p's offsets and attention geometry and returns the total bytes.
 size_t smem_layout(PersistParams &p, int G, int chunk) {
+    p.splits = G / p.heads;
+    p.chunk = chunk;
+    // Every window up to the context fits `splits` splits of chunk_max keys.
+    p.chunk_max = std::max(chunk, (p.context + p.splits - 1) / p.splits);
     size_t off = 0;
     for (int st = 0; st < kNumStages; ++st) {
         p.off_w[st] = (unsigned)off;
         const size_t rows_max = ((size_t)p.stage_rows[st] + G - 1) / G;
         off = align128(off + rows_max * p.stage_stride[st]);
     }
-    const size_t kv_bytes = (size_t)p.kv_heads * chunk * p.hd * 4;
+    const size_t kv_bytes = (size_t)p.chunk_max * p.hd * 4;
     p.off_k = (unsigned)off;
     off = align128(off + kv_bytes);
     p.off_v = (unsigned)off;
@@ -752,30 +752,30 @@ size_t smem_layout(PersistParams &p, int G, int chunk) {
     p.off_x = (unsigned)off;
     off = align128(off + xw * 4);
     p.off_q = (unsigned)off;
-    off = align128(off + (size_t)p.heads * p.hd * 4);
+    off = align128(off + (size_t)p.hd * 4);
     p.off_kcur = (unsigned)off;
-    off = align128(off + (size_t)p.kv_heads * p.hd * 4);
+    off = align128(off + (size_t)p.hd * 4);
     p.off_vcur = (unsigned)off;
-    off = align128(off + (size_t)p.kv_heads * p.hd * 4);
+    off = align128(off + (size_t)p.hd * 4);
     p.off_sc = (unsigned)off;
-    off = align128(off + (size_t)kMaxGroup * chunk * 4);
+    off = align128(off + (size_t)p.chunk_max * 4);
     for (int b = 0; b < 2; ++b) {
         p.off_nrm[b] = (unsigned)off;
         off = align128(off + (size_t)p.norm_stride * 4);
     }
     p.off_rope = (unsigned)off;
     off = align128(off + (size_t)4 * p.hd * 4);
-    // Scratch of the weighted key sums and of the split combine.
-    const size_t group = (size_t)p.heads / p.kv_heads;
+    // Scratch of the weighted key sums (parts x hd) and of the split combine
+    // (at most max(threads, heads * hd / 4) float4).
     p.off_acc = (unsigned)off;
-    off = align128(off + std::max((size_t)kPersistThreads * group, (size_t)4 * p.heads * p.hd) * 4);
-    // Staged input vectors (qkv, gate / up) and the combine's (m, l) pairs.
+    off = align128(off + std::max((size_t)4 * kPersistThreads, (size_t)p.heads * p.hd) * 4);
+    // Staged input vectors (qkv, gate / up, the heads' O rows) and the
+    // combine's (m, l) pairs.
     size_t vin = std::max((size_t)(p.heads + 2 * p.kv_heads) * p.hd, (size_t)2 * p.ffn);
-    vin = std::max(vin, std::max((size_t)p.hidden, (size_t)2 * G * p.heads));
+    vin = std::max(vin, std::max((size_t)p.heads * p.hidden, (size_t)2 * G));
     p.off_vin = (unsigned)off;
     off = align128(off + vin * 4);
     p.off_cw = p.off_ml = 0;
-    p.chunk = chunk;
     return off;
 }
 
@@ -799,6 +799,10 @@ PersistPlan persist_plan(int device, const PersistParams &s, const char **why) {
         *why = "hidden / ffn / head_dim alignment";
         return plan;
     }
+    if (s.layers > 64 || G < s.heads) {
+        *why = "more than 64 layers or fewer SMs than heads";
+        return plan;
+    }
     // Every CTA must have rows in every product (the buffers' reuse relies on it).
     for (int st = 0; st < kNumStages; ++st)
         if (s.stage_stride[st] % 16 || s.stage_rows[st] < G) {
@@ -810,8 +814,6 @@ PersistPlan persist_plan(int device, const PersistParams &s, const char **why) {
         const int v = atoi(e);
         if (v >= 1 && v <= 256) chunk = v;
     }
-    // Every split count of a window up to the context fits the grid.
-    chunk = std::max(chunk, (s.context + G - 1) / G);
     PersistParams lay = s;
     const size_t bytes = smem_layout(lay, G, chunk);
     int optin = 0;
