@@ -11,6 +11,15 @@
  * QK-norm, RoPE, attention over the KV cache, GeGLU and the greedy argmax are
  * kernels, and one token's whole step is a CUDA graph, so a token costs no
  * host round trip.
+ *
+ * When the model fits it (any Gemma-3 shape whose products have at least one
+ * row per SM and whose per-SM slices fit shared memory), all layers of a
+ * token run as ONE persistent kernel, one block per SM, whose stages wait for
+ * each other's outputs through epoch-tagged words in global memory; a
+ * generated token adds the LM-head GEMV and the argmax (3 kernels).
+ * Otherwise - or with the environment variable SAPPHIRE_DECODE_PERSISTENT=0
+ * at creation - each stage is its own kernel (5 per layer).  Both give the
+ * reference's greedy ids.
  */
 #ifndef SAPPHIRE_DECODE_H
 #define SAPPHIRE_DECODE_H
@@ -79,6 +88,14 @@ SAPPHIRE_API int sapphire_decoder_last_times(sapphire_decoder_t *d, float *promp
 /** Kernel launches of one generated token (graph nodes). */
 SAPPHIRE_API int sapphire_decoder_launches_per_token(sapphire_decoder_t *d);
 SAPPHIRE_API void sapphire_decoder_destroy(sapphire_decoder_t *d);
+
+/** Test hook (no reference counterpart): on != 0 makes decoders created
+ *  afterwards run a persistent step in which one block withholds its layer-0
+ *  q / k / v rows and every wait is limited to 1 ms, so the step's bounded
+ *  waits run out without any GPU fault; creation then fails with the expiry
+ *  in kernel_ctx_last_error and the context stays usable.  Returns the
+ *  previous setting.  Process-wide. */
+SAPPHIRE_API int sapphire_test_decode_stall(int on);
 
 #ifdef __cplusplus
 }

@@ -110,6 +110,7 @@ _SIGNATURES = {
     "sapphire_safetensors_tensor": (vp, [vp, C.c_char_p]),
     "sapphire_safetensors_close": (None, [vp]),
     "sapphire_decoder_create_from_safetensors": (vp, [vp, vp, vp]),
+    "sapphire_test_decode_stall": (i32, [i32]),
     # include/sapphire_decode.h
     "sapphire_decoder_create": (vp, [vp, vp, vp]),
     "sapphire_decoder_generate": (i32, [vp, vp, i32, i32, vp, vp]),

@@ -586,6 +586,10 @@ struct sapphire_decoder {
 
 namespace {
 
+// Test hook (sapphire_test_decode_stall): decoders created while it is set
+// run a persistent step in which one block withholds its output.
+std::atomic<int> g_test_decode_stall{0};
+
 int dev_alloc(sapphire_decoder_t *d, void **p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
     if (e != cudaSuccess) {
@@ -1072,7 +1076,8 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             pp.norm_out = d->norm;
             pp.ctl = d->ctl;
             pp.err = ctx->d_err;
-            pp.wait_ns = 2000000000ull;
+            pp.test_stall = g_test_decode_stall.load();
+            pp.wait_ns = pp.test_stall ? 1000000ull : 2000000000ull;
             persist_layout(d->plan, pp);
         }
         // Scratch of the GEMVs sized for the largest weight, before capture.
@@ -1093,10 +1098,13 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
         cudaStream_t st = ctx->stream;
         if (set_state(d, 0, 1, st) || enqueue_step(d, false, st) < 0 || enqueue_step(d, true, st) < 0) break;
         d->epochs += 1;
-        if (cudaStreamSynchronize(st) != cudaSuccess || check_kernel_error(ctx, "sapphire_decoder_create")) {
-            ctx_fail(ctx, "sapphire_decoder_create", "warm-up step failed");
+        const cudaError_t se = cudaStreamSynchronize(st);
+        if (se != cudaSuccess) {
+            ctx_fail(ctx, "sapphire_decoder_create", "warm-up step failed: %s", cudaGetErrorString(se));
             break;
         }
+        // A kernel error of the warm-up (its message names the cause).
+        if (check_kernel_error(ctx, "sapphire_decoder_create warm-up step")) break;
         if (capture(d, false, &d->g_prompt, &d->launches_prompt) ||
             capture(d, true, &d->g_gen, &d->launches_gen)) {
             if (!d->persist || !d->coop) break;
@@ -1225,6 +1233,8 @@ extern "C" SAPPHIRE_API int sapphire_decoder_last_times(sapphire_decoder_t *d, f
     if (generate_ms) *generate_ms = d->last_gen_ms;
     return 0;
 }
+
+extern "C" SAPPHIRE_API int sapphire_test_decode_stall(int on) { return g_test_decode_stall.exchange(on ? 1 : 0); }
 
 extern "C" SAPPHIRE_API int sapphire_decoder_launches_per_token(sapphire_decoder_t *d) {
     return d ? d->launches_gen : -1;

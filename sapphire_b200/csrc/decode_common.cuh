@@ -132,6 +132,7 @@ struct PersistParams {
     unsigned *ctl;                // [0] abort flag, [1] launches so far (never cleared: the epoch base)
     int *err;
     unsigned long long wait_ns;   // bound of every wait
+    int test_stall;               // test hook: the last CTA withholds its layer-0 qkv rows
     // Dynamic shared-memory offsets (bytes).
     unsigned off_w[kNumStages], off_k, off_v, off_hidden, off_x, off_q, off_kcur, off_vcur, off_cw, off_sc, off_ml;
     unsigned off_nrm[2], off_rope, off_acc, off_vin;

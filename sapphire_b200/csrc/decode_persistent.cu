@@ -660,7 +660,8 @@ __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(c
         norm_to(hidden, nrm, H, p.stage_nb[kStQkv] * 32, p.eps, xs, red);
         mbar_wait(&mbar[kStQkv], par, p);
         __syncthreads();
-        gemv_stage(p, kStQkv, smem + p.off_w[kStQkv], xs, p.qkv, e_qkv, 1);
+        if (!(p.test_stall && l == 0 && blockIdx.x == gridDim.x - 1))
+            gemv_stage(p, kStQkv, smem + p.off_w[kStQkv], xs, p.qkv, e_qkv, 1);
         __syncthreads();
         if (threadIdx.x == 0) {
             if (more) issue_stage(p, l + 1, kStQkv, smem, &mbar[kStQkv]);

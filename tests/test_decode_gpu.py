@@ -119,3 +119,41 @@ def test_from_safetensors_rejects_wrong_dtype(sp, ctx, decoder, tmp_path):
     with safetensors.SafeTensors(path) as st:
         with pytest.raises(sp.SapphireError, match="lm_head.weight"):
             Decoder.from_safetensors(ctx, small, st)
+
+
+def test_stage_per_kernel_path_matches_reference(sp, ctx, decoder, golden, monkeypatch):
+    """The one-kernel-per-stage step (SAPPHIRE_DECODE_PERSISTENT=0 at
+    creation) gives the reference's ids as well."""
+    from sapphire_b200.decode import Decoder
+    cfg, model, _ = decoder
+    monkeypatch.setenv("SAPPHIRE_DECODE_PERSISTENT", "0")
+    dec = Decoder(ctx, cfg, model)
+    try:
+        assert dec.launches_per_token > 10      # one kernel per stage
+        ids, _ = dec.generate(model["prompt"], cfg.generate)
+        assert np.array_equal(ids, golden["tokens"])
+    finally:
+        dec.close()
+
+
+def test_persistent_step_reports_an_expired_wait(sp, ctx, decoder, golden):
+    """A persistent step in which one block never writes its output (a test
+    hook: nothing sets the words the others wait for) gives up after its
+    bounded wait: creation fails with the expiry reported, no GPU fault, and a
+    decoder created afterwards still decodes the reference's ids."""
+    from sapphire_b200.decode import Decoder
+    cfg, model, dec = decoder
+    assert dec.launches_per_token == 3          # persistent step + LM head + argmax
+    prev = sp.lib.sapphire_test_decode_stall(1)
+    try:
+        with pytest.raises(sp.SapphireError, match="gave up waiting"):
+            Decoder(ctx, cfg, model)
+    finally:
+        sp.lib.sapphire_test_decode_stall(prev)
+    ok = Decoder(ctx, cfg, model)
+    try:
+        ids, _ = ok.generate(model["prompt"][:64], 8)
+        ref, _ = dec.generate(model["prompt"][:64], 8)
+        assert np.array_equal(ids, ref)
+    finally:
+        ok.close()
