@@ -364,9 +364,52 @@ __device__ void prepare_x(const StreamParams &p, const XImage &xi) {
     // odd-block row is staged as zeros, so its digits and correction are 0),
     // the Q4_0 corrections and the ternary x sum.
     long long sx = 0;
+    if (DT != DTYPE_Q4_0) {
+        // Q8_0 / TQ2_0: elements 4k .. 4k+3 of a block land in four
+        // consecutive bytes, (k & 3) * 8 + (k >> 2) * 4, of each digit row
+        // (digit_byte), so lane 8q + k converts them from one 16-byte load
+        // and stores one word per row: a warp converts blocks 4w + 4NC i + q.
+        const int q = lane >> 3, k = lane & 7;
+        const int wb = (k & 3) * 8 + (k >> 2) * 4;
+        long long sxl = 0;
+        for (int b0 = 4 * warp; b0 < nbp; b0 += 4 * NC) {
+            const int b = b0 + q;
+            const float4 t = b < nbp ? *reinterpret_cast<const float4 *>(stage + (size_t)b * 32 + 4 * k)
+                                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            __syncwarp();
+            if (b < nbp) {
+                const float tv[4] = {t.x, t.y, t.z, t.w};
+                uint32_t w0 = 0, w1 = 0, w2 = 0;
+                int sb = 0;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int X = isfinite(tv[e]) ? __float2int_rn(tv[e] * f1 * f2) : 0;
+                    const int d0 = ((X & 0xFF) ^ 0x80) - 0x80;
+                    const int X1 = (X - d0) >> 8;
+                    const int d1 = ((X1 & 0xFF) ^ 0x80) - 0x80;
+                    const int d2 = (X1 - d1) >> 8;
+                    w0 |= (uint32_t)(d0 & 0xFF) << (8 * e);
+                    w1 |= (uint32_t)(d1 & 0xFF) << (8 * e);
+                    w2 |= (uint32_t)(d2 & 0xFF) << (8 * e);
+                    sb += X;       // |X| < 2^22: four fit int32
+                }
+                uint8_t *blk = xi.img + (size_t)b * kImgBlock;
+                *reinterpret_cast<uint32_t *>(blk + wb) = w0;
+                *reinterpret_cast<uint32_t *>(blk + 32 + wb) = w1;
+                *reinterpret_cast<uint32_t *>(blk + 64 + wb) = w2;
+                *reinterpret_cast<uint32_t *>(blk + 96 + wb) = 0u;
+                sxl += sb;
+            }
+        }
+        if (DT == DTYPE_TQ2_0) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sxl += __shfl_xor_sync(0xffffffffu, sxl, o);
+            sx = sxl;
+        }
+    }
     const int off = digit_byte<DT>(lane);
 #pragma unroll 2
-    for (int b = warp; b < nbp; b += NC) {
+    for (int b = warp; DT == DTYPE_Q4_0 && b < nbp; b += NC) {
         uint8_t *blk = xi.img + (size_t)b * kImgBlock;
         const float t = stage[b * 32 + lane];
         __syncwarp();
