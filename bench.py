@@ -563,7 +563,8 @@ def measure_gemv(args, env, cfg, with_cpu: bool) -> dict:
                      "frac_sustained_covers": "the same bytes over ms_per_step (steps back to back)"},
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": 4 * cfg.cols,
                 "d2h_bytes_per_step": 4 * cfg.rows, "ms_per_step": round(e2e_ms, 5),
-                "path": "kernel_gemv with pinned host x/y (weights resident after upload)"},
+                "path": "kernel_gemv with pinned host x/y (weights resident after upload): x copied in, "
+                        "y written by the GEMV through the host mapping, then the stream synchronised"},
         "gpu_launches": args.steps,
         "parity": parity,
     }

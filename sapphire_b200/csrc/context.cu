@@ -93,6 +93,15 @@ bool ptr_is_device(const void *p, int *dev) {
     return false;
 }
 
+float *host_mapped(float *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? static_cast<float *>(a.devicePointer) : nullptr;
+}
+
 bool weight_shape(const tensor_t *A, int *rows, int *cols) {
     if (!A || tensor_ndim(A) != 2) return false;
     const int *s = tensor_shape(A);

@@ -69,12 +69,23 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
 
     if (ctx->world <= 1) {
         float *yd = Y;
+        bool copy_out = false;
         if (!y_on_dev) {
-            if (ensure_scratch(ctx, &ctx->d_y, &ctx->d_y_cap, (size_t)batch * rows * sizeof(float))) return -1;
-            yd = ctx->d_y;
+            // A batch-1 result for page-locked host memory is written by the
+            // kernel itself through the memory's device mapping: its rows
+            // cross PCIe while the product runs instead of in a copy after it
+            // (y is valid once the stream has synchronised, as before).
+            float *mapped = batch == 1 ? host_mapped(Y) : nullptr;
+            if (mapped) {
+                yd = mapped;
+            } else {
+                if (ensure_scratch(ctx, &ctx->d_y, &ctx->d_y_cap, (size_t)batch * rows * sizeof(float))) return -1;
+                yd = ctx->d_y;
+                copy_out = true;
+            }
         }
         if (launch_product(ctx, *w, xd, cols, yd, rows, batch, st)) return -1;
-        if (!y_on_dev)
+        if (copy_out)
             CUDA_TRY(ctx, cudaMemcpyAsync(Y, yd, (size_t)batch * rows * sizeof(float), cudaMemcpyDeviceToHost, st));
     } else {
         // Row-sharded: each rank computes Y_local[b][per] for its rows, then an

@@ -200,6 +200,30 @@ def test_unaligned_x_pointer(sp, ctx, oracle):
     assert normwise_rel(y, oracle_y(oracle, Q4_0, packed, rows, cols, buf[1:])[0]) < GEMV_RTOL
 
 
+@pytest.mark.parametrize("dtype,rows,cols", [(Q8_0, 262144, 640), (Q4_0, 4096, 640), (TQ2_0, 1000, 16384),
+                                            (Q4_0, 2048, 640), (F32, 300, 96)])
+def test_page_locked_host_y(sp, ctx, oracle, dtype, rows, cols):
+    """kernel_gemv into page-locked host y: the kernel writes the rows through
+    the host mapping (no copy after the product); the result is bit for bit
+    the one of the copy path (pageable y) and within the bar of the oracle."""
+    packed = rand_packed(oracle, dtype, rows, cols, seed=21)
+    A = sp.Tensor(dtype, (rows, cols), packed)
+    x = np.random.default_rng(21).standard_normal(cols, dtype=np.float32)
+    y_copy = np.zeros(rows, dtype=np.float32)
+    assert sp.lib.kernel_gemv(ctx.handle, y_copy.ctypes.data, A.handle, x.ctypes.data) == 0
+    hp = sp.lib.kernel_host_alloc(rows * 4)
+    assert hp
+    try:
+        y_pin = np.ctypeslib.as_array(C.cast(hp, C.POINTER(C.c_float)), shape=(rows,))
+        for _ in range(2):
+            y_pin[:] = np.nan
+            assert sp.lib.kernel_gemv(ctx.handle, hp, A.handle, x.ctypes.data) == 0
+            assert np.array_equal(y_pin, y_copy)
+        assert normwise_rel(y_pin, oracle_y(oracle, dtype, packed, rows, cols, x)[0]) < GEMV_RTOL
+    finally:
+        sp.lib.kernel_host_free(hp)
+
+
 def test_device_pointer_path(sp, ctx, oracle):
     import torch
     rows, cols = 4096, 640
