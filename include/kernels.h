@@ -127,6 +127,9 @@ SAPPHIRE_API void kernel_gemm_bf16_avx2(const gemm_args_t* args);
  *  Quantized A needs a context (NULL gives -1, as in the reference); F32/BF16
  *  with a NULL context run on a process-wide default context.  x and y may be
  *  host or device pointers; the call is synchronous (y is valid on return).
+ *  A page-locked host y (cudaHostAlloc / kernel_host_alloc / registered) is
+ *  written by the kernel through its device mapping while the product runs;
+ *  other host y receive a copy after it.
  *  The first call with a given weight tensor uploads it (see
  *  kernel_tensor_upload in sapphire_cuda.h).  0 on success, -1 on error. */
 SAPPHIRE_API int kernel_gemv(kernel_context_t *ctx, float *y, const tensor_t *A, const float *x);
