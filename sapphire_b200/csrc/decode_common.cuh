@@ -134,7 +134,7 @@ struct PersistParams {
     unsigned long long wait_ns;   // bound of every wait
     int test_stall;               // test hook: the last CTA withholds its layer-0 qkv rows
     // Dynamic shared-memory offsets (bytes).
-    unsigned off_w[kNumStages], off_k, off_v, off_hidden, off_x, off_q, off_kcur, off_vcur, off_cw, off_sc, off_ml;
+    unsigned off_w[kNumStages], off_k, off_v, off_hidden, off_x, off_q, off_kcur, off_vcur, off_sc;
     unsigned off_nrm[2], off_rope, off_acc, off_vin;
 };
 

@@ -776,7 +776,6 @@ size_t smem_layout(PersistParams &p, int G, int chunk) {
     vin = std::max(vin, std::max((size_t)p.heads * p.hidden, (size_t)2 * G));
     p.off_vin = (unsigned)off;
     off = align128(off + vin * 4);
-    p.off_cw = p.off_ml = 0;
     return off;
 }
 
@@ -842,7 +841,8 @@ PersistPlan persist_plan(int device, const PersistParams &s, const char **why) {
     plan.grid = G;
     plan.chunk = chunk;
     plan.smem = bytes;
-    plan.part_floats = (size_t)G * s.heads * (s.hd + 4);
+    // One partial row per (split, head): splits * heads <= G rows.
+    plan.part_floats = (size_t)G * (s.hd + 4);
     return plan;
 }
 
