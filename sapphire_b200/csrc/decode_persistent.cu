@@ -197,8 +197,9 @@ __device__ void fetch_vec(const unsigned long long *src, int n, unsigned epoch, 
 }
 
 // Rows [r0, r1) of stage s that CTA c computes (balanced split of the rows).
+// (32-bit arithmetic: persist_plan admits rows * grid < 2^32.)
 __device__ __forceinline__ void stage_rows(const PersistParams &p, int s, int &r0, int &r1) {
-    const long long R = p.stage_rows[s], G = gridDim.x, c = blockIdx.x;
+    const unsigned R = (unsigned)p.stage_rows[s], G = gridDim.x, c = blockIdx.x;
     r0 = (int)(c * R / G);
     r1 = (int)((c + 1) * R / G);
 }
@@ -346,8 +347,9 @@ __device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, cons
             const uint32_t c2 = *reinterpret_cast<const uint32_t *>(row2 + 4 * k);
             const float4 a0 = *reinterpret_cast<const float4 *>(x1p + 8 * k);
             const float4 a1 = *reinterpret_cast<const float4 *>(x1p + 8 * k + 4);
-            const float4 b0 = *reinterpret_cast<const float4 *>(x2p + 8 * k);
-            const float4 b1 = *reinterpret_cast<const float4 *>(x2p + 8 * k + 4);
+            // Rows of one x (every stage but the head-split O) share the loads.
+            const float4 b0 = seg ? *reinterpret_cast<const float4 *>(x2p + 8 * k) : a0;
+            const float4 b1 = seg ? *reinterpret_cast<const float4 *>(x2p + 8 * k + 4) : a1;
             acc = fmaf(sc[k >> 2], q4_word_dot(c1, a0, a1), acc);
             acc2 = fmaf(sc2[k >> 2], q4_word_dot(c2, b0, b1), acc2);
         }
@@ -805,7 +807,7 @@ PersistPlan persist_plan(int device, const PersistParams &s, const char **why) {
     }
     // Every CTA must have rows in every product (the buffers' reuse relies on it).
     for (int st = 0; st < kNumStages; ++st)
-        if (s.stage_stride[st] % 16 || s.stage_rows[st] < G) {
+        if (s.stage_stride[st] % 16 || s.stage_rows[st] < G || (unsigned long long)s.stage_rows[st] * G >= (1ull << 32)) {
             *why = "row layout";
             return plan;
         }
