@@ -930,6 +930,16 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
                 for (int s = 0; s < kNumStages; ++s) {
                     const int nb = pp.stage_nb[s], stride = pp.stage_stride[s];
                     uint8_t *dst = rows.data() + (size_t)l * lb + pp.stage_off[s];
+                    if (s == kStGu) {
+                        // Gate row i and up row i as rows 2i and 2i + 1.
+                        const size_t src_rb = sapphire_row_bytes_internal(DTYPE_Q4_0, c.hidden);
+                        const uint8_t *gate = static_cast<const uint8_t *>(p[4]), *up = static_cast<const uint8_t *>(p[5]);
+                        for (int i = 0; i < c.ffn; ++i, dst += 2 * stride) {
+                            put_row(dst, gate + (size_t)i * src_rb, nb, 0);
+                            put_row(dst + stride, up + (size_t)i * src_rb, nb, 0);
+                        }
+                        continue;
+                    }
                     const int pieces = s == kStO ? c.heads : 1;
                     for (int h = 0; h < pieces; ++h)
                         for (const auto &part : parts[s]) {
@@ -1043,7 +1053,7 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             if (!copied ||
                 dev_alloc(d, (void **)&pp.qkv, (size_t)(d->q_dim + 2 * d->kv_dim) * 8) ||
                 dev_alloc(d, (void **)&pp.o_out, (size_t)c.heads * c.hidden * 8 * kPersistReplicas) ||
-                dev_alloc(d, (void **)&pp.gu, (size_t)2 * c.ffn * 8 * kPersistReplicas) ||
+                dev_alloc(d, (void **)&pp.gu, (size_t)c.ffn * 8 * kPersistReplicas) ||
                 dev_alloc(d, (void **)&pp.down_out, (size_t)c.hidden * 8 * kPersistReplicas) ||
                 dev_alloc(d, (void **)&pp.part, d->plan.part_floats * 4) ||
                 dev_alloc(d, (void **)&d->ctl, 4 * sizeof(unsigned)))
@@ -1051,7 +1061,7 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             // Tagged words start with epoch 0, which no launch uses.
             if (cudaMemset(pp.qkv, 0, (size_t)(d->q_dim + 2 * d->kv_dim) * 8) != cudaSuccess ||
                 cudaMemset(pp.o_out, 0, (size_t)c.heads * c.hidden * 8 * kPersistReplicas) != cudaSuccess ||
-                cudaMemset(pp.gu, 0, (size_t)2 * c.ffn * 8 * kPersistReplicas) != cudaSuccess ||
+                cudaMemset(pp.gu, 0, (size_t)c.ffn * 8 * kPersistReplicas) != cudaSuccess ||
                 cudaMemset(pp.down_out, 0, (size_t)c.hidden * 8 * kPersistReplicas) != cudaSuccess ||
                 cudaMemset(pp.part, 0, d->plan.part_floats * 4) != cudaSuccess ||
                 cudaMemset(d->ctl, 0, 4 * sizeof(unsigned)) != cudaSuccess) {

@@ -118,6 +118,8 @@ struct PersistParams {
     // o_out, gu and down_out, which every CTA reads, are written in
     // kPersistReplicas copies ([replica][row]); CTA c polls copy c % kPersistReplicas.
     unsigned long long *qkv, *o_out, *gu, *down_out;
+    // gu holds gelu_tanh(gate) * up (ffn words per copy): the GU stage's rows
+    // are gate / up pairs (row 2i = gate row i, 2i + 1 = up row i).
     // Attention partials per split and head, part[(b * heads + h)]: [m word,
     // l word, acc (hd floats)] (the m / l words are tagged and stored with
     // release after acc).  The O product is split by head: stage O's row

@@ -21,8 +21,9 @@
 //           range holds pos writes the token's K / V rows
 //     O     every CTA: attn = combine of the nsplit partials, its rows of Wo . attn
 //     GU    every CTA: h += rmsnorm_delta(o_out, attn_post[l]),
-//           x = rmsnorm_delta(h, ffn[l]); its rows of [Wgate; Wup] . x
-//     DOWN  every CTA: x = gelu_tanh(gate) * up; its rows of Wdown . x
+//           x = rmsnorm_delta(h, ffn[l]); its (gate, up) row pairs . x, and
+//           gelu_tanh(gate) * up of each pair
+//     DOWN  every CTA: its rows of Wdown . (the GU stage's outputs)
 //   then CTA 0: h += rmsnorm_delta(down_out, ffn_post[L-1]) and either the
 //   final norm (the LM head's input) or the prompt-state advance.
 //
@@ -197,11 +198,20 @@ __device__ void fetch_vec(const unsigned long long *src, int n, unsigned epoch, 
 }
 
 // Rows [r0, r1) of stage s that CTA c computes (balanced split of the rows).
-// (32-bit arithmetic: persist_plan admits rows * grid < 2^32.)
+// Stage GU holds gate row i and up row i as rows 2i and 2i + 1, split by
+// pairs, so a block holds both rows of each of its pairs.  (32-bit
+// arithmetic: persist_plan admits rows * grid < 2^32.)
 __device__ __forceinline__ void stage_rows(const PersistParams &p, int s, int &r0, int &r1) {
-    const unsigned R = (unsigned)p.stage_rows[s], G = gridDim.x, c = blockIdx.x;
-    r0 = (int)(c * R / G);
-    r1 = (int)((c + 1) * R / G);
+    const unsigned G = gridDim.x, c = blockIdx.x;
+    if (s == kStGu) {
+        const unsigned P = (unsigned)p.stage_rows[s] / 2;
+        r0 = (int)(2 * (c * P / G));
+        r1 = (int)(2 * ((c + 1) * P / G));
+    } else {
+        const unsigned R = (unsigned)p.stage_rows[s];
+        r0 = (int)(c * R / G);
+        r1 = (int)((c + 1) * R / G);
+    }
 }
 
 // Attention work of CTA c at layer l: query head h = c / splits and keys
@@ -325,14 +335,20 @@ __device__ __forceinline__ float q4_word_dot(uint32_t code, float4 x0, float4 x1
 // this CTA's rows of stage s (weights in shared memory), one warp per row, two rows at a time; lane k
 // of a row takes 4-byte code word k (8 weights of block k / 4) and its x
 // values xs[8k .. 8k + 8).
+//
+// Stage GU (pairs): a warp takes rows 2j and 2j + 1 (gate and up of output j)
+// and writes one word, gelu_tanh(gate) * up, to y[j] (the DOWN stage's input).
 __device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, const float *xs, unsigned long long *y,
                            unsigned epoch, int replicas, int seg = 0, int seg0 = 0) {
     int r0, r1;
     stage_rows(p, s, r0, r1);
     const int nb = p.stage_nb[s], stride = p.stage_stride[s], nwords = nb * 4, nr = r1 - r0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int r = warp; r < nr; r += 2 * kPWarps) {
-        const int r2 = r + kPWarps;
+    const bool pairs = s == kStGu;
+    const int ny = pairs ? p.stage_rows[s] / 2 : p.stage_rows[s];   // outputs per copy
+    for (int i = warp; pairs ? 2 * i < nr : i < nr; i += pairs ? kPWarps : 2 * kPWarps) {
+        const int r = pairs ? 2 * i : i;
+        const int r2 = pairs ? r + 1 : r + kPWarps;
         const bool two = r2 < nr;
         const uint8_t *row = w + (size_t)r * stride, *row2 = w + (size_t)(two ? r2 : r) * stride;
         const float *sc = reinterpret_cast<const float *>(row + (size_t)nb * 16);
@@ -356,8 +372,12 @@ __device__ void gemv_stage(const PersistParams &p, int s, const uint8_t *w, cons
         acc = warp_sum(acc);
         acc2 = warp_sum(acc2);
         // Every lane holds the sums (xor reduction): lane k writes copy k.
-        if (lane < replicas) {
-            unsigned long long *yk = y + (size_t)lane * p.stage_rows[s];
+        if (pairs) {
+            // GeGLU of the reference (src/transformer/activations.c:64-82).
+            const float g = geglu_tanh(acc, acc2);
+            if (lane < replicas) st_word(y + (size_t)lane * ny + (r0 + r) / 2, tagged(epoch, g));
+        } else if (lane < replicas) {
+            unsigned long long *yk = y + (size_t)lane * ny;
             st_word(yk + r0 + r, tagged(epoch, acc));
             if (two) st_word(yk + r0 + r2, tagged(epoch, acc2));
         }
@@ -616,7 +636,7 @@ __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(c
     const int rep = blockIdx.x % kPersistReplicas;
     const unsigned long long *o_rep = p.o_out + (size_t)rep * p.stage_rows[kStO],
                              *down_rep = p.down_out + (size_t)rep * H,
-                             *gu_rep = p.gu + (size_t)rep * 2 * p.ffn;
+                             *gu_rep = p.gu + (size_t)rep * p.ffn;
     // The state and the launch count are read once, at the start: CTA 0
     // changes them only after it has consumed the last stage, which every
     // CTA contributed to.
@@ -688,11 +708,11 @@ __global__ void __launch_bounds__(kPersistThreads, 1) decode_persistent_kernel(c
         gemv_stage(p, kStGu, smem + p.off_w[kStGu], xs, p.gu, e_gu, kPersistReplicas);
         __syncthreads();
         if (threadIdx.x == 0 && more) issue_stage(p, l + 1, kStGu, smem, &mbar[kStGu]);
-        // DOWN: x = gelu_tanh(gate) * up.
+        // DOWN: x = gelu_tanh(gate) * up, formed by the GU stage's blocks.
         {
             const int F = p.ffn, width = p.stage_nb[kStDown] * 32;
-            fetch_vec(gu_rep, 2 * F, e_gu, vin, p, &s_abort);
-            for (int i = threadIdx.x; i < width; i += kPersistThreads) xs[i] = i < F ? geglu_tanh(vin[i], vin[F + i]) : 0.0f;
+            for (int i = F + threadIdx.x; i < width; i += kPersistThreads) xs[i] = 0.0f;
+            fetch_vec(gu_rep, F, e_gu, xs, p, &s_abort);
         }
         mbar_wait(&mbar[kStDown], par, p);
         __syncthreads();
@@ -740,7 +760,8 @@ size_t smem_layout(PersistParams &p, int G, int chunk) {
     size_t off = 0;
     for (int st = 0; st < kNumStages; ++st) {
         p.off_w[st] = (unsigned)off;
-        const size_t rows_max = ((size_t)p.stage_rows[st] + G - 1) / G;
+        const size_t rows_max = st == kStGu ? 2 * (((size_t)p.stage_rows[st] / 2 + G - 1) / G)
+                                            : ((size_t)p.stage_rows[st] + G - 1) / G;
         off = align128(off + rows_max * p.stage_stride[st]);
     }
     const size_t kv_bytes = (size_t)p.chunk_max * p.hd * 4;
@@ -805,9 +826,10 @@ PersistPlan persist_plan(int device, const PersistParams &s, const char **why) {
         *why = "more than 64 layers or fewer SMs than heads";
         return plan;
     }
-    // Every CTA must have rows in every product (the buffers' reuse relies on it).
+    // Every CTA must have rows in every product (the buffers' reuse relies on
+    // it; stage GU counts pairs).
     for (int st = 0; st < kNumStages; ++st)
-        if (s.stage_stride[st] % 16 || s.stage_rows[st] < G || (unsigned long long)s.stage_rows[st] * G >= (1ull << 32)) {
+        if (s.stage_stride[st] % 16 || s.stage_rows[st] < (st == kStGu ? 2 * G : G) || (unsigned long long)s.stage_rows[st] * G >= (1ull << 32)) {
             *why = "row layout";
             return plan;
         }
