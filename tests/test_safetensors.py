@@ -183,3 +183,32 @@ def test_decoder_loader_checks_names_and_shapes(st_mod, tmp_path):
             assert b"model.norm.weight" in lib.kernel_ctx_last_error(ctx)
     finally:
         lib.kernel_ctx_destroy(ctx)
+
+
+@pytest.mark.gpu
+def test_gemv_on_file_tensors(st_mod, sp, ctx, oracle, tmp_path):
+    """Q4_0 / Q8_0 / TQ2_0 tensors read from a file are views the GEMV takes
+    as they are: kernel_gemv on each view matches the oracle on the same bytes."""
+    from conftest import GEMV_RTOL, normwise_rel
+    from sapphire_b200 import workloads
+    rng = np.random.default_rng(11)
+    rows, cols = 3000, 704
+    w = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)
+    trits = rng.integers(-1, 2, size=(rows, cols), dtype=np.int8)
+    tscale = rng.uniform(0.01, 0.1, size=rows).astype(np.float32)
+    packed = {"q4": (sp.DTYPE_Q4_0, oracle.quantize(sp.DTYPE_Q4_0, w)),
+              "q8": (sp.DTYPE_Q8_0, oracle.quantize(sp.DTYPE_Q8_0, w)),
+              "tq2": (sp.DTYPE_TQ2_0, oracle.pack_tq2(trits, tscale))}
+    path = str(tmp_path / "w.safetensors")
+    st_mod.save(path, {k: (sp.DTYPE_NAMES[dt], (rows, cols), b) for k, (dt, b) in packed.items()})
+    x = rng.standard_normal(cols, dtype=np.float32)
+    with st_mod.SafeTensors(path) as st:
+        for name, (dt, b) in packed.items():
+            y = np.zeros(rows, dtype=np.float32)
+            assert sp.lib.kernel_gemv(ctx.handle, y.ctypes.data, st.tensor(name), x.ctypes.data) == 0
+            ref = oracle.gemv(dt, b, rows, cols, workloads.pad_cols(x[None, :], cols), f64=True)[0]
+            assert normwise_rel(y, ref) < GEMV_RTOL, name
+        # The weights were uploaded from the mapping: release them before the
+        # file closes (the context keys device copies by tensor).
+        for name in packed:
+            sp.lib.kernel_tensor_evict(ctx.handle, st.tensor(name))
