@@ -136,6 +136,14 @@ class DecodeConfig:
 
 C3 = DecodeConfig()
 
+# A small grouped-query model for the decode tests: two KV heads shared by
+# four query heads, head_dim 64, six layers (layer 5 global), a 32-position
+# window - shapes C3 does not exercise.  query_pre_attn_scalar = head_dim, as
+# the reference's decode harness sets it.
+GQA_TINY = DecodeConfig(name="gqa_tiny", layers=6, hidden=256, ffn=512, heads=4, kv_heads=2, head_dim=64,
+                        vocab=4096, prompt=48, generate=24, context=128, sliding_window=32,
+                        query_pre_attn_scalar=64.0)
+
 
 def bf16_bits(x: np.ndarray) -> np.ndarray:
     """fp32 -> bf16 bit patterns (uint16), round to nearest even (finite values)."""

@@ -157,3 +157,27 @@ def test_persistent_step_reports_an_expired_wait(sp, ctx, decoder, golden):
         assert np.array_equal(ids, ref)
     finally:
         ok.close()
+
+
+@pytest.mark.parametrize("persistent", ["1", "0"])
+def test_grouped_query_model_matches_reference(sp, ctx, monkeypatch, persistent):
+    """A small grouped-query model (two KV heads for four query heads,
+    head_dim 64, a global and five local layers, window 32) decodes the
+    reference decode's ids through both step implementations
+    (tests/golden/decode_gqa_tiny_seed3.npz, tests/golden/make_decode_golden.py)."""
+    from sapphire_b200 import workloads
+    from sapphire_b200.decode import Decoder
+    golden = np.load(os.path.join(GOLDEN, "decode_gqa_tiny_seed3.npz"))
+    cfg = workloads.GQA_TINY
+    model = workloads.make_decode_model(cfg, lambda a: sp.quantize(ctx, Q4_0, a), seed=3)
+    assert workloads.model_digest(model) == str(golden["digest"])
+    monkeypatch.setenv("SAPPHIRE_DECODE_PERSISTENT", persistent)
+    dec = Decoder(ctx, cfg, model)
+    try:
+        # 3 launches per generated token for the persistent step, 5 per layer otherwise.
+        assert (dec.launches_per_token == 3) == (persistent == "1")
+        ids, margins = dec.generate(model["prompt"], cfg.generate)
+        assert np.array_equal(ids, golden["tokens"]), (ids, golden["tokens"])
+        assert np.max(np.abs(margins - golden["margins"])) < 1e-3
+    finally:
+        dec.close()
