@@ -138,7 +138,10 @@ SAPPHIRE_API int kernel_gemv(kernel_context_t *ctx, float *y, const tensor_t *A,
  *  b < batch_size (the reference passes out_stride as its "is GEMM" flag and
  *  always uses a row stride of `rows`, src/kernels/dispatch.c:98, pool.c:133).
  *  With out_stride == 0 only X[0..cols) is used, like kernel_gemv.
- *  Q4_0 / Q8_0 / TQ2_0 are supported here (the reference returns -1 for them). */
+ *  Q4_0 / Q8_0 / TQ2_0 are supported here (the reference returns -1 for them).
+ *  A Q4_0 product of 16 or more rows runs on the tensor cores with bf16
+ *  activations unless kernel_ctx_set_fp32_products (sapphire_cuda.h) keeps
+ *  fp32 (one row product per activation row). */
 SAPPHIRE_API int kernel_gemm(kernel_context_t *ctx, float *Y, const tensor_t *A, const float *X, int batch_size, int out_stride);
 
 /** y = A @ x for 1-D F32 tensors x, y (shape-checked). */

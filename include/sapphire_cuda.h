@@ -70,7 +70,8 @@ SAPPHIRE_API int kernel_gemv_device(kernel_context_t *ctx, float *y, const tenso
 /** Y[b*rows + r] = A[r,:] . X[b*cols ..] for b < batch_size (device pointers).
  *  A Q4_0 weight with batch_size >= 16 (here and in kernel_gemm) runs the
  *  tensor-core prefill product: activations rounded to bf16 (nearest even),
- *  weights dequantised exactly, fp32 accumulation. */
+ *  weights dequantised exactly, fp32 accumulation - unless the context keeps
+ *  fp32 products (kernel_ctx_set_fp32_products). */
 SAPPHIRE_API int kernel_gemm_device(kernel_context_t *ctx, float *Y, const tensor_t *A, const float *X, int batch_size);
 /** Tensor-core prefill product from bf16 activations already on the device
  *  (no counterpart in the reference, whose Q4_0 kernel_gemm returns -1):
@@ -113,6 +114,13 @@ SAPPHIRE_API int kernel_ctx_get_device(kernel_context_t *ctx);
  *  thread's current device at kernel_ctx_create).  -1 after init or when the
  *  device does not exist. */
 SAPPHIRE_API int kernel_ctx_set_device(kernel_context_t *ctx, int device);
+/** on != 0: batched Q4_0 products of this context (kernel_gemm,
+ *  kernel_gemm_device) keep fp32 activations - one fp32 row product per
+ *  activation row, the reference's arithmetic - instead of the bf16
+ *  tensor-core product from batch 16 on.  Off by default.  No reference
+ *  counterpart (the reference's Q4_0 kernel_gemm returns -1).  0, or -1 for
+ *  a NULL context. */
+SAPPHIRE_API int kernel_ctx_set_fp32_products(kernel_context_t *ctx, int on);
 /** Message of the last error recorded on the context ("" if none). */
 SAPPHIRE_API const char* kernel_ctx_last_error(kernel_context_t *ctx);
 

@@ -88,6 +88,7 @@ _SIGNATURES = {
     "sapphire_shard_rows": (i32, [i32, i32, i32, vp, vp]),
     "kernel_ctx_synchronize": (i32, [vp]),
     "kernel_ctx_set_device": (i32, [vp, i32]),
+    "kernel_ctx_set_fp32_products": (i32, [vp, i32]),
     "kernel_ctx_get_stream": (vp, [vp]),
     "kernel_ctx_set_stream": (i32, [vp, vp]),
     "kernel_ctx_get_device": (i32, [vp]),

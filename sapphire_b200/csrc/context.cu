@@ -371,7 +371,7 @@ int launch_product(kernel_context_t *ctx, const DevWeight &w, const float *x, in
                    int batch, cudaStream_t st) {
     if (batch == 1) return launch_gemv_best(ctx, w, x, y, st);
     if (w.dtype == DTYPE_F32 || w.dtype == DTYPE_BF16) return launch_gemv(ctx, w, x, x_stride, y, y_stride, batch, st);
-    if (gemm_tc_supported(w, batch)) {
+    if (!ctx->fp32_products && gemm_tc_supported(w, batch)) {
         if (ensure_pipe_scratch(ctx, 0, 0)) return -1;
         return launch_gemm_tc(ctx, w, x, x_stride, y, y_stride, batch, ctx->d_err, st);
     }
@@ -596,6 +596,13 @@ extern "C" SAPPHIRE_API int kernel_ctx_set_stream(kernel_context_t *ctx, void *s
 }
 
 extern "C" SAPPHIRE_API int kernel_ctx_get_device(kernel_context_t *ctx) { return ctx ? ctx->device : -1; }
+
+extern "C" SAPPHIRE_API int kernel_ctx_set_fp32_products(kernel_context_t *ctx, int on) {
+    if (!ctx) return -1;
+    std::lock_guard<std::recursive_mutex> lk(ctx->exec_mutex);
+    ctx->fp32_products = on != 0;
+    return 0;
+}
 
 extern "C" SAPPHIRE_API int kernel_ctx_set_device(kernel_context_t *ctx, int device) {
     if (!ctx) return -1;

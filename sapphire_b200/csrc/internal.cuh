@@ -91,6 +91,7 @@ struct sapphire_context {
     int num_threads = 0;
     int chunk_size = 16;
     bool initialized = false;
+    bool fp32_products = false;    // batched Q4_0 products keep fp32 activations (kernel_ctx_set_fp32_products)
     int device = 0;
     cudaStream_t stream = nullptr;
     bool own_stream = false;

@@ -104,3 +104,30 @@ def test_batch_threshold_paths_agree(sp, ctx, oracle):
     ref32 = oracle.gemv(Q4_0, packed, rows, cols, padded(X, cols))
     assert normwise_rel(Y15, ref32[:15]) < GEMV_RTOL
     assert normwise_rel(Y16, ref32) < 1e-2          # bf16 activations
+
+
+def test_fp32_products_switch(sp, ctx, oracle):
+    """kernel_ctx_set_fp32_products(ctx, 1): a batch-32 Q4_0 kernel_gemm keeps
+    fp32 activations - each row equals kernel_gemv of that row bit for bit and
+    matches the oracle on the unrounded activations; switched off again, the
+    same call runs the bf16 tensor-core product."""
+    from conftest import GEMV_RTOL, normwise_rel
+    from sapphire_b200 import workloads
+    rows, cols, batch = 1024, 640, 32
+    rng = np.random.default_rng(17)
+    w = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)
+    packed = oracle.quantize(sp.DTYPE_Q4_0, w)
+    A = sp.Tensor(sp.DTYPE_Q4_0, (rows, cols), packed)
+    X = rng.standard_normal((batch, cols), dtype=np.float32)
+    ref = oracle.gemv(sp.DTYPE_Q4_0, packed, rows, cols, workloads.pad_cols(X, cols), f64=True)
+    assert sp.lib.kernel_ctx_set_fp32_products(ctx.handle, 1) == 0
+    try:
+        Y = sp.gemm(ctx, A, X, batch)
+        for b in range(batch):
+            assert np.array_equal(Y[b], sp.gemv(ctx, A, X[b])), b
+            assert normwise_rel(Y[b], ref[b]) < GEMV_RTOL
+    finally:
+        assert sp.lib.kernel_ctx_set_fp32_products(ctx.handle, 0) == 0
+    Yb = sp.gemm(ctx, A, X, batch)
+    assert not np.array_equal(Yb, Y)        # bf16 activations on the tensor cores
+    assert normwise_rel(Yb, ref) < 1e-2
