@@ -910,6 +910,8 @@ def measure_decode(args, env, cfg, with_cpu: bool, steps: int, warmup: int) -> d
     peaks = measured_peaks()
     bpt = float(np.mean([decode_bytes_per_token(cfg, cfg.prompt - 1 + g) for g in range(cfg.generate)]))
     ms_tok = gen_total / n_tok
+    exec_kind = ("one persistent kernel for all layers, then the LM head and the argmax"
+                 if dec.launches_per_prompt_token == 1 else "one kernel per stage")
     achieved = bpt / (ms_tok * 1e-3) / 1e9
     entry = {
         "metric": DECODE_METRIC, "value": round(value, 2), "unit": DECODE_UNIT, "n_gpus": world,
@@ -918,9 +920,9 @@ def measure_decode(args, env, cfg, with_cpu: bool, steps: int, warmup: int) -> d
         "data": "synthetic (PCG64 seed 0; random-init Gemma-3-270M, N(0,0.02) weights, Q4_0 projections "
                 "and LM head, bf16 embedding, zero norm weights)",
         "config": decode_config(cfg, world),
-        "execution": ("device-resident decode step captured in CUDA graphs" if world == 1 else
-                      "device-resident decode step captured in CUDA graphs on every rank, LM-head rows sharded, "
-                      "argmax agreed through 8-byte peer-memory words"),
+        "execution": (f"device-resident decode step in CUDA graphs ({exec_kind})" if world == 1 else
+                      f"device-resident decode step in CUDA graphs ({exec_kind}) on every rank, LM-head rows "
+                      "sharded, argmax agreed through 8-byte peer-memory words"),
         "prompt_tok_s": round((cfg.prompt - 1) * steps / (prompt_total * 1e-3), 1),
         "tokens_match_reference": all_match,
         "parity": {"ok": all_match, "checked": f"all {cfg.generate} greedy ids of every rank against the "
@@ -934,7 +936,7 @@ def measure_decode(args, env, cfg, with_cpu: bool, steps: int, warmup: int) -> d
                 "ms_per_step": round(wall_total / steps * 1e3, 3),
                 "path": "sapphire_decoder_generate with a host prompt and host ids (prompt phase included)"},
         "gpu_launches": steps * (cfg.generate * dec.launches_per_token
-                                 + (cfg.prompt - 1) * (dec.launches_per_token - 1)),
+                                 + (cfg.prompt - 1) * dec.launches_per_prompt_token),
     }
     if rank == 0:
         entry["clocks"] = sampler.summary()

@@ -87,6 +87,8 @@ SAPPHIRE_API int sapphire_decoder_last_logits(sapphire_decoder_t *d, float *out)
 SAPPHIRE_API int sapphire_decoder_last_times(sapphire_decoder_t *d, float *prompt_ms, float *generate_ms);
 /** Kernel launches of one generated token (graph nodes). */
 SAPPHIRE_API int sapphire_decoder_launches_per_token(sapphire_decoder_t *d);
+/** Kernels a prompt token's step launches (no LM head, no argmax). */
+SAPPHIRE_API int sapphire_decoder_launches_per_prompt_token(sapphire_decoder_t *d);
 SAPPHIRE_API void sapphire_decoder_destroy(sapphire_decoder_t *d);
 
 /** Test hook (no reference counterpart): on != 0 makes decoders created

@@ -118,6 +118,7 @@ _SIGNATURES = {
     "sapphire_decoder_last_logits": (i32, [vp, vp]),
     "sapphire_decoder_last_times": (i32, [vp, C.POINTER(f32), C.POINTER(f32)]),
     "sapphire_decoder_launches_per_token": (i32, [vp]),
+    "sapphire_decoder_launches_per_prompt_token": (i32, [vp]),
     "sapphire_decoder_destroy": (None, [vp]),
 }
 

@@ -1250,6 +1250,10 @@ extern "C" SAPPHIRE_API int sapphire_decoder_launches_per_token(sapphire_decoder
     return d ? d->launches_gen : -1;
 }
 
+extern "C" SAPPHIRE_API int sapphire_decoder_launches_per_prompt_token(sapphire_decoder_t *d) {
+    return d ? d->launches_prompt : -1;
+}
+
 // ------------------------------------------------- model from a file ------
 // Names as the reference's tensor map (src/loader/gemma3_map.c).
 namespace {

@@ -74,6 +74,10 @@ class Decoder:
     def launches_per_token(self) -> int:
         return lib.sapphire_decoder_launches_per_token(self.handle)
 
+    @property
+    def launches_per_prompt_token(self) -> int:
+        return lib.sapphire_decoder_launches_per_prompt_token(self.handle)
+
     def close(self) -> None:
         if self.handle:
             lib.sapphire_decoder_destroy(self.handle)
