@@ -1125,7 +1125,7 @@ extern "C" SAPPHIRE_API sapphire_decoder_t *sapphire_decoder_create(kernel_conte
             if (d->g_prompt) cudaGraphExecDestroy(d->g_prompt);
             d->g_prompt = nullptr;
             d->coop = false;
-            LOG_INFO("decoder: persistent step captured without the cooperative attribute");
+            LOG_WARN("decoder: persistent step captured without the cooperative attribute");
             if (capture(d, false, &d->g_prompt, &d->launches_prompt) ||
                 capture(d, true, &d->g_gen, &d->launches_gen))
                 break;

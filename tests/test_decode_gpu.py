@@ -144,6 +144,7 @@ def test_persistent_step_reports_an_expired_wait(sp, ctx, decoder, golden):
     from sapphire_b200.decode import Decoder
     cfg, model, dec = decoder
     assert dec.launches_per_token == 3          # persistent step + LM head + argmax
+    assert dec.launches_per_prompt_token == 1
     prev = sp.lib.sapphire_test_decode_stall(1)
     try:
         with pytest.raises(sp.SapphireError, match="gave up waiting"):
