@@ -149,6 +149,16 @@ def test_null_safety(sp):
     L.tensor_release(None)
     L.kernel_ctx_destroy(None)
     assert L.dtype_name(sp.DTYPE_TQ2_0) == b"TQ2_0" and L.dtype_name(99) == b"UNKNOWN"
+    # Additive entry points refuse a NULL handle instead of touching it.
+    assert L.kernel_ctx_set_fp32_products(None, 1) == -1
+    assert L.sapphire_decoder_launches_per_token(None) == -1
+    assert L.sapphire_decoder_launches_per_prompt_token(None) == -1
+    assert L.sapphire_decoder_generate(None, None, 0, 0, None, None) == -1
+    L.sapphire_decoder_destroy(None)
+    assert L.sapphire_safetensors_count(None) == -1 and not L.sapphire_safetensors_name(None, 0)
+    assert not L.sapphire_safetensors_tensor(None, b"x") and not L.sapphire_safetensors_open(None)
+    L.sapphire_safetensors_close(None)
+    assert not L.sapphire_decoder_create_from_safetensors(None, None, None)
 
 
 def test_simd_lane_count(sp):
