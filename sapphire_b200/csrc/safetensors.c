@@ -275,10 +275,15 @@ static int parse_entry(jcur *c, st_entry *e) {
     return 1;
 }
 
-// Bytes the payload of a tensor must hold.
+// Bytes the payload of a tensor must hold; 0 when the shape does not fit the
+// dtype or its element count overflows (a file is untrusted input).
 static int expected_bytes(const st_entry *e, uint64_t *bytes) {
     uint64_t n = 1;
-    for (int i = 0; i < e->ndim; ++i) n *= (uint64_t)e->shape[i];
+    for (int i = 0; i < e->ndim; ++i) {
+        const uint64_t d = (uint64_t)e->shape[i];
+        if (d != 0 && n > (UINT64_MAX / 8) / d) return 0;
+        n *= d;
+    }
     switch (e->dtype) {
         case DTYPE_F32: *bytes = n * 4; return 1;
         case DTYPE_BF16:
@@ -377,7 +382,8 @@ SAPPHIRE_API sapphire_safetensors_t *sapphire_safetensors_open(const char *path)
             if (!parse_entry(&c, e)) goto bad;
             uint64_t want = 0;
             if (!expected_bytes(e, &want)) {
-                LOG_ERROR("tensor '%s': a quantized tensor needs a positive 2-D shape [rows, cols]", e->name);
+                LOG_ERROR("tensor '%s': shape does not fit its dtype (a quantized tensor needs a positive 2-D "
+                          "shape [rows, cols]; the element count must fit 64 bits)", e->name);
                 goto bad;
             }
             if (e->end < e->begin || e->end > st->data_size || e->end - e->begin != want) {

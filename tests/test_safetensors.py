@@ -72,7 +72,7 @@ def _raw(path, header: bytes, data: bytes = b"", hlen=None):
 
 
 @pytest.mark.parametrize("case", ["missing", "short", "hlen", "json", "dtype", "shape1d", "size", "beyond",
-                                  "offsets_reversed", "no_offsets"])
+                                  "offsets_reversed", "no_offsets", "overflow", "dim_too_large"])
 def test_rejects_bad_files(st_mod, tmp_path, case):
     from sapphire_b200 import SapphireError
     path = str(tmp_path / f"{case}.safetensors")
@@ -97,6 +97,12 @@ def test_rejects_bad_files(st_mod, tmp_path, case):
         _raw(path, json.dumps({"w": {"dtype": "F32", "shape": [1], "data_offsets": [4, 0]}}).encode(), bytes(8))
     elif case == "no_offsets":
         _raw(path, json.dumps({"w": {"dtype": "F32", "shape": [1]}}).encode(), bytes(4))
+    elif case == "overflow":
+        # 2^62 * 2^2 elements: the byte count wraps to 16 in 64 bits.
+        _raw(path, json.dumps({"w": {"dtype": "F32", "shape": [2147483647] * 2 + [1073741825, 2],
+                                      "data_offsets": [0, 16]}}).encode(), bytes(16))
+    elif case == "dim_too_large":
+        _raw(path, json.dumps({"w": {"dtype": "F32", "shape": [1 << 31], "data_offsets": [0, 4]}}).encode(), bytes(4))
     with pytest.raises(SapphireError):
         st_mod.SafeTensors(path)
 
