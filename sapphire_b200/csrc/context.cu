@@ -93,13 +93,15 @@ bool ptr_is_device(const void *p, int *dev) {
     return false;
 }
 
-float *host_mapped(float *p) {
+float *host_mapped(float *p, int device) {
     cudaPointerAttributes a;
     if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
         cudaGetLastError();
         return nullptr;
     }
-    return a.type == cudaMemoryTypeHost ? static_cast<float *>(a.devicePointer) : nullptr;
+    // Only memory page-locked for this device's context: memory pinned by
+    // another device's context without the portable flag is not mapped here.
+    return (a.type == cudaMemoryTypeHost && a.device == device) ? static_cast<float *>(a.devicePointer) : nullptr;
 }
 
 bool weight_shape(const tensor_t *A, int *rows, int *cols) {

@@ -75,7 +75,7 @@ int run_product(kernel_context_t *ctx, float *Y, const tensor_t *A, const float 
             // kernel itself through the memory's device mapping: its rows
             // cross PCIe while the product runs instead of in a copy after it
             // (y is valid once the stream has synchronised, as before).
-            float *mapped = batch == 1 ? host_mapped(Y) : nullptr;
+            float *mapped = batch == 1 ? host_mapped(Y, ctx->device) : nullptr;
             if (mapped) {
                 yd = mapped;
             } else {

@@ -168,9 +168,10 @@ void ctx_fail(kernel_context_t *ctx, const char *where, const char *fmt, ...)
 
 // True if p is device (or managed) memory; *dev receives its ordinal.
 bool ptr_is_device(const void *p, int *dev);
-// Device address of page-locked host memory (registered or cudaHostAlloc'ed)
-// as the device sees it through its mapping; nullptr for any other pointer.
-float *host_mapped(float *p);
+// Device address of page-locked host memory (registered or cudaHostAlloc'ed
+// while `device` was current) as that device sees it through its mapping;
+// nullptr for any other pointer.
+float *host_mapped(float *p, int device);
 
 // Process-wide context used for NULL-context dense GEMV and the row ABI.
 kernel_context_t *default_context();
