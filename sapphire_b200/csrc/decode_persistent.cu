@@ -812,9 +812,9 @@ PersistPlan persist_plan(int device, const PersistParams &s, const char **why) {
         *why = "no SM count";
         return plan;
     }
-    const int group = s.kv_heads > 0 ? s.heads / s.kv_heads : 0;
-    if (s.hd % 64 || s.hd > kMaxHeadDim || s.kv_heads <= 0 || s.heads % s.kv_heads ||
-        (group != 1 && group != 2 && group != 4 && group != 8)) {
+    // One attention block serves one query head, so any grouping of query
+    // heads over KV heads works.
+    if (s.hd % 64 || s.hd > kMaxHeadDim || s.kv_heads <= 0 || s.heads % s.kv_heads) {
         *why = "head shape";
         return plan;
     }
