@@ -667,6 +667,11 @@ __device__ __forceinline__ void put_word(unsigned long long *p, unsigned epoch, 
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(((unsigned long long)epoch << 32) | bits)
                  : "memory");
 }
+__device__ __forceinline__ unsigned long long ld_part(const unsigned long long *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
 // Polls a word until it carries `epoch` (bounded); false if the wait ran out.
 __device__ __forceinline__ bool get_word(const unsigned long long *p, unsigned epoch, uint32_t &bits) {
     for (unsigned i = 0; i < kWaitLimit; ++i) {
@@ -726,27 +731,38 @@ __device__ void flush_tile(const StreamParams &p, const XImage &xi, int tile, in
         if (kWords == 2) put_word(w + 1, p.epoch, (uint32_t)(mine >> 32));
         return;
     }
-    // The finisher: sum the parts in slot order.
+    // The finisher: sum the parts in slot order.  The words of kSlots slots
+    // are loaded at once (one round trip per batch rather than one per word,
+    // which matters when a short shard spreads a tile over dozens of warps);
+    // only a word that does not carry the epoch yet is polled again.
+    constexpr int kSlots = 8 / kWords;
     bool ok = true;
-    unsigned long long sum;
-    if (DT == DTYPE_TQ2_0) {
-        long long t = (long long)mine;
-        for (int j = 1; j < k; ++j) {
-            const unsigned long long *w = base + ((size_t)j * 32 + lane) * kWords;
-            uint32_t lo = 0, hi = 0;
-            ok = ok && get_word(w, p.epoch, lo) && get_word(w + 1, p.epoch, hi);
-            t += (long long)(((unsigned long long)hi << 32) | lo);
+    long long ti = (long long)mine;
+    float tf = __uint_as_float((uint32_t)mine);
+    for (int j0 = 1; j0 < k; j0 += kSlots) {
+        unsigned long long w[kSlots][kWords];
+#pragma unroll
+        for (int q = 0; q < kSlots; ++q)
+#pragma unroll
+            for (int h = 0; h < kWords; ++h)
+                w[q][h] = j0 + q < k ? ld_part(base + ((size_t)(j0 + q) * 32 + lane) * kWords + h) : 0ull;
+#pragma unroll
+        for (int q = 0; q < kSlots; ++q) {
+            if (j0 + q >= k) break;
+            uint32_t bits[kWords];
+#pragma unroll
+            for (int h = 0; h < kWords; ++h) {
+                bits[h] = (uint32_t)w[q][h];
+                if ((unsigned)(w[q][h] >> 32) != p.epoch)
+                    ok = ok && get_word(base + ((size_t)(j0 + q) * 32 + lane) * kWords + h, p.epoch, bits[h]);
+            }
+            if (DT == DTYPE_TQ2_0)
+                ti += (long long)(((unsigned long long)bits[kWords - 1] << 32) | bits[0]);
+            else
+                tf += __uint_as_float(bits[0]);
         }
-        sum = (unsigned long long)t;
-    } else {
-        float t = __uint_as_float((uint32_t)mine);
-        for (int j = 1; j < k; ++j) {
-            uint32_t bits = 0;
-            ok = ok && get_word(base + (size_t)j * 32 + lane, p.epoch, bits);
-            t += __uint_as_float(bits);
-        }
-        sum = __float_as_uint(t);
     }
+    const unsigned long long sum = DT == DTYPE_TQ2_0 ? (unsigned long long)ti : __float_as_uint(tf);
     if (!ok) atomicOr(p.err, 1);
     if (row_ok) store_y(p, (size_t)tile * 32 + lane, ok ? finish_row<DT>(xi, sum, nonfinite, rs) : __int_as_float(0x7FC00000));
 }
