@@ -1,12 +1,14 @@
-"""Host-side arithmetic of the pipelined GEMV's work split (CPU only).
+"""Host-side arithmetic of the GEMV kernels' work split (CPU only).
 
-The kernel (sapphire_b200/csrc/gemv_pipe.cu) gives warp w the items
+The dense kernel (sapphire_b200/csrc/gemv_pipe.cu) gives warp w the items
 [floor(w*T/W), floor((w+1)*T/W)), finds the owner of item i as
 ceil((i+1)*W/T) - 1, and sizes the split-tile scratch with
 pipe_kmax(T, W, nseg).  These are restated here and checked by brute force:
 the owner formula must name the warp whose range holds the item, and no tile
 may have more contributing warps than pipe_kmax allows (the scratch slot index
-would overflow otherwise).
+would overflow otherwise).  The streaming kernel of the quantized formats
+(sapphire_b200/csrc/gemv_stream.cu: range_begin, unit_owner, stream_kmax)
+splits 64-column units over its consumer warps with the same three formulas.
 """
 from __future__ import annotations
 
@@ -54,3 +56,13 @@ def test_partition_benchmark_shapes():
         ntiles = (rows + 31) // 32
         nseg = (kchunks + 7) // 8
         check(ntiles, nseg, W)
+
+
+def test_partition_stream_shapes():
+    # Units of 64 columns per 32-row tile, 11 (Q8_0 / Q4_0) or 15 (TQ2_0)
+    # consumer warps per SM; full weights and the row slices one rank of 2, 4
+    # or 8 streams.
+    for rows, cols, nc in ((262144, 640, 11), (262144, 640, 15), (16384, 16384, 15), (2048, 640, 11)):
+        for world in (1, 2, 4, 8):
+            nloc = (rows + world - 1) // world
+            check((nloc + 31) // 32, (cols // 32 + 1) // 2, 148 * nc)
