@@ -191,6 +191,36 @@ def test_decoder_loader_checks_names_and_shapes(st_mod, tmp_path):
         lib.kernel_ctx_destroy(ctx)
 
 
+def test_reader_survives_mutated_files(tmp_path):
+    """tests/c/fuzz_safetensors.c: the reader's own sources built with
+    AddressSanitizer and UndefinedBehaviorSanitizer, fed 20,000 mutated files
+    (about 4 s).  Any out-of-bounds access, use after free, leak or overflow
+    ends the run with a non-zero status."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    exe = str(tmp_path / "fuzz_safetensors")
+    csrc = os.path.join(ROOT, "sapphire_b200", "csrc")
+    build = subprocess.run([cc, "-O1", "-g", "-std=c11", "-fsanitize=address,undefined", "-fno-sanitize-recover=all",
+                            "-fno-omit-frame-pointer", "-I", os.path.join(ROOT, "include"),
+                            os.path.join(ROOT, "tests", "c", "fuzz_safetensors.c"),
+                            os.path.join(csrc, "safetensors.c"), os.path.join(csrc, "tensor.c"),
+                            os.path.join(csrc, "log.c"), "-o", exe], capture_output=True, text=True)
+    if build.returncode != 0:
+        pytest.skip("sanitizer build unavailable: " + build.stderr[-300:])
+    env = dict(os.environ, SAPPHIRE_LOG_LEVEL="100")
+    run = subprocess.run([exe, "20000", "1", str(tmp_path / "mutated.safetensors")], capture_output=True,
+                         text=True, env=env, timeout=300)
+    if "LeakSanitizer has encountered a fatal error" in run.stderr:
+        pytest.skip("leak checking is not available in this environment")
+    assert run.returncode == 0, run.stderr[-3000:]
+    assert run.stdout.startswith("iterations 20000 ")
+    opened = int(run.stdout.split()[3])
+    assert opened > 0          # some mutated files are still valid and get read
+
+
 @pytest.mark.gpu
 def test_gemv_on_file_tensors(st_mod, sp, ctx, oracle, tmp_path):
     """Q4_0 / Q8_0 / TQ2_0 tensors read from a file are views the GEMV takes
