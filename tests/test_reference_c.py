@@ -3,7 +3,8 @@ linked against libsapphire_cuda.so (tests/c/Makefile): the drop-in check of
 the C-ABI with the reference's callers rather than ctypes.
 
 * test_tensor (reference src/test/test_tensor.c) exercises only the host
-  tensor API, so it runs here on the CPU;
+  tensor API, so it runs here on the CPU, once as built by the Makefile and
+  once built from source with sanitizers;
 * test_dispatch (src/test/test_dispatch.c: the Q4_0 row kernels, aligned and
   unaligned, within 1e-4 of each other) and test_tensor_gemv
   (src/test/test_tensor_gemv.c: kernel_gemv / _add / _batch / _tensor and the
@@ -45,6 +46,33 @@ def _run(name: str, timeout: float = 300.0) -> subprocess.CompletedProcess:
 
 def test_reference_tensor_api_test_passes():
     r = _run("test_tensor")
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    m = re.search(r"(\d+) passed, (\d+) failed", r.stdout)
+    assert m and int(m.group(2)) == 0 and int(m.group(1)) > 0, r.stdout[-2000:]
+
+
+def test_reference_tensor_api_test_under_sanitizers(tmp_path):
+    """The reference's test_tensor.c against this library's tensor.c, built
+    from source with AddressSanitizer and UndefinedBehaviorSanitizer: every
+    case passes with no out-of-bounds access, use after free or leak."""
+    import shutil
+    ref = os.environ.get("SAPPHIRE_REFERENCE_DIR") or os.path.join(os.path.dirname(ROOT), "reference")
+    src = os.path.join(ref, "src", "test", "test_tensor.c")
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if not os.path.exists(src) or cc is None:
+        pytest.skip("needs the reference checkout and a C compiler")
+    exe = str(tmp_path / "test_tensor_asan")
+    csrc = os.path.join(ROOT, "sapphire_b200", "csrc")
+    build = subprocess.run([cc, "-O1", "-g", "-std=c11", "-fsanitize=address,undefined", "-fno-sanitize-recover=all",
+                            "-I", os.path.join(ROOT, "include"), "-I", os.path.join(ref, "include"), src,
+                            os.path.join(csrc, "tensor.c"), os.path.join(csrc, "log.c"),
+                            os.path.join(ROOT, "tests", "c", "tensor_hooks.c"), "-o", exe, "-lm"],
+                           capture_output=True, text=True)
+    if build.returncode != 0:
+        pytest.skip("sanitizer build unavailable: " + build.stderr[-300:])
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    if "LeakSanitizer has encountered a fatal error" in r.stderr:
+        pytest.skip("leak checking is not available in this environment")
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     m = re.search(r"(\d+) passed, (\d+) failed", r.stdout)
     assert m and int(m.group(2)) == 0 and int(m.group(1)) > 0, r.stdout[-2000:]
